@@ -1,0 +1,161 @@
+/*
+ * pathpack_b200.h — C ABI of the B200 (sm_100a) backend for the numeric hot path of PATHPACK.jl's semiring
+ * multifrontal solver: mlu / mstar / lmul! / rmul! / Matrix(F) over MinPlus, MaxPlus, MaxMin, MinMax, MaxProd,
+ * PlusProd and OrAnd.
+ *
+ * The symbolic phase stays on the host (in PATHPACK.jl: `ssymbolic`, src/CPU/chordal_ssymbolic.jl:26-57, with
+ * CliqueTrees.jl).  Its output crosses this ABI once (pp_set_structure); the numeric work runs on one GPU per
+ * handle.  Plain C types only: no C++ or torch types cross the boundary.
+ *
+ * Conventions
+ *   - Every function returns an int32 status: PP_OK (0) or a negative PP_E* code; pp_last_error() gives the
+ *     message.  Nothing throws across the ABI.
+ *   - Host arrays passed in are only read during the call (copied or staged); no pointer is retained.
+ *   - Device memory is owned by the handle and released by pp_destroy, also after an error.
+ *   - A handle is bound to one device and one stream; calls on one handle must be serialised by the caller.
+ *     Different handles may be used from different threads.  Calls with host outputs return after the data
+ *     is in host memory; calls with device outputs are ordered on the handle's stream (pp_sync waits).
+ *   - Matrices are column-major (Julia's layout), with a leading dimension.
+ *   - Index arrays are int64 and may be 1-based (as Julia and CliqueTrees hold them, `base` = 1) or 0-based.
+ */
+#ifndef PATHPACK_B200_H
+#define PATHPACK_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PP_OK 0
+#define PP_EINVAL (-1)       /* bad argument, shape or structure */
+#define PP_EUNSUPPORTED (-2) /* semiring / element type pair the backend does not take */
+#define PP_ENOMEM (-3)       /* device or host memory exhausted (checked before work starts) */
+#define PP_EDEVICE (-4)      /* CUDA error */
+#define PP_ETIMEOUT (-5)     /* a bounded device wait expired */
+#define PP_ESTATE (-6)       /* call out of order (e.g. a solve before pp_factor) */
+
+/* semirings: the reference's MinPlus, MaxPlus, MaxMin, MinMax, MaxProd, PlusProd, OrAnd
+   (src/CPU/semiring/tropical.jl, bottleneck.jl, real.jl, boolean.jl) */
+enum { PP_MINPLUS = 0, PP_MAXPLUS = 1, PP_MAXMIN = 2, PP_MINMAX = 3, PP_MAXPROD = 4, PP_PLUSPROD = 5, PP_ORAND = 6 };
+/* element types */
+enum { PP_F32 = 0, PP_F64 = 1, PP_I32 = 2 };
+/* where a caller buffer lives */
+enum { PP_HOST = 0, PP_DEVICE = 1 };
+
+typedef struct pp_handle pp_handle;
+
+typedef struct pp_stats {
+    int64_t n, nf, nB;          /* vertices, fronts, strongly connected components */
+    int64_t nlevels;            /* tree levels of the factorization schedule */
+    int64_t nD, nL, nN;         /* lengths of LD/UD, LL/UL and Nval */
+    int64_t max_front;          /* largest nn + na */
+    double pairs_factor;        /* (x)(+) pairs of one factorization, unpadded structure */
+    double ms_factor;           /* device time of the last pp_factor */
+    double ms_solve;            /* device time of the last pp_lmul / pp_rmul / pp_star */
+    double pairs_solve;         /* (x)(+) pairs of the last solve */
+    int64_t device_bytes;       /* device memory held by the handle */
+    int64_t kernel_launches;    /* kernels launched by the last call */
+} pp_stats;
+
+/* The library's version, major * 10000 + minor * 100 + patch. */
+int32_t pp_version(void);
+
+/* Whether the backend takes the (semiring, element type) pair: PP_OK or PP_EUNSUPPORTED.
+   Replaces check_semiring, ext/PATHPACKCUDAExt/runtime/config.jl:359-377.  Supported: every semiring over
+   PP_F32 and PP_F64 except OrAnd; MinPlus and OrAnd over PP_I32.  Int32 MinPlus is defined on [0, INT32_MAX]
+   with a saturating product (INT32_MAX is "no path" and absorbs). */
+int32_t pp_check_semiring(int32_t semiring, int32_t dtype);
+
+/* The message of the last failed call on this thread (h may be NULL), or "" after success. */
+const char *pp_last_error(const pp_handle *h);
+
+/* Create a handle on a CUDA device (stream, device structures created lazily). */
+int32_t pp_create(int32_t device, pp_handle **h);
+/* Release everything the handle holds.  Safe on NULL. */
+int32_t pp_destroy(pp_handle *h);
+
+/* Upload the symbolic structure (replaces the ChordalSSymbolic that `ChordalSLU` holds,
+   src/CPU/chordal_slu.jl:1-26 and src/CPU/chordal_ssymbolic.jl:1-8):
+     n, nf, nB          vertices, fronts, components
+     Rptr[nf+1]         residual of front f = positions Rptr[f] .. Rptr[f+1]-1   (pointers(S.res))
+     Sptr[nf+1], Stgt   separator of front f, sorted positions                   (pointers/targets(S.sep))
+     Bptr[nB+1]         vertex range of each component                           (F.S.Bptr)
+     Fptr[nB+1]         front range of each component                            (F.S.Fptr)
+     Nptr[n+1], Ntgt    coupling: rows of earlier components of each position    (pointers/targets(F.S.N))
+     perm[n]            original vertex at each position                         (F.rperm = F.cperm)
+   Fronts must be in postorder and the parent of a front is the front of its first separator vertex.
+   base = 1 for 1-based arrays (Julia), 0 for 0-based. */
+int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, const int64_t *Rptr, const int64_t *Sptr,
+                         const int64_t *Stgt, const int64_t *Bptr, const int64_t *Fptr, const int64_t *Nptr,
+                         const int64_t *Ntgt, const int64_t *perm, int32_t base);
+
+/* Assemble A (n x n CSC on the host: colptr[n+1], rowval[nnz], nzval[nnz] of the element type; A[i, j] is the
+   weight of the arc i -> j; no duplicate entries) into the factor arrays on the device.  Replaces
+   copyto!(F::ChordalSLU, A), src/CPU/chordal_slu.jl:116-321. */
+int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, const int64_t *colptr, const int64_t *rowval,
+                    const void *nzval, int32_t base);
+
+/* Upload already assembled factor arrays (host): LD, UD (|LD| values), LL, UL (|LL|), Nval (|Nval|). */
+int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, const void *LD, const void *LL, const void *UD,
+                      const void *UL, const void *Nval);
+
+/* Factorize the star, A* = U* L*, in place on the device.  Replaces lu!(F) -> sgetrf!(F),
+   src/CPU/abstract_slu.jl:119-121 and src/CPU/chordal/sgetrf.jl:3-290. */
+int32_t pp_factor(pp_handle *h);
+
+/* Download the factor arrays to the host (any pointer may be NULL). */
+int32_t pp_get_factor(pp_handle *h, void *LD, void *LL, void *UD, void *UL);
+
+/* B <- A* B: lmul!(F, B), src/CPU/abstract_slu.jl:131-134.  B is n x k, column-major, leading dimension ldb,
+   on the host (where = PP_HOST) or on this handle's device (PP_DEVICE). */
+int32_t pp_lmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where);
+
+/* B <- B A*: rmul!(B, F), src/CPU/abstract_slu.jl:142-145.  B is k x n, column-major, leading dimension ldb. */
+int32_t pp_rmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where);
+
+/* Columns col0 .. col0+ncols-1 of the star A* (original labels) into C (n x ncols, column-major, leading
+   dimension ldc).  ncols = n and col0 = 0 is Matrix(F), src/CPU/abstract_slu.jl:10-14; column panels let
+   several GPUs share one star. */
+int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where);
+
+/* Wait for the handle's stream. */
+int32_t pp_sync(pp_handle *h);
+
+/* Counters of the handle (sizes, pair counts, device times of the last calls). */
+int32_t pp_get_stats(pp_handle *h, pp_stats *s);
+
+/* The handle's CUDA stream (a cudaStream_t), for callers that order their own work after the handle's. */
+void *pp_stream(pp_handle *h);
+
+/* ---- dense kernels on caller device memory (ordered on `stream`, a cudaStream_t or NULL) ---- */
+
+/* C <- C (+) A (x) B, A m x k, B k x n, C m x n, column-major device arrays.
+   Replaces sgemx_gpu!(s, C, A, B), ext/PATHPACKCUDAExt/dense/sgemx.jl:27-45 (and CPU.sgemx!). */
+int32_t pp_gemm(int32_t semiring, int32_t dtype, int64_t m, int64_t n, int64_t k, void *C, int64_t ldc, const void *A,
+                int64_t lda, const void *B, int64_t ldb, void *stream);
+
+/* In-place LU of the star of `count` dense n x n blocks stored back to back (block b at A + b*n*n, column-major).
+   Replaces sgetrf_gpu!(s, A) on each block, ext/PATHPACKCUDAExt/dense/sgetrf.jl:31-125 (and CPU.sgetrf!). */
+int32_t pp_getrf_batched(int32_t semiring, int32_t dtype, int64_t n, int64_t count, void *A, void *stream);
+
+/* ---- host symbolic stand-in (for callers without Julia's symbolic phase) ---- */
+
+typedef struct pp_symbolic_result pp_symbolic_result;
+
+/* SCCs, ordering and clique tree of the n x n pattern colptr/rowval (0-based CSC).  method 0 = nested
+   dissection (leaf = piece size ordered by minimum degree, 0 = default), 1 = natural order.  The result is
+   0-based; read it with pp_symbolic_sizes / pp_symbolic_get and release it with pp_symbolic_free. */
+int32_t pp_symbolic(int64_t n, const int64_t *colptr, const int64_t *rowval, int32_t method, int32_t leaf,
+                    pp_symbolic_result **out);
+/* sizes[5] = n, nf, nB, |Stgt|, |Ntgt| */
+void pp_symbolic_sizes(const pp_symbolic_result *r, int64_t *sizes);
+void pp_symbolic_get(const pp_symbolic_result *r, int64_t *Rptr, int64_t *Sptr, int64_t *Stgt, int64_t *Bptr,
+                     int64_t *Fptr, int64_t *Nptr, int64_t *Ntgt, int64_t *perm);
+void pp_symbolic_free(pp_symbolic_result *r);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

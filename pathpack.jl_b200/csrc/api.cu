@@ -1,0 +1,896 @@
+// api.cu — the C ABI (include/pathpack_b200.h): handles, structure upload and checks, schedules, workspace,
+// and the drivers of mlu / lmul! / rmul! / Matrix(F) on one GPU.
+//
+// What each entry point replaces in the reference is stated in the header.  The structure checks are those
+// the reference's solver relies on (postorder clique tree, separators inside the parent's bag); the error
+// conventions follow the reference's typed errors (check_semiring, ext/PATHPACKCUDAExt/runtime/config.jl:359-377;
+// the memory check before any work, api.jl:1031-1045; freeing everything on failure, api.jl:141-147).
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "ops.h"
+#include "pathpack_b200_internal.h"
+
+namespace pp {
+extern const Ops ops_minplus_f32, ops_minplus_f64, ops_minplus_i32, ops_maxplus_f32, ops_maxplus_f64,
+    ops_maxmin_f32, ops_maxmin_f64, ops_minmax_f32, ops_minmax_f64, ops_maxprod_f32, ops_maxprod_f64,
+    ops_plusprod_f32, ops_plusprod_f64, ops_orand_i32;
+
+const Ops *get_ops(int sr, int dt) {
+    switch (sr * 3 + dt) {
+        case PP_MINPLUS * 3 + 0: return &ops_minplus_f32;
+        case PP_MINPLUS * 3 + 1: return &ops_minplus_f64;
+        case PP_MINPLUS * 3 + 2: return &ops_minplus_i32;
+        case PP_MAXPLUS * 3 + 0: return &ops_maxplus_f32;
+        case PP_MAXPLUS * 3 + 1: return &ops_maxplus_f64;
+        case PP_MAXMIN * 3 + 0: return &ops_maxmin_f32;
+        case PP_MAXMIN * 3 + 1: return &ops_maxmin_f64;
+        case PP_MINMAX * 3 + 0: return &ops_minmax_f32;
+        case PP_MINMAX * 3 + 1: return &ops_minmax_f64;
+        case PP_MAXPROD * 3 + 0: return &ops_maxprod_f32;
+        case PP_MAXPROD * 3 + 1: return &ops_maxprod_f64;
+        case PP_PLUSPROD * 3 + 0: return &ops_plusprod_f32;
+        case PP_PLUSPROD * 3 + 1: return &ops_plusprod_f64;
+        case PP_ORAND * 3 + 2: return &ops_orand_i32;
+        default: return nullptr;
+    }
+}
+}  // namespace pp
+
+using namespace pp;
+
+static thread_local std::string g_err;
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    cudaError_t ensure(size_t b) {
+        if (b <= bytes && p) return cudaSuccess;
+        release();
+        if (b == 0) b = 16;
+        cudaError_t e = cudaMalloc(&p, b);
+        if (e == cudaSuccess) bytes = b;
+        return e;
+    }
+    template <typename U>
+    U *as() const {
+        return static_cast<U *>(p);
+    }
+};
+
+struct pp_handle {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    std::string err;
+    bool have_structure = false, have_values = false, factored = false;
+    int sr = -1, dt = -1;
+    const Ops *ops = nullptr;
+    HostPlan hp;
+    // host copies used by the drivers
+    std::vector<int> invp;
+    // device structure
+    DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
+        d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_ffronts, d_sfronts, d_sverts;
+    // values and work
+    DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val;
+    int64_t nD = 0, nL = 0;
+    size_t ws_esize = 0;
+    pp_stats st{};
+};
+
+static int32_t fail(pp_handle *h, int32_t code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    if (h) h->err = buf;
+    return code;
+}
+
+static int32_t cuda_fail(pp_handle *h, cudaError_t e, const char *what) {
+    return fail(h, PP_EDEVICE, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(h, x, what)                                         \
+    do {                                                       \
+        cudaError_t e_ = (x);                                  \
+        if (e_ != cudaSuccess) return cuda_fail((h), e_, what); \
+    } while (0)
+
+static void ok(pp_handle *h) {
+    g_err.clear();
+    if (h) h->err.clear();
+}
+
+template <typename U>
+static cudaError_t upload(DevBuf &b, const std::vector<U> &v, cudaStream_t st) {
+    cudaError_t e = b.ensure(sizeof(U) * std::max<size_t>(v.size(), 1));
+    if (e != cudaSuccess) return e;
+    if (!v.empty()) e = cudaMemcpyAsync(b.p, v.data(), sizeof(U) * v.size(), cudaMemcpyHostToDevice, st);
+    return e;
+}
+
+static int32_t check_pair(int32_t sr, int32_t dt) { return get_ops(sr, dt) ? PP_OK : PP_EUNSUPPORTED; }
+
+extern "C" int32_t pp_version(void) { return 100; }
+
+extern "C" int32_t pp_check_semiring(int32_t semiring, int32_t dtype) {
+    if (check_pair(semiring, dtype) != PP_OK)
+        return fail(nullptr, PP_EUNSUPPORTED, "semiring %d with element type %d is not supported", semiring, dtype);
+    ok(nullptr);
+    return PP_OK;
+}
+
+extern "C" const char *pp_last_error(const pp_handle *h) { return h ? h->err.c_str() : g_err.c_str(); }
+
+extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
+    if (!out) return fail(nullptr, PP_EINVAL, "pp_create: null output pointer");
+    *out = nullptr;
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "pp_create: no CUDA device");
+    if (device < 0 || device >= ndev) return fail(nullptr, PP_EINVAL, "pp_create: device %d of %d", device, ndev);
+    auto *h = new (std::nothrow) pp_handle();
+    if (!h) return fail(nullptr, PP_ENOMEM, "pp_create: out of host memory");
+    h->device = device;
+    e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreate(&h->ev0);
+    if (e == cudaSuccess) e = cudaEventCreate(&h->ev1);
+    if (e != cudaSuccess) {
+        pp_destroy(h);
+        return cuda_fail(nullptr, e, "pp_create");
+    }
+    *out = h;
+    ok(nullptr);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_destroy(pp_handle *h) {
+    if (!h) return PP_OK;
+    cudaSetDevice(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    if (h->ev0) cudaEventDestroy(h->ev0);
+    if (h->ev1) cudaEventDestroy(h->ev1);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;  // DevBuf destructors free the device memory
+    return PP_OK;
+}
+
+extern "C" void *pp_stream(pp_handle *h) { return h ? (void *)h->stream : nullptr; }
+
+// ---------------------------------------------------------------- structure
+
+extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, const int64_t *Rptr,
+                                    const int64_t *Sptr, const int64_t *Stgt, const int64_t *Bptr, const int64_t *Fptr,
+                                    const int64_t *Nptr, const int64_t *Ntgt, const int64_t *perm, int32_t base) {
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_set_structure: null handle");
+    if (n < 0 || nf < 0 || nB < 0 || (n > 0 && (nf < 1 || nB < 1)) || n >= INT32_MAX)
+        return fail(h, PP_EINVAL, "pp_set_structure: sizes n=%lld nf=%lld nB=%lld", (long long)n, (long long)nf,
+                    (long long)nB);
+    if (n > 0 && (!Rptr || !Sptr || !Bptr || !Fptr || !Nptr || !perm))
+        return fail(h, PP_EINVAL, "pp_set_structure: null array");
+    if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_set_structure: base must be 0 or 1");
+    cudaSetDevice(h->device);
+    h->have_structure = h->have_values = h->factored = false;
+    HostPlan hp;
+    hp.n = (int)n;
+    hp.nf = (int)nf;
+    hp.nB = (int)nB;
+    const int64_t b = base;
+    try {
+        std::vector<int64_t> R(nf + 1), Sp(nf + 1), Bp(nB + 1), Fp(nB + 1), Np(n + 1);
+        for (int64_t i = 0; i <= nf; i++) {
+            R[i] = Rptr[i] - b;
+            Sp[i] = Sptr[i] - b;
+        }
+        for (int64_t i = 0; i <= nB; i++) {
+            Bp[i] = Bptr[i] - b;
+            Fp[i] = Fptr[i] - b;
+        }
+        for (int64_t i = 0; i <= n; i++) Np[i] = Nptr[i] - b;
+        if (R[0] != 0 || R[nf] != n || Sp[0] != 0 || Bp[0] != 0 || Bp[nB] != n || Fp[0] != 0 || Fp[nB] != nf ||
+            Np[0] != 0)
+            return fail(h, PP_EINVAL, "pp_set_structure: pointer arrays must start at the base and end at n/nf");
+        const int64_t nS = Sp[nf], nN = Np[n];
+        if (nS < 0 || nN < 0 || (nS > 0 && !Stgt) || (nN > 0 && !Ntgt))
+            return fail(h, PP_EINVAL, "pp_set_structure: separator/coupling arrays");
+        if (nS >= INT32_MAX || nN >= ((int64_t)1 << 40)) return fail(h, PP_EINVAL, "pp_set_structure: too large");
+        hp.nn.resize(nf);
+        hp.na.resize(nf);
+        hp.sptr.resize(nf + 1);
+        hp.dptr.assign(nf + 1, 0);
+        hp.lptr.assign(nf + 1, 0);
+        std::vector<int> rlo(nf), idx(n), stgt(nS), rel(nS), pnt(nf, -1), fcc(nf), permv(n), invp(n, -1), bptr(nB + 1);
+        for (int64_t f = 0; f < nf; f++) {
+            const int64_t nn = R[f + 1] - R[f], na = Sp[f + 1] - Sp[f];
+            if (nn <= 0 || na < 0) return fail(h, PP_EINVAL, "pp_set_structure: front %lld is empty", (long long)f);
+            rlo[f] = (int)R[f];
+            hp.nn[f] = (int)nn;
+            hp.na[f] = (int)na;
+            hp.sptr[f] = Sp[f];
+            hp.dptr[f + 1] = hp.dptr[f] + nn * nn;
+            hp.lptr[f + 1] = hp.lptr[f] + nn * na;
+            for (int64_t v = R[f]; v < R[f + 1]; v++) idx[v] = (int)f;
+        }
+        hp.sptr[nf] = nS;
+        for (int64_t q = 0; q < nS; q++) {
+            const int64_t v = Stgt[q] - b;
+            if (v < 0 || v >= n) return fail(h, PP_EINVAL, "pp_set_structure: separator vertex out of range");
+            stgt[q] = (int)v;
+        }
+        for (int64_t i = 0; i < n; i++) {
+            const int64_t v = perm[i] - b;
+            if (v < 0 || v >= n || invp[v] >= 0) return fail(h, PP_EINVAL, "pp_set_structure: perm is not a permutation");
+            permv[i] = (int)v;
+            invp[v] = (int)i;
+        }
+        // parents, relative indices, children (fronts in postorder: every parent after its children)
+        std::vector<int> nchd(nf + 1, 0);
+        for (int64_t f = 0; f < nf; f++) {
+            const int na = hp.na[f];
+            if (na == 0) continue;
+            const int v0 = stgt[Sp[f]];
+            if (v0 < R[f + 1]) return fail(h, PP_EINVAL, "pp_set_structure: separator of front %lld overlaps it", (long long)f);
+            const int p = idx[v0];
+            pnt[f] = p;
+            nchd[p + 1]++;
+            const int pr = rlo[p], pnn = hp.nn[p];
+            int64_t q = Sp[p];
+            for (int64_t k = Sp[f]; k < Sp[f + 1]; k++) {
+                const int v = stgt[k];
+                if (k > Sp[f] && v <= stgt[k - 1]) return fail(h, PP_EINVAL, "pp_set_structure: separator not sorted");
+                if (v < pr) return fail(h, PP_EINVAL, "pp_set_structure: separator vertex before the parent");
+                if (v < pr + pnn) {
+                    rel[k] = v - pr;
+                } else {
+                    while (q < Sp[p + 1] && stgt[q] < v) q++;
+                    if (q >= Sp[p + 1] || stgt[q] != v)
+                        return fail(h, PP_EINVAL, "pp_set_structure: separator of front %lld not in its parent's bag",
+                                    (long long)f);
+                    rel[k] = pnn + (int)(q - Sp[p]);
+                }
+            }
+        }
+        hp.chdptr.assign(nf + 1, 0);
+        for (int64_t f = 0; f < nf; f++) hp.chdptr[f + 1] = hp.chdptr[f] + nchd[f + 1];
+        hp.chdtgt.assign(std::max<int64_t>(hp.chdptr[nf], 1), 0);
+        {
+            std::vector<int> fill(hp.chdptr.begin(), hp.chdptr.end() - 1);
+            for (int64_t f = 0; f < nf; f++)
+                if (pnt[f] >= 0) hp.chdtgt[fill[pnt[f]]++] = (int)f;
+        }
+        for (int64_t c = 0; c < nB; c++) {
+            if (Bp[c + 1] < Bp[c] || Fp[c + 1] < Fp[c]) return fail(h, PP_EINVAL, "pp_set_structure: component pointers");
+            bptr[c] = (int)Bp[c];
+            for (int64_t f = Fp[c]; f < Fp[c + 1]; f++) fcc[f] = (int)c;
+            if (Fp[c + 1] > Fp[c] && (R[Fp[c]] != Bp[c] || R[Fp[c + 1]] != Bp[c + 1]))
+                return fail(h, PP_EINVAL, "pp_set_structure: component %lld fronts do not cover its vertices", (long long)c);
+        }
+        bptr[nB] = (int)n;
+        std::vector<int> ntgt(std::max<int64_t>(nN, 1), 0);
+        for (int64_t j = 0; j < n; j++) {
+            if (Np[j + 1] < Np[j]) return fail(h, PP_EINVAL, "pp_set_structure: coupling pointers");
+            const int jstrt = bptr[fcc[idx[j]]];
+            for (int64_t p = Np[j]; p < Np[j + 1]; p++) {
+                const int64_t i = Ntgt[p] - b;
+                if (i < 0 || i >= jstrt) return fail(h, PP_EINVAL, "pp_set_structure: coupling row not in an earlier component");
+                if (p > Np[j] && i <= ntgt[p - 1]) return fail(h, PP_EINVAL, "pp_set_structure: coupling rows not sorted");
+                ntgt[p] = (int)i;
+            }
+        }
+        hp.nN = nN;
+        // heights: leaves 0, a parent one above its highest child
+        std::vector<int> height(nf, 0);
+        int maxh = 0;
+        for (int64_t f = 0; f < nf; f++) {
+            if (pnt[f] >= 0) {
+                if (pnt[f] <= f) return fail(h, PP_EINVAL, "pp_set_structure: fronts are not in postorder");
+                height[pnt[f]] = std::max(height[pnt[f]], height[f] + 1);
+            }
+            maxh = std::max(maxh, height[f]);
+        }
+        // coupling stages
+        std::vector<int> comp_of_vertex(n);
+        for (int64_t c = 0; c < nB; c++)
+            for (int64_t v = Bp[c]; v < Bp[c + 1]; v++) comp_of_vertex[v] = (int)c;
+        std::vector<int> lstage(nB, 0), rstage(nB, 0);
+        std::vector<char> ccoupled(nB, 0);
+        for (int64_t c = 0; c < nB; c++)  // rmul: after every predecessor
+            for (int64_t j = Bp[c]; j < Bp[c + 1]; j++)
+                for (int64_t p = Np[j]; p < Np[j + 1]; p++) {
+                    const int a = comp_of_vertex[ntgt[p]];
+                    rstage[c] = std::max(rstage[c], rstage[a] + 1);
+                    ccoupled[c] = 1;
+                }
+        // lmul: after every successor (successors have larger indices)
+        for (int64_t c = nB - 1; c >= 0; c--)
+            for (int64_t j = Bp[c]; j < Bp[c + 1]; j++)
+                for (int64_t p = Np[j]; p < Np[j + 1]; p++) {
+                    const int a = comp_of_vertex[ntgt[p]];
+                    lstage[a] = std::max(lstage[a], lstage[c] + 1);
+                }
+        auto build_stages = [&](const std::vector<int> &stage_of, std::vector<Stage> &out, std::vector<int> &sfronts,
+                                std::vector<int> &sverts) {
+            int ns = 0;
+            for (int64_t c = 0; c < nB; c++) ns = std::max(ns, stage_of[c] + 1);
+            if (nB == 0) ns = 0;
+            std::vector<std::vector<int>> comps(ns);
+            for (int64_t c = 0; c < nB; c++) comps[stage_of[c]].push_back((int)c);
+            out.clear();
+            for (int s = 0; s < ns; s++) {
+                Stage sg;
+                std::vector<std::vector<int>> byh(maxh + 1);
+                for (int c : comps[s])
+                    for (int64_t f = Fp[c]; f < Fp[c + 1]; f++) byh[height[f]].push_back((int)f);
+                for (int hh = 0; hh <= maxh; hh++) {
+                    if (byh[hh].empty()) continue;
+                    sg.levels.push_back({(int64_t)sfronts.size(), (int)byh[hh].size()});
+                    sfronts.insert(sfronts.end(), byh[hh].begin(), byh[hh].end());
+                }
+                sg.voff = (int64_t)sverts.size();
+                for (int c : comps[s])
+                    for (int64_t j = Bp[c]; j < Bp[c + 1]; j++)
+                        if (Np[j + 1] > Np[j]) sverts.push_back((int)j);
+                sg.nverts = (int)(sverts.size() - sg.voff);
+                sg.coupled = sg.nverts > 0;
+                out.push_back(std::move(sg));
+            }
+        };
+        std::vector<int> sfronts, sverts;
+        build_stages(lstage, hp.lstages, sfronts, sverts);
+        // rmul stages: the gather concerns the stage's own columns j (rows of earlier components feed them)
+        build_stages(rstage, hp.rstages, sfronts, sverts);
+        (void)ccoupled;
+        // factorization levels (classified per element size in prepare_workspace)
+        hp.flevels.assign(maxh + 1, Level());
+        std::vector<int64_t> Np64(Np.begin(), Np.end());
+        // device uploads
+        cudaStream_t st = h->stream;
+        CK(h, upload(h->d_rlo, rlo, st), "upload");
+        CK(h, upload(h->d_nn, hp.nn, st), "upload");
+        CK(h, upload(h->d_na, hp.na, st), "upload");
+        CK(h, upload(h->d_sptr, hp.sptr, st), "upload");
+        CK(h, upload(h->d_stgt, stgt, st), "upload");
+        CK(h, upload(h->d_rel, rel, st), "upload");
+        CK(h, upload(h->d_dptr, hp.dptr, st), "upload");
+        CK(h, upload(h->d_lptr, hp.lptr, st), "upload");
+        CK(h, upload(h->d_chdptr, hp.chdptr, st), "upload");
+        CK(h, upload(h->d_chdtgt, hp.chdtgt, st), "upload");
+        CK(h, upload(h->d_nptr, Np64, st), "upload");
+        CK(h, upload(h->d_ntgt, ntgt, st), "upload");
+        CK(h, upload(h->d_perm, permv, st), "upload");
+        CK(h, upload(h->d_invp, invp, st), "upload");
+        CK(h, upload(h->d_idx, idx, st), "upload");
+        CK(h, upload(h->d_bptr, bptr, st), "upload");
+        CK(h, upload(h->d_fcc, fcc, st), "upload");
+        CK(h, upload(h->d_sfronts, sfronts, st), "upload");
+        CK(h, upload(h->d_sverts, sverts, st), "upload");
+        CK(h, cudaStreamSynchronize(st), "upload");
+        DevPlan &d = hp.dev;
+        d.n = (int)n;
+        d.nf = (int)nf;
+        d.nB = (int)nB;
+        d.rlo = h->d_rlo.as<int>();
+        d.nn = h->d_nn.as<int>();
+        d.na = h->d_na.as<int>();
+        d.sptr = h->d_sptr.as<int64_t>();
+        d.stgt = h->d_stgt.as<int>();
+        d.rel = h->d_rel.as<int>();
+        d.dptr = h->d_dptr.as<int64_t>();
+        d.lptr = h->d_lptr.as<int64_t>();
+        d.chdptr = h->d_chdptr.as<int>();
+        d.chdtgt = h->d_chdtgt.as<int>();
+        d.nptr = h->d_nptr.as<int64_t>();
+        d.ntgt = h->d_ntgt.as<int>();
+        d.perm = h->d_perm.as<int>();
+        d.invp = h->d_invp.as<int>();
+        d.idx = h->d_idx.as<int>();
+        d.bptr = h->d_bptr.as<int>();
+        d.fcc = h->d_fcc.as<int>();
+        d.mptr = nullptr;
+        d.mld = nullptr;
+        d.fws = nullptr;
+        hp.d_sfronts = h->d_sfronts.as<int>();
+        hp.d_sverts = h->d_sverts.as<int>();
+        hp.d_rel = h->d_rel.as<int>();
+        h->invp = invp;
+        // factorization heights, kept for prepare_workspace
+        h->hp = std::move(hp);
+        h->hp.mld.clear();
+        h->hp.esize = 0;
+        // stash heights in flevels via a temporary: store front ids by height (classified later)
+        h->hp.h_ffronts.clear();
+        std::vector<std::vector<int>> byh(maxh + 1);
+        for (int64_t f = 0; f < nf; f++) byh[height[f]].push_back((int)f);
+        for (int hh = 0; hh <= maxh; hh++) {
+            FrontGroup g;
+            g.off = (int64_t)h->hp.h_ffronts.size();
+            g.count = (int)byh[hh].size();
+            g.max_nj = 0;
+            g.large = false;
+            h->hp.flevels[hh].groups.assign(1, g);
+            h->hp.h_ffronts.insert(h->hp.h_ffronts.end(), byh[hh].begin(), byh[hh].end());
+        }
+        h->nD = h->hp.dptr[nf];
+        h->nL = h->hp.lptr[nf];
+        h->ws_esize = 0;
+        // counters
+        pp_stats &s = h->st;
+        s = pp_stats{};
+        s.n = n;
+        s.nf = nf;
+        s.nB = nB;
+        s.nlevels = maxh + 1;
+        s.nD = h->nD;
+        s.nL = h->nL;
+        s.nN = nN;
+        double pairs = 0;
+        int64_t mx = 0;
+        for (int64_t f = 0; f < nf; f++) {
+            const double nn = h->hp.nn[f], na = h->hp.na[f], nj = nn + na;
+            auto S2 = [](double m) { return (m - 1) * m * (2 * m - 1) / 6; };
+            pairs += S2(nj) - S2(na);
+            mx = std::max<int64_t>(mx, (int64_t)nj);
+        }
+        s.pairs_factor = pairs;
+        s.max_front = mx;
+    } catch (const std::bad_alloc &) {
+        return fail(h, PP_ENOMEM, "pp_set_structure: out of host memory");
+    }
+    h->have_structure = true;
+    ok(h);
+    return PP_OK;
+}
+
+// Workspace layout for the element size of the values: fronts whose frontal matrix fits the one-CTA kernel's
+// shared memory keep a compact na x na update matrix; larger fronts keep their whole nj x nj frontal matrix,
+// and their update matrix is its trailing block.  Fronts of each level are grouped by size class.
+static int32_t prepare_workspace(pp_handle *h) {
+    HostPlan &hp = h->hp;
+    if (h->ws_esize == h->ops->esize && !hp.mld.empty()) return PP_OK;
+    const int limit = h->ops->small_limit;
+    const int nf = hp.nf;
+    hp.mptr.assign(nf, 0);
+    hp.fws.assign(nf, -1);
+    hp.mld.assign(nf, 1);
+    int64_t off = 0;
+    for (int f = 0; f < nf; f++) {
+        const int nn = hp.nn[f], na = hp.na[f], nj = nn + na;
+        if (nj <= limit) {
+            hp.mptr[f] = off;
+            hp.mld[f] = std::max(na, 1);
+            off += (int64_t)na * na;
+        } else {
+            hp.fws[f] = off;
+            hp.mptr[f] = off + nn + (int64_t)nn * nj;
+            hp.mld[f] = nj;
+            off += (int64_t)nj * nj;
+        }
+        off = (off + 3) & ~(int64_t)3;  // 16-byte alignment of every block
+    }
+    hp.ws_elems = off;
+    // size classes per level
+    std::vector<int> fronts;
+    const int classes[5] = {16, 32, 64, 128, limit};
+    for (Level &L : hp.flevels) {
+        std::vector<int> ids;
+        for (const FrontGroup &g : L.groups)
+            for (int t = 0; t < g.count; t++) ids.push_back(hp.h_ffronts[g.off + t]);
+        std::vector<FrontGroup> groups;
+        int lo = 0;
+        for (int c = 0; c < 5; c++) {
+            const int hi = classes[c];
+            if (hi <= lo) continue;
+            FrontGroup g;
+            g.off = (int64_t)fronts.size();
+            g.max_nj = 0;
+            g.large = false;
+            for (int f : ids) {
+                const int nj = hp.nn[f] + hp.na[f];
+                if (nj > lo && nj <= hi) {
+                    fronts.push_back(f);
+                    g.max_nj = std::max(g.max_nj, nj);
+                }
+            }
+            g.count = (int)(fronts.size() - g.off);
+            if (g.count) groups.push_back(g);
+            lo = hi;
+        }
+        FrontGroup g;
+        g.off = (int64_t)fronts.size();
+        g.large = true;
+        g.max_nj = 0;
+        for (int f : ids) {
+            const int nj = hp.nn[f] + hp.na[f];
+            if (nj > limit) {
+                fronts.push_back(f);
+                g.max_nj = std::max(g.max_nj, nj);
+            }
+        }
+        g.count = (int)(fronts.size() - g.off);
+        if (g.count) groups.push_back(g);
+        L.groups = std::move(groups);
+    }
+    hp.h_ffronts = fronts;
+    cudaStream_t st = h->stream;
+    CK(h, upload(h->d_mptr, hp.mptr, st), "upload");
+    CK(h, upload(h->d_mld, hp.mld, st), "upload");
+    CK(h, upload(h->d_fws, hp.fws, st), "upload");
+    CK(h, upload(h->d_ffronts, fronts, st), "upload");
+    CK(h, cudaStreamSynchronize(st), "upload");
+    hp.dev.mptr = h->d_mptr.as<int64_t>();
+    hp.dev.mld = h->d_mld.as<int>();
+    hp.dev.fws = h->d_fws.as<int64_t>();
+    hp.d_ffronts = h->d_ffronts.as<int>();
+    h->ws_esize = h->ops->esize;
+    return PP_OK;
+}
+
+static int32_t need_memory(pp_handle *h, size_t bytes, const char *what) {
+    size_t fr = 0, tot = 0;
+    if (cudaMemGetInfo(&fr, &tot) == cudaSuccess && bytes > fr)
+        return fail(h, PP_ENOMEM, "%s: needs %.3f GB of device memory, %.3f GB free", what, bytes / 1e9, fr / 1e9);
+    return PP_OK;
+}
+
+static int32_t set_semiring(pp_handle *h, int32_t sr, int32_t dt, const char *who) {
+    const Ops *o = get_ops(sr, dt);
+    if (!o) return fail(h, PP_EUNSUPPORTED, "%s: semiring %d with element type %d is not supported", who, sr, dt);
+    if (h->ops != o) {
+        h->ops = o;
+        h->ws_esize = 0;
+    }
+    h->sr = sr;
+    h->dt = dt;
+    int32_t r = prepare_workspace(h);
+    if (r != PP_OK) return r;
+    const size_t es = o->esize;
+    const size_t need = es * (2 * (size_t)h->nD + 2 * (size_t)h->nL + (size_t)h->hp.nN);
+    if (need_memory(h, need, who) != PP_OK) return PP_ENOMEM;
+    CK(h, h->LD.ensure(es * std::max<int64_t>(h->nD, 1)), who);
+    CK(h, h->UD.ensure(es * std::max<int64_t>(h->nD, 1)), who);
+    CK(h, h->LL.ensure(es * std::max<int64_t>(h->nL, 1)), who);
+    CK(h, h->UL.ensure(es * std::max<int64_t>(h->nL, 1)), who);
+    CK(h, h->Nval.ensure(es * std::max<int64_t>(h->hp.nN, 1)), who);
+    return PP_OK;
+}
+
+static Values values_of(pp_handle *h) {
+    Values v;
+    v.LD = h->LD.p;
+    v.LL = h->LL.p;
+    v.UD = h->UD.p;
+    v.UL = h->UL.p;
+    v.Nval = h->Nval.p;
+    v.W = h->W.p;
+    return v;
+}
+
+extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, const int64_t *colptr,
+                               const int64_t *rowval, const void *nzval, int32_t base) {
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_assemble: null handle");
+    if (!h->have_structure) return fail(h, PP_ESTATE, "pp_assemble: no structure (call pp_set_structure first)");
+    if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_assemble: base must be 0 or 1");
+    cudaSetDevice(h->device);
+    int32_t r = set_semiring(h, semiring, dtype, "pp_assemble");
+    if (r != PP_OK) return r;
+    const int n = h->hp.n;
+    if (n > 0 && (!colptr || (colptr[n] - base > 0 && (!rowval || !nzval))))
+        return fail(h, PP_EINVAL, "pp_assemble: null array");
+    std::vector<int> cp(n + 1), rv;
+    try {
+        for (int j = 0; j <= n; j++) {
+            const int64_t v = colptr[j] - base;
+            if (v < 0 || (j > 0 && v < cp[j - 1]) || v >= INT32_MAX) return fail(h, PP_EINVAL, "pp_assemble: colptr");
+            cp[j] = (int)v;
+        }
+        if (cp[0] != 0) return fail(h, PP_EINVAL, "pp_assemble: colptr must start at the base");
+        rv.resize(std::max(cp[n], 1));
+        for (int p = 0; p < cp[n]; p++) {
+            const int64_t v = rowval[p] - base;
+            if (v < 0 || v >= n) return fail(h, PP_EINVAL, "pp_assemble: row index out of range");
+            rv[p] = (int)v;
+        }
+        // no duplicate entries within a column (sparse() combines them before copyto!)
+        std::vector<int> mark(n, -1);
+        for (int j = 0; j < n; j++)
+            for (int p = cp[j]; p < cp[j + 1]; p++) {
+                if (mark[rv[p]] == j) return fail(h, PP_EINVAL, "pp_assemble: duplicate entry in column %d", j);
+                mark[rv[p]] = j;
+            }
+        if (semiring == PP_MINPLUS && dtype == PP_I32) {
+            const int32_t *a = static_cast<const int32_t *>(nzval);
+            for (int p = 0; p < cp[n]; p++)
+                if (a[p] < 0) return fail(h, PP_EUNSUPPORTED, "pp_assemble: Int32 MinPlus takes weights in [0, INT32_MAX]");
+        }
+    } catch (const std::bad_alloc &) {
+        return fail(h, PP_ENOMEM, "pp_assemble: out of host memory");
+    }
+    cudaStream_t st = h->stream;
+    const size_t es = h->ops->esize;
+    CK(h, upload(h->csc_ptr, cp, st), "pp_assemble");
+    CK(h, upload(h->csc_row, rv, st), "pp_assemble");
+    CK(h, h->csc_val.ensure(es * std::max(cp[n], 1)), "pp_assemble");
+    if (cp[n] > 0) CK(h, cudaMemcpyAsync(h->csc_val.p, nzval, es * cp[n], cudaMemcpyHostToDevice, st), "pp_assemble");
+    CK(h, h->ops->assemble(h->hp, h->csc_ptr.as<int>(), h->csc_row.as<int>(), h->csc_val.p, values_of(h), st),
+       "pp_assemble");
+    CK(h, cudaStreamSynchronize(st), "pp_assemble");
+    h->have_values = true;
+    h->factored = false;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, const void *LD, const void *LL,
+                                 const void *UD, const void *UL, const void *Nval) {
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_set_values: null handle");
+    if (!h->have_structure) return fail(h, PP_ESTATE, "pp_set_values: no structure");
+    cudaSetDevice(h->device);
+    int32_t r = set_semiring(h, semiring, dtype, "pp_set_values");
+    if (r != PP_OK) return r;
+    const size_t es = h->ops->esize;
+    cudaStream_t st = h->stream;
+    if ((h->nD > 0 && (!LD || !UD)) || (h->nL > 0 && (!LL || !UL)) || (h->hp.nN > 0 && !Nval))
+        return fail(h, PP_EINVAL, "pp_set_values: null array");
+    if (h->nD) CK(h, cudaMemcpyAsync(h->LD.p, LD, es * h->nD, cudaMemcpyHostToDevice, st), "pp_set_values");
+    if (h->nD) CK(h, cudaMemcpyAsync(h->UD.p, UD, es * h->nD, cudaMemcpyHostToDevice, st), "pp_set_values");
+    if (h->nL) CK(h, cudaMemcpyAsync(h->LL.p, LL, es * h->nL, cudaMemcpyHostToDevice, st), "pp_set_values");
+    if (h->nL) CK(h, cudaMemcpyAsync(h->UL.p, UL, es * h->nL, cudaMemcpyHostToDevice, st), "pp_set_values");
+    if (h->hp.nN) CK(h, cudaMemcpyAsync(h->Nval.p, Nval, es * h->hp.nN, cudaMemcpyHostToDevice, st), "pp_set_values");
+    CK(h, cudaStreamSynchronize(st), "pp_set_values");
+    h->have_values = true;
+    h->factored = false;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_factor(pp_handle *h) {
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_factor: null handle");
+    if (!h->have_values) return fail(h, PP_ESTATE, "pp_factor: no values (call pp_assemble or pp_set_values)");
+    cudaSetDevice(h->device);
+    const size_t wbytes = h->ops->esize * std::max<int64_t>(h->hp.ws_elems, 1);
+    if (wbytes > h->W.bytes) {
+        h->W.release();
+        if (need_memory(h, wbytes, "pp_factor") != PP_OK) return PP_ENOMEM;
+        CK(h, h->W.ensure(wbytes), "pp_factor");
+    }
+    cudaStream_t st = h->stream;
+    int64_t nl = 0;
+    CK(h, cudaEventRecord(h->ev0, st), "pp_factor");
+    CK(h, h->ops->factor(h->hp, values_of(h), st, &nl), "pp_factor");
+    CK(h, cudaEventRecord(h->ev1, st), "pp_factor");
+    CK(h, cudaEventSynchronize(h->ev1), "pp_factor");
+    float ms = 0;
+    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+    h->st.ms_factor = ms;
+    h->st.kernel_launches = nl;
+    h->factored = true;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_get_factor(pp_handle *h, void *LD, void *LL, void *UD, void *UL) {
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_get_factor: null handle");
+    if (!h->have_values) return fail(h, PP_ESTATE, "pp_get_factor: no values");
+    cudaSetDevice(h->device);
+    const size_t es = h->ops->esize;
+    cudaStream_t st = h->stream;
+    if (LD && h->nD) CK(h, cudaMemcpyAsync(LD, h->LD.p, es * h->nD, cudaMemcpyDeviceToHost, st), "pp_get_factor");
+    if (UD && h->nD) CK(h, cudaMemcpyAsync(UD, h->UD.p, es * h->nD, cudaMemcpyDeviceToHost, st), "pp_get_factor");
+    if (LL && h->nL) CK(h, cudaMemcpyAsync(LL, h->LL.p, es * h->nL, cudaMemcpyDeviceToHost, st), "pp_get_factor");
+    if (UL && h->nL) CK(h, cudaMemcpyAsync(UL, h->UL.p, es * h->nL, cudaMemcpyDeviceToHost, st), "pp_get_factor");
+    CK(h, cudaStreamSynchronize(st), "pp_get_factor");
+    ok(h);
+    return PP_OK;
+}
+
+static double solve_pairs_per_rhs(const HostPlan &hp) {
+    double s = 0;
+    for (int f = 0; f < hp.nf; f++) {
+        const double nn = hp.nn[f], na = hp.na[f];
+        s += nn * (nn - 1) + 2 * nn * na;
+    }
+    return s + (double)hp.nN;
+}
+
+// lmul! / rmul! on the device layout X[position][rhs]
+static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where, int left, const char *who) {
+    if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
+    if (!h->factored) return fail(h, PP_ESTATE, "%s: no factorization (call pp_factor)", who);
+    const int n = h->hp.n;
+    if (k < 0 || k >= INT32_MAX / 2) return fail(h, PP_EINVAL, "%s: k = %lld", who, (long long)k);
+    if (where != PP_HOST && where != PP_DEVICE) return fail(h, PP_EINVAL, "%s: where", who);
+    if (k == 0 || n == 0) {
+        ok(h);
+        return PP_OK;
+    }
+    if (!B) return fail(h, PP_EINVAL, "%s: null B", who);
+    if (left ? ldb < n : ldb < k) return fail(h, PP_EINVAL, "%s: leading dimension %lld", who, (long long)ldb);
+    cudaSetDevice(h->device);
+    const size_t es = h->ops->esize;
+    const int64_t ldx = (k + 3) & ~(int64_t)3;
+    const size_t xbytes = es * (size_t)n * ldx;
+    const size_t bbytes = es * (size_t)n * k;
+    size_t need = (xbytes > h->X.bytes ? xbytes : 0) + (where == PP_HOST && bbytes > h->stage_in.bytes ? bbytes : 0);
+    if (need_memory(h, need, who) != PP_OK) return PP_ENOMEM;
+    CK(h, h->X.ensure(xbytes), who);
+    cudaStream_t st = h->stream;
+    void *Bd = B;
+    int64_t ldbd = ldb;
+    if (where == PP_HOST) {
+        CK(h, h->stage_in.ensure(bbytes), who);
+        Bd = h->stage_in.p;
+        if (left) {
+            ldbd = n;
+            CK(h, cudaMemcpy2DAsync(Bd, es * n, B, es * ldb, es * n, k, cudaMemcpyHostToDevice, st), who);
+        } else {
+            ldbd = k;
+            CK(h, cudaMemcpy2DAsync(Bd, es * k, B, es * ldb, es * k, n, cudaMemcpyHostToDevice, st), who);
+        }
+    }
+    int64_t nl = 0;
+    CK(h, cudaEventRecord(h->ev0, st), who);
+    if (left)
+        CK(h, h->ops->rows_in(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    else
+        CK(h, h->ops->cols_in(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    CK(h, h->ops->solve(h->hp, values_of(h), left, h->X.p, ldx, (int)k, st, &nl), who);
+    if (left)
+        CK(h, h->ops->rows_out(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    else
+        CK(h, h->ops->cols_out(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    CK(h, cudaEventRecord(h->ev1, st), who);
+    if (where == PP_HOST) {
+        if (left)
+            CK(h, cudaMemcpy2DAsync(B, es * ldb, Bd, es * n, es * n, k, cudaMemcpyDeviceToHost, st), who);
+        else
+            CK(h, cudaMemcpy2DAsync(B, es * ldb, Bd, es * k, es * k, n, cudaMemcpyDeviceToHost, st), who);
+    }
+    CK(h, cudaStreamSynchronize(st), who);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+    h->st.ms_solve = ms;
+    h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)k;
+    h->st.kernel_launches = nl + 2;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_lmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where) {
+    return run_solve(h, B, ldb, k, where, 1, "pp_lmul");
+}
+
+extern "C" int32_t pp_rmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where) {
+    return run_solve(h, B, ldb, k, where, 0, "pp_rmul");
+}
+
+extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where) {
+    const char *who = "pp_star";
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_star: null handle");
+    if (!h->factored) return fail(h, PP_ESTATE, "pp_star: no factorization (call pp_factor)");
+    const int n = h->hp.n;
+    if (col0 < 0 || ncols < 0 || col0 + ncols > n) return fail(h, PP_EINVAL, "pp_star: columns out of range");
+    if (where != PP_HOST && where != PP_DEVICE) return fail(h, PP_EINVAL, "pp_star: where");
+    if (ncols == 0) {
+        ok(h);
+        return PP_OK;
+    }
+    if (!C || ldc < n) return fail(h, PP_EINVAL, "pp_star: C / ldc");
+    cudaSetDevice(h->device);
+    const size_t es = h->ops->esize;
+    // panel width: about 256 MB of right-hand sides per panel, a multiple of 32 columns
+    int64_t pw = ((int64_t)1 << 28) / std::max<int64_t>((int64_t)es * n, 1);
+    pw = std::max<int64_t>(32, std::min<int64_t>(pw & ~(int64_t)31, 4096));
+    pw = std::min<int64_t>(pw, (ncols + 31) & ~(int64_t)31);
+    const int64_t ldx = pw;
+    const size_t xbytes = es * (size_t)n * ldx;
+    const size_t sbytes = where == PP_HOST ? es * (size_t)n * pw : 0;
+    if (need_memory(h, (xbytes > h->X.bytes ? xbytes : 0) + (sbytes > h->stage_out.bytes ? sbytes : 0), who) != PP_OK)
+        return PP_ENOMEM;
+    CK(h, h->X.ensure(xbytes), who);
+    if (sbytes) CK(h, h->stage_out.ensure(sbytes), who);
+    cudaStream_t st = h->stream;
+    int64_t nl = 0;
+    float total = 0;
+    for (int64_t c0 = 0; c0 < ncols; c0 += pw) {
+        const int w = (int)std::min<int64_t>(pw, ncols - c0);
+        CK(h, cudaEventRecord(h->ev0, st), who);
+        CK(h, h->ops->fill_zero(h->X.p, (int64_t)n * ldx, st), who);
+        CK(h, h->ops->unit_sources(h->X.p, ldx, h->hp.dev.invp, col0 + c0, w, st), who);
+        CK(h, h->ops->solve(h->hp, values_of(h), 1, h->X.p, ldx, w, st, &nl), who);
+        void *dst = where == PP_HOST ? h->stage_out.p : (void *)(static_cast<char *>(C) + es * (size_t)c0 * ldc);
+        const int64_t lddst = where == PP_HOST ? n : ldc;
+        CK(h, h->ops->rows_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
+        CK(h, cudaEventRecord(h->ev1, st), who);
+        nl += 3;
+        if (where == PP_HOST)
+            CK(h, cudaMemcpy2DAsync(static_cast<char *>(C) + es * (size_t)c0 * ldc, es * ldc, h->stage_out.p, es * n,
+                                    es * n, w, cudaMemcpyDeviceToHost, st),
+               who);
+        CK(h, cudaStreamSynchronize(st), who);
+        float ms = 0;
+        cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+        total += ms;
+    }
+    h->st.ms_solve = total;
+    h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)ncols;
+    h->st.kernel_launches = nl;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_sync(pp_handle *h) {
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_sync: null handle");
+    cudaSetDevice(h->device);
+    CK(h, cudaStreamSynchronize(h->stream), "pp_sync");
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_get_stats(pp_handle *h, pp_stats *s) {
+    if (!h || !s) return fail(h, PP_EINVAL, "pp_get_stats: null argument");
+    int64_t bytes = 0;
+    for (DevBuf *b : {&h->d_rlo, &h->d_nn, &h->d_na, &h->d_sptr, &h->d_stgt, &h->d_rel, &h->d_dptr, &h->d_lptr,
+                      &h->d_chdptr, &h->d_chdtgt, &h->d_mptr, &h->d_mld, &h->d_fws, &h->d_nptr, &h->d_ntgt,
+                      &h->d_perm, &h->d_invp, &h->d_idx, &h->d_bptr, &h->d_fcc, &h->d_ffronts, &h->d_sfronts,
+                      &h->d_sverts, &h->LD, &h->LL, &h->UD, &h->UL, &h->Nval, &h->W, &h->X, &h->stage_in,
+                      &h->stage_out, &h->csc_ptr, &h->csc_row, &h->csc_val})
+        bytes += (int64_t)b->bytes;
+    h->st.device_bytes = bytes;
+    *s = h->st;
+    ok(h);
+    return PP_OK;
+}
+
+// ---------------------------------------------------------------- dense kernels on caller memory
+
+extern "C" int32_t pp_gemm(int32_t semiring, int32_t dtype, int64_t m, int64_t n, int64_t k, void *C, int64_t ldc,
+                           const void *A, int64_t lda, const void *B, int64_t ldb, void *stream) {
+    const Ops *o = get_ops(semiring, dtype);
+    if (!o) return fail(nullptr, PP_EUNSUPPORTED, "pp_gemm: semiring %d with element type %d", semiring, dtype);
+    if (m < 0 || n < 0 || k < 0 || m >= INT32_MAX || n >= INT32_MAX || k >= INT32_MAX)
+        return fail(nullptr, PP_EINVAL, "pp_gemm: sizes");
+    if (m == 0 || n == 0 || k == 0) {
+        ok(nullptr);
+        return PP_OK;
+    }
+    if (!C || !A || !B || ldc < m || lda < m || ldb < k) return fail(nullptr, PP_EINVAL, "pp_gemm: arrays / leading dimensions");
+    cudaError_t e = o->gemm(m, n, k, C, ldc, A, lda, B, ldb, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "pp_gemm");
+    ok(nullptr);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_getrf_batched(int32_t semiring, int32_t dtype, int64_t n, int64_t count, void *A, void *stream) {
+    const Ops *o = get_ops(semiring, dtype);
+    if (!o) return fail(nullptr, PP_EUNSUPPORTED, "pp_getrf_batched: semiring %d with element type %d", semiring, dtype);
+    if (n < 0 || count < 0) return fail(nullptr, PP_EINVAL, "pp_getrf_batched: sizes");
+    if (n == 0 || count == 0) {
+        ok(nullptr);
+        return PP_OK;
+    }
+    if (n > o->small_limit)
+        return fail(nullptr, PP_EUNSUPPORTED, "pp_getrf_batched: blocks larger than %d x %d", o->small_limit, o->small_limit);
+    if (!A) return fail(nullptr, PP_EINVAL, "pp_getrf_batched: null A");
+    cudaError_t e = o->getrf_batched((int)n, count, A, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "pp_getrf_batched");
+    ok(nullptr);
+    return PP_OK;
+}

@@ -1,0 +1,257 @@
+// gemm.cuh — the semiring GEMM C <- C (+) A (x) B on the ALUs (column-major operands).
+//
+// Replaces sgemx_gpu! and its kernels v2/v4/v6/v7/v8 (ext/PATHPACKCUDAExt/dense/sgemx.jl:27-737,
+// dense/sgemx_simt.jl:1-502).  The non-field semirings have no tensor-core form, so this is a register-tiled
+// SIMT kernel: a 256-thread CTA computes a BM x BN tile of C, each thread a TM x TN sub-tile held in registers,
+// with A and B staged through double-buffered shared memory.
+//
+// Shared memory holds k-pairs: As[kp][m] = (A[m][2kp], A[m][2kp+1]) and Bs[kp][n] likewise, so one step of
+// the inner loop combines two k's into each accumulator.  For Float32 MinPlus/MaxPlus that step is one
+// packed add (add.f32x2, FADD2) and one 3-input min/max (FMNMX3): one instruction per (x)(+) pair, the same
+// count as the reference's sm_100 kernel v8 (dense/sgemx_simt.jl:185-253).
+//
+// Thread (tr, tc) = (tid % 16, tid / 16) owns rows {q*16V + tr*V + e} and columns {q*16V + tc*V + e}, V pairs
+// per 16-byte vector, so the shared-memory reads of a warp are contiguous 256-byte runs (no bank conflicts).
+//
+// Out-of-range operands read as szero, which leaves an accumulator unchanged in every semiring (szero is
+// absorbing for (x) and the unit of (+); szero (x) szero = szero also for PlusProd).  Accumulators start from C
+// and take k in increasing order, which for PlusProd is the order of the reference's sgemx2!.
+#pragma once
+
+#include "semiring.cuh"
+
+namespace pp {
+
+template <typename T>
+struct alignas(2 * sizeof(T)) Pair {
+    T x, y;
+};
+
+template <typename T>
+struct GemmCfg;
+template <>
+struct GemmCfg<float> {
+    static constexpr int TM = 8, TN = 8, BK = 16;
+};
+template <>
+struct GemmCfg<int32_t> {
+    static constexpr int TM = 8, TN = 8, BK = 16;
+};
+template <>
+struct GemmCfg<double> {
+    static constexpr int TM = 8, TN = 4, BK = 8;
+};
+
+template <int SR, typename T>
+struct GemmKernel {
+    using S = Sem<SR, T>;
+    using P = Pair<T>;
+    static constexpr int TM = GemmCfg<T>::TM, TN = GemmCfg<T>::TN, BK = GemmCfg<T>::BK;
+    static constexpr int V = 16 / (int)sizeof(P);  // pairs per 16-byte vector
+    static constexpr int BM = 16 * TM, BN = 16 * TN, KP = BK / 2;
+    static constexpr int RA = 16 / (int)sizeof(T);  // rows of A per thread-chunk (one 16-byte load per column)
+    static constexpr int RB = 16 / (int)sizeof(T);  // k's of B per thread-chunk
+    static constexpr int ACH = (BM / RA) * KP;       // A chunks per tile
+    static constexpr int BCH = BN * (BK / RB);       // B chunks per tile
+    static constexpr int ANT = (ACH + 255) / 256, BNT = (BCH + 255) / 256;
+    static_assert(TM % V == 0 && TN % V == 0, "tile");
+    static constexpr size_t smem_bytes = 2 * (size_t)KP * (BM + BN) * sizeof(P);
+};
+
+template <typename T, int R>
+struct Vec;
+template <>
+struct Vec<float, 4> {
+    using type = float4;
+};
+template <>
+struct Vec<int32_t, 4> {
+    using type = int4;
+};
+template <>
+struct Vec<double, 2> {
+    using type = double2;
+};
+
+template <int SR, typename T>
+__global__ void __launch_bounds__(256, 1)
+    gemm_kernel(int M, int N, int K, T *__restrict__ C, int64_t ldc, const T *__restrict__ A, int64_t lda,
+                const T *__restrict__ B, int64_t ldb) {
+    using G = GemmKernel<SR, T>;
+    using S = typename G::S;
+    using P = typename G::P;
+    constexpr int TM = G::TM, TN = G::TN, BK = G::BK, V = G::V, BM = G::BM, BN = G::BN, KP = G::KP;
+    constexpr int RA = G::RA, RB = G::RB;
+    using VecT = typename Vec<T, RA>::type;
+
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    P *As = reinterpret_cast<P *>(smem_raw);  // [2][KP][BM]
+    P *Bs = As + 2 * KP * BM;                 // [2][KP][BN]
+
+    const int tid = threadIdx.x;
+    const int tr = tid & 15, tc = tid >> 4;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const T z = S::zero();
+
+    // accumulators start from C
+    T acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+        const int m = m0 + (i / V) * 16 * V + tr * V + (i % V);
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+            const int n = n0 + (j / V) * 16 * V + tc * V + (j % V);
+            acc[i][j] = (m < M && n < N) ? C[(int64_t)m + (int64_t)n * ldc] : z;
+        }
+    }
+
+    const bool avec = ((reinterpret_cast<uintptr_t>(A) | (uintptr_t)(lda * sizeof(T))) & 15) == 0;
+    const bool bvec = ((reinterpret_cast<uintptr_t>(B) | (uintptr_t)(ldb * sizeof(T))) & 15) == 0;
+
+    T ra[G::ANT][2][RA];
+    T rb[G::BNT][RB];
+
+    auto load_tile = [&](int k0) {
+#pragma unroll
+        for (int t = 0; t < G::ANT; t++) {
+            const int c = tid + t * 256;
+            if (c < G::ACH) {
+                const int kp = c / (BM / RA), mr = (c % (BM / RA)) * RA;
+                const int m = m0 + mr;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int k = k0 + 2 * kp + h;
+                    if (avec && k < K && m + RA <= M) {
+                        const VecT v = *reinterpret_cast<const VecT *>(A + (int64_t)m + (int64_t)k * lda);
+                        const T *pv = reinterpret_cast<const T *>(&v);
+#pragma unroll
+                        for (int e = 0; e < RA; e++) ra[t][h][e] = pv[e];
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < RA; e++)
+                            ra[t][h][e] = (k < K && m + e < M) ? A[(int64_t)(m + e) + (int64_t)k * lda] : z;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < G::BNT; t++) {
+            const int c = tid + t * 256;
+            if (c < G::BCH) {
+                const int kc = c % (BK / RB), nn = c / (BK / RB);
+                const int n = n0 + nn, k = k0 + kc * RB;
+                if (bvec && n < N && k + RB <= K) {
+                    const VecT v = *reinterpret_cast<const VecT *>(B + (int64_t)k + (int64_t)n * ldb);
+                    const T *pv = reinterpret_cast<const T *>(&v);
+#pragma unroll
+                    for (int e = 0; e < RB; e++) rb[t][e] = pv[e];
+                } else {
+#pragma unroll
+                    for (int e = 0; e < RB; e++)
+                        rb[t][e] = (n < N && k + e < K) ? B[(int64_t)(k + e) + (int64_t)n * ldb] : z;
+                }
+            }
+        }
+    };
+    auto store_tile = [&](int buf) {
+        P *as = As + buf * KP * BM;
+        P *bs = Bs + buf * KP * BN;
+#pragma unroll
+        for (int t = 0; t < G::ANT; t++) {
+            const int c = tid + t * 256;
+            if (c < G::ACH) {
+                const int kp = c / (BM / RA), mr = (c % (BM / RA)) * RA;
+#pragma unroll
+                for (int e = 0; e < RA; e++) {
+                    P p;
+                    p.x = ra[t][0][e];
+                    p.y = ra[t][1][e];
+                    as[kp * BM + mr + e] = p;
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < G::BNT; t++) {
+            const int c = tid + t * 256;
+            if (c < G::BCH) {
+                const int kc = c % (BK / RB), nn = c / (BK / RB);
+#pragma unroll
+                for (int e = 0; e < RB; e += 2) {
+                    P p;
+                    p.x = rb[t][e];
+                    p.y = rb[t][e + 1];
+                    bs[((kc * RB + e) / 2) * BN + nn] = p;
+                }
+            }
+        }
+    };
+
+    const int nk = (K + BK - 1) / BK;
+    if (nk > 0) {
+        load_tile(0);
+        store_tile(0);
+    }
+    __syncthreads();
+    for (int kt = 0; kt < nk; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < nk) load_tile((kt + 1) * BK);
+        const P *as = As + buf * KP * BM;
+        const P *bs = Bs + buf * KP * BN;
+#pragma unroll
+        for (int kp = 0; kp < KP; kp++) {
+            P a[TM], b[TN];
+#pragma unroll
+            for (int q = 0; q < TM / V; q++) {
+                const float4 v = *reinterpret_cast<const float4 *>(as + kp * BM + q * 16 * V + tr * V);
+                const P *pv = reinterpret_cast<const P *>(&v);
+#pragma unroll
+                for (int e = 0; e < V; e++) a[q * V + e] = pv[e];
+            }
+#pragma unroll
+            for (int q = 0; q < TN / V; q++) {
+                const float4 v = *reinterpret_cast<const float4 *>(bs + kp * BN + q * 16 * V + tc * V);
+                const P *pv = reinterpret_cast<const P *>(&v);
+#pragma unroll
+                for (int e = 0; e < V; e++) b[q * V + e] = pv[e];
+            }
+#pragma unroll
+            for (int i = 0; i < TM; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) acc[i][j] = S::muladd2(acc[i][j], a[i].x, a[i].y, b[j].x, b[j].y);
+        }
+        if (kt + 1 < nk) store_tile(buf ^ 1);
+        __syncthreads();
+    }
+
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+        const int m = m0 + (i / V) * 16 * V + tr * V + (i % V);
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+            const int n = n0 + (j / V) * 16 * V + tc * V + (j % V);
+            if (m < M && n < N) C[(int64_t)m + (int64_t)n * ldc] = acc[i][j];
+        }
+    }
+}
+
+// host launcher
+template <int SR, typename T>
+cudaError_t launch_gemm(int64_t M, int64_t N, int64_t K, T *C, int64_t ldc, const T *A, int64_t lda, const T *B,
+                        int64_t ldb, cudaStream_t st) {
+    using G = GemmKernel<SR, T>;
+    if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool attr[64] = {};
+    if (dev < 64 && !attr[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<SR, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)G::smem_bytes);
+        if (e != cudaSuccess) return e;
+        attr[dev] = true;
+    }
+    dim3 grid((unsigned)((M + G::BM - 1) / G::BM), (unsigned)((N + G::BN - 1) / G::BN));
+    gemm_kernel<SR, T><<<grid, 256, G::smem_bytes, st>>>((int)M, (int)N, (int)K, C, ldc, A, lda, B, ldb);
+    return cudaGetLastError();
+}
+
+}  // namespace pp

@@ -1,0 +1,51 @@
+// plan.h — device view of the symbolic structure and the host schedule built from it.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+namespace pp {
+
+// Device arrays of a structure (0-based, positions = permuted labels).  Per front f: the residual is
+// rlo[f] .. rlo[f]+nn[f]-1, the separator stgt[sptr[f] .. sptr[f+1]-1] with rel[] its positions in the
+// parent's bag, the blocks of the factor arrays start at dptr[f] (nn x nn) and lptr[f] (nn x na / na x nn),
+// and the front's update matrix lives in the workspace at mptr[f] with leading dimension mld[f].
+struct DevPlan {
+    int n, nf, nB;
+    const int *rlo, *nn, *na;
+    const int64_t *sptr;
+    const int *stgt, *rel;
+    const int64_t *dptr, *lptr;
+    const int *chdptr, *chdtgt;
+    const int64_t *mptr;
+    const int *mld;
+    const int64_t *fws;  // frontal matrix of a large front (elements), -1 for small fronts
+    const int64_t *nptr;
+    const int *ntgt;
+    const int *perm, *invp, *idx, *bptr, *fcc;
+};
+
+// A group of fronts launched together: one size class of one tree level.
+struct FrontGroup {
+    int64_t off;   // offset into the device front list
+    int count;
+    int max_nj;    // largest nn + na in the group
+    bool large;    // blocked path, one front at a time
+};
+
+struct Level {
+    std::vector<FrontGroup> groups;
+};
+
+// Solve schedule of one stage: components whose coupling predecessors (rmul) or successors (lmul) are all
+// in earlier stages.
+struct Stage {
+    std::vector<std::pair<int64_t, int>> levels;  // (offset, count) into the device solve-front list, by height
+    int64_t voff = 0;                             // offset into the device vertex list of the stage
+    int nverts = 0;
+    bool coupled = false;                          // any coupling entries touch the stage
+};
+
+}  // namespace pp

@@ -1,0 +1,192 @@
+"""The reference's user API on the B200 library: mlu, mstar, lu_, lmul_, rmul_, Matrix.
+
+PATHPACK.jl (src/CPU/abstract_slu.jl) exposes
+    F = mlu(s, A; alg, nt)   factor the star A* = U* L*          (:44-58)
+    mstar(s, A)              Matrix(mlu(s, A))                   (:81-87)
+    lu!(F)                   refactor in place                   (:119-121)
+    lmul!(F, B)              B <- A* B (columns of the star)     (:131-134)
+    rmul!(B, F)              B <- B A* (rows of the star)        (:142-145)
+    Matrix(F)                the whole star                      (:10-14)
+Python has no `!`: the in-place functions are lmul_, rmul_, lu_.  A factor is a B200SLU (the analogue of
+ChordalSLU, src/CPU/chordal_slu.jl:1-26) holding a library handle on one GPU.  Arrays are column-major as
+Julia's: numpy arrays are used in Fortran order (copied when they are not); CUDA torch tensors with column
+stride 1 are used in place on the device.
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import semiring as sr
+from ._lib import PP_DEVICE, PP_HOST, check, i64ptr, lib, pp_stats, vptr
+from .symbolic import Structure, ssymbolic
+
+
+def _csc(A, dtype=None):
+    """(n, colptr, rowval, nzval) of a square scipy.sparse matrix or dense array (entries != 0 are arcs for
+    dense input only through scipy), duplicates already combined by the caller."""
+    import scipy.sparse as sp
+
+    if not sp.issparse(A):
+        A = sp.csc_matrix(np.asarray(A))
+    A = sp.csc_matrix(A)
+    A.sort_indices()
+    n, m = A.shape
+    if n != m:
+        raise ValueError("the matrix must be square, got %s" % (A.shape,))
+    data = A.data if dtype is None else A.data.astype(dtype)
+    return n, A.indptr.astype(np.int64), A.indices.astype(np.int64), np.ascontiguousarray(data)
+
+
+class B200SLU:
+    """A factorization of the star of A over a semiring, held on one GPU (mlu's result)."""
+
+    def __init__(self, s, dtype, structure, device=0):
+        dtype = np.dtype(dtype)
+        if not sr.supported(s, dtype):
+            raise TypeError("%r over %s is not supported (pp_check_semiring)" % (s, dtype))
+        self.s, self.dtype, self.S, self.device = s, dtype, structure, device
+        self._dt = sr.DTYPES[dtype]
+        L = lib()
+        h = C.c_void_p()
+        check(L.pp_create(device, C.byref(h)))
+        self._h = h
+        S = structure
+        check(L.pp_set_structure(h, S.n, S.nf, S.nB, i64ptr(S.Rptr), i64ptr(S.Sptr), i64ptr(S.Stgt), i64ptr(S.Bptr),
+                                 i64ptr(S.Fptr), i64ptr(S.Nptr), i64ptr(S.Ntgt), i64ptr(S.perm), 0), h)
+
+    # --- lifecycle
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().pp_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def shape(self):
+        return (self.S.n, self.S.n)
+
+    # --- numeric phase
+    def assemble(self, A):
+        """copyto!(F, A): scatter A's entries into the factor arrays on the device."""
+        n, cp, rv, nz = _csc(A, self.dtype)
+        if n != self.S.n:
+            raise ValueError("matrix size %d does not match the structure (%d)" % (n, self.S.n))
+        check(lib().pp_assemble(self._h, self.s.id, self._dt, i64ptr(cp), i64ptr(rv), vptr(nz), 0), self._h)
+        return self
+
+    def set_values(self, LD, LL, UD, UL, Nval):
+        c = lambda a: np.ascontiguousarray(a, dtype=self.dtype)
+        LD, LL, UD, UL, Nval = (c(a) for a in (LD, LL, UD, UL, Nval))
+        check(lib().pp_set_values(self._h, self.s.id, self._dt, vptr(LD), vptr(LL), vptr(UD), vptr(UL), vptr(Nval)),
+              self._h)
+        return self
+
+    def factor(self):
+        """lu!(F): the multifrontal factorization of the star on the GPU."""
+        check(lib().pp_factor(self._h), self._h)
+        return self
+
+    def factors(self):
+        """(LD, LL, UD, UL) downloaded to the host (the ChordalSLU fields LDval, LLval, UDval, ULval)."""
+        nD, nL, _ = self.S.sizes()
+        LD, UD = np.empty(nD, self.dtype), np.empty(nD, self.dtype)
+        LL, UL = np.empty(nL, self.dtype), np.empty(nL, self.dtype)
+        check(lib().pp_get_factor(self._h, vptr(LD), vptr(LL), vptr(UD), vptr(UL)), self._h)
+        return LD, LL, UD, UL
+
+    def stats(self):
+        st = pp_stats()
+        check(lib().pp_get_stats(self._h, C.byref(st)), self._h)
+        return {k: getattr(st, k) for k, _ in pp_stats._fields_}
+
+    def sync(self):
+        check(lib().pp_sync(self._h), self._h)
+
+    # --- solves
+    def _solve(self, B, left):
+        n = self.S.n
+        fn = lib().pp_lmul if left else lib().pp_rmul
+        if hasattr(B, "data_ptr"):  # a CUDA torch tensor, used in place
+            if B.dtype.itemsize != self.dtype.itemsize or not B.is_cuda:
+                raise TypeError("B must be a CUDA tensor of the factor's element type")
+            if B.dim() == 1:
+                k, ld = 1, (n if left else 1)
+            else:
+                if B.stride(0) != 1:
+                    raise ValueError("B must be column-major (stride(0) == 1)")
+                k, ld = (B.shape[1], B.stride(1)) if left else (B.shape[0], B.stride(1))
+            check(fn(self._h, vptr(B), ld, k, PP_DEVICE), self._h)
+            return B
+        X = np.asarray(B)
+        vec = X.ndim == 1
+        X2 = X.reshape(-1, 1) if (vec and left) else (X.reshape(1, -1) if vec else X)
+        if (X2.shape[0] if left else X2.shape[1]) != n:
+            raise ValueError("B has %s rows/columns, the factor has %d vertices" % (X2.shape, n))
+        W = np.asfortranarray(X2, dtype=self.dtype)
+        k = W.shape[1] if left else W.shape[0]
+        ld = W.shape[0]
+        check(fn(self._h, vptr(W), ld, k, PP_HOST), self._h)
+        if isinstance(B, np.ndarray) and B.dtype == self.dtype and (W is B or np.shares_memory(W, B)):
+            return B
+        if isinstance(B, np.ndarray) and B.flags.writeable:
+            B[...] = W.reshape(B.shape)
+            return B
+        return W.reshape(X.shape)
+
+    def star(self, col0=0, ncols=None, out=None):
+        """Columns col0 .. col0+ncols-1 of A* (original labels) as an n x ncols column-major array."""
+        n = self.S.n
+        ncols = n - col0 if ncols is None else ncols
+        if out is None:
+            out = np.empty((n, ncols), dtype=self.dtype, order="F")
+        if hasattr(out, "data_ptr"):
+            check(lib().pp_star(self._h, vptr(out), out.stride(1), col0, ncols, PP_DEVICE), self._h)
+        else:
+            if not out.flags.f_contiguous:
+                raise ValueError("out must be column-major")
+            check(lib().pp_star(self._h, vptr(out), n, col0, ncols, PP_HOST), self._h)
+        return out
+
+
+def mlu(s, A, *, dtype=None, structure=None, device=0, method="nd"):
+    """F = mlu(s, A): symbolic analysis (host), assembly and factorization of the star on the GPU."""
+    n, cp, rv, nz = _csc(A, dtype)
+    dt = np.dtype(dtype) if dtype is not None else nz.dtype
+    S = structure if structure is not None else ssymbolic(n, cp, rv, method)
+    F = B200SLU(s, dt, S, device)
+    check(lib().pp_assemble(F._h, s.id, F._dt, i64ptr(cp), i64ptr(rv), vptr(np.ascontiguousarray(nz, dt)), 0), F._h)
+    return F.factor()
+
+
+def lu_(F):
+    """lu!(F): refactor (after assemble / set_values with new weights on the same structure)."""
+    return F.factor()
+
+
+def lmul_(F, B):
+    """lmul!(F, B): B <- A* B, the least solution of X = A X (+) B."""
+    return F._solve(B, True)
+
+
+def rmul_(B, F):
+    """rmul!(B, F): B <- B A*, the least solution of X = X A (+) B."""
+    return F._solve(B, False)
+
+
+def Matrix(F):
+    """Matrix(F): the whole star A*, n x n column-major."""
+    return F.star()
+
+
+def mstar(s, A, **kw):
+    """mstar(s, A) = Matrix(mlu(s, A))."""
+    F = mlu(s, A, **kw)
+    try:
+        return F.star()
+    finally:
+        F.close()

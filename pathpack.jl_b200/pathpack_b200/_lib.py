@@ -39,7 +39,7 @@ SIGNATURES = {
     "pp_last_error": (C.c_char_p, [_P]),
     "pp_create": (C.c_int32, [C.c_int32, C.POINTER(_P)]),
     "pp_destroy": (C.c_int32, [_P]),
-    "pp_set_structure": (C.c_int32, [_P, C.c_int64, C.c_int64, C.c_int64] + [_I64P] * 9 + [C.c_int32]),
+    "pp_set_structure": (C.c_int32, [_P, C.c_int64, C.c_int64, C.c_int64] + [_I64P] * 8 + [C.c_int32]),
     "pp_assemble": (C.c_int32, [_P, C.c_int32, C.c_int32, _I64P, _I64P, _P, C.c_int32]),
     "pp_set_values": (C.c_int32, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "pp_factor": (C.c_int32, [_P]),

@@ -79,6 +79,14 @@ class B200SLU:
         check(lib().pp_assemble(self._h, self.s.id, self._dt, i64ptr(cp), i64ptr(rv), vptr(nz), 0), self._h)
         return self
 
+    def assemble_csc(self, colptr, rowval, nzval):
+        """copyto!(F, A) from 0-based CSC arrays of A (no duplicates)."""
+        cp = np.ascontiguousarray(colptr, dtype=np.int64)
+        rv = np.ascontiguousarray(rowval, dtype=np.int64)
+        nz = np.ascontiguousarray(nzval, dtype=self.dtype)
+        check(lib().pp_assemble(self._h, self.s.id, self._dt, i64ptr(cp), i64ptr(rv), vptr(nz), 0), self._h)
+        return self
+
     def set_values(self, LD, LL, UD, UL, Nval):
         c = lambda a: np.ascontiguousarray(a, dtype=self.dtype)
         LD, LL, UD, UL, Nval = (c(a) for a in (LD, LL, UD, UL, Nval))

@@ -1,0 +1,159 @@
+"""Parity of the B200 library (through the C ABI) with the oracle, on the GPU.
+
+Every case runs the same seeded inputs through libpathpack_b200.so and through the oracle (the CPU
+restatement of the reference solver) and compares: bit-exact for the idempotent semirings (the device
+kernels keep the reference's per-element dataflow), rtol 1e-5 / 1e-12 for PlusProd and for the star of the
+floating tropical semirings (whose dense triangular star the reference associates differently).
+"""
+import numpy as np
+import pytest
+
+import pathpack_b200 as pp
+from oracle.oracle import OracleLU
+from oracle import oracle as orc
+from tests.helpers import CASES, EXACT, close, graph, same, weights
+
+pytestmark = pytest.mark.gpu
+
+SR = {s.__class__.__name__: s for s in [pp.MinPlus(), pp.MaxPlus(), pp.MaxMin(), pp.MinMax(), pp.MaxProd(),
+                                         pp.PlusProd(), pp.OrAnd()]}
+
+
+def torch_dt(dtype):
+    import torch
+
+    return {np.dtype(np.float32): torch.float32, np.dtype(np.float64): torch.float64,
+            np.dtype(np.int32): torch.int32}[np.dtype(dtype)]
+
+
+@pytest.mark.parametrize("name,dtype", CASES)
+@pytest.mark.parametrize("mnk", [(1, 1, 1), (7, 5, 3), (33, 65, 17), (130, 129, 40), (257, 200, 129)])
+def test_gemm(gpu, name, dtype, mnk):
+    import torch
+
+    m, n, k = mnk
+    rng = np.random.default_rng(m * 1000 + n * 10 + k)
+    A = np.asfortranarray(weights(name, dtype, m * k, 1).reshape(m, k))
+    B = np.asfortranarray(weights(name, dtype, k * n, 2).reshape(k, n))
+    C = np.asfortranarray(weights(name, dtype, m * n, 3).reshape(m, n))
+    if name != "OrAnd" and np.dtype(dtype) != np.int32:  # some "no path" entries
+        A[rng.random(A.shape) < 0.2] = SR[name].zero(dtype)
+    want = orc.gemm(name, C.copy(order="F"), A, B)
+    td = torch_dt(dtype)
+    At = torch.from_numpy(A.T.copy()).to("cuda").T  # column-major views
+    Bt = torch.from_numpy(B.T.copy()).to("cuda").T
+    Ct = torch.from_numpy(C.T.copy()).to("cuda").T
+    L = pp.lib()
+    pp._lib.check(L.pp_gemm(SR[name].id, pp.semiring.DTYPES[np.dtype(dtype)], m, n, k, Ct.data_ptr(), m,
+                            At.data_ptr(), m, Bt.data_ptr(), k, None))
+    torch.cuda.synchronize()
+    got = Ct.cpu().numpy()
+    assert Ct.dtype == td
+    same(got, want, name, dtype, "gemm %s" % (mnk,))
+
+
+@pytest.mark.parametrize("name,dtype", [("MinPlus", np.int32), ("MinPlus", np.float32), ("MaxMin", np.float64),
+                                        ("PlusProd", np.float64), ("OrAnd", np.int32)])
+@pytest.mark.parametrize("n", [1, 5, 64, 65, 128])
+def test_getrf_batched(gpu, name, dtype, n):
+    import torch
+
+    count = 7
+    A = weights(name, dtype, count * n * n, n).reshape(count, n, n)
+    if name == "MinPlus":
+        for b in range(count):
+            np.fill_diagonal(A[b], 0)
+    want = orc.getrf_batched(name, A.copy())
+    At = torch.from_numpy(A.copy()).to("cuda")
+    pp._lib.check(pp.lib().pp_getrf_batched(SR[name].id, pp.semiring.DTYPES[np.dtype(dtype)], n, count,
+                                            At.data_ptr(), None))
+    torch.cuda.synchronize()
+    same(At.cpu().numpy(), want, name, dtype, "getrf n=%d" % n)
+
+
+def factor_both(kind, name, dtype, seed=0):
+    n, cp, rv, nz = graph(kind, name, dtype, seed)
+    S = pp.ssymbolic(n, cp, rv)
+    F = pp.B200SLU(SR[name], dtype, S, device=0).assemble_csc(cp, rv, nz).factor()
+    O = OracleLU(name, dtype, S).assemble(cp, rv, nz).factor()
+    return n, S, F, O
+
+
+@pytest.mark.parametrize("name,dtype", CASES)
+@pytest.mark.parametrize("kind", ["grid", "sprand", "knn", "grid3d"])
+def test_factor_and_solves(gpu, name, dtype, kind):
+    n, S, F, O = factor_both(kind, name, dtype)
+    try:
+        for got, want, what in zip(F.factors(), (O.LD, O.LL, O.UD, O.UL), ("LD", "LL", "UD", "UL")):
+            same(got, want, name, dtype, "%s %s" % (kind, what))
+        rng = np.random.default_rng(5)
+        z, one = SR[name].zero(dtype), SR[name].one(dtype)
+        k = 37
+        B = np.full((n, k), z, dtype=dtype, order="F")
+        src = rng.choice(n, size=k, replace=False)
+        B[src, np.arange(k)] = one
+        B[rng.random(B.shape) < 0.05] = one
+        same(pp.lmul_(F, B.copy(order="F")), O.lmul(B), name, dtype, "%s lmul" % kind)
+        R = np.asfortranarray(B.T)
+        same(pp.rmul_(R.copy(order="F"), F), O.rmul(R), name, dtype, "%s rmul" % kind)
+        C = pp.Matrix(F)
+        close(C, O.star(), name, dtype, "%s star" % kind)
+        # the star through lmul's dataflow is the oracle's lmul of the identity, bit for bit
+        E = np.full((n, n), z, dtype=dtype, order="F")
+        np.fill_diagonal(E, one)
+        same(C, O.lmul(E), name, dtype, "%s star vs lmul(I)" % kind)
+    finally:
+        F.close()
+
+
+@pytest.mark.parametrize("name,dtype", [("MinPlus", np.float64), ("MaxMin", np.float32), ("PlusProd", np.float64),
+                                        ("MinPlus", np.float32)])
+def test_large_fronts(gpu, name, dtype):
+    """Fronts larger than the shared-memory kernel takes go through the blocked path (panel + GEMM)."""
+    n, S, F, O = factor_both("grid3d14", name, dtype)
+    try:
+        assert (S.nn + S.na).max() > {4: 202, 8: 143}[np.dtype(dtype).itemsize], "no large front"
+        for got, want, what in zip(F.factors(), (O.LD, O.LL, O.UD, O.UL), ("LD", "LL", "UD", "UL")):
+            same(got, want, name, dtype, "grid3d14 %s" % what)
+        B = np.asfortranarray(weights(name, dtype, n * 40, 9).reshape(n, 40))
+        same(pp.lmul_(F, B.copy(order="F")), O.lmul(B), name, dtype, "grid3d14 lmul")
+    finally:
+        F.close()
+
+
+@pytest.mark.parametrize("fixture", ["paris", "bunny"])
+def test_reference_structures(gpu, fixture):
+    """The reference's own AMF structures and factors (docs/src/public/data/*-lu.bin.gz): the device
+    factorization of MinPlus Float32 reproduces PATHPACK.jl's factor bit for bit."""
+    import os
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", fixture + ".npz"))
+    n = int(z["n"])
+    from pathpack_b200 import graphs
+
+    cp, rv, nz = graphs.csc(n, z["I"].astype(np.int64), z["J"].astype(np.int64), z["W"])
+    S = pp.Structure.from_arrays(n, z["Rptr"], z["Sptr"], z["Stgt"], z["Bptr"], z["Fptr"], z["Nptr"], z["Ntgt"],
+                                 z["perm"])
+    F = pp.B200SLU(pp.MinPlus(), np.float32, S).assemble_csc(cp, rv, nz).factor()
+    try:
+        LD, LL, UD, UL = F.factors()
+        nn = S.nn
+        Dp = np.concatenate([[0], np.cumsum(nn * nn)])
+        D = np.empty_like(UD)
+        for f in range(S.nf):
+            m = nn[f]
+            blk = slice(Dp[f], Dp[f + 1])
+            U = UD[blk].reshape(m, m, order="F")
+            L = LD[blk].reshape(m, m, order="F")
+            D[blk] = np.where(np.triu(np.ones((m, m), bool)), U, L).reshape(-1, order="F")
+        same(D, z["D"], "MinPlus", np.float32, fixture + " D")
+        same(UL, z["UL"], "MinPlus", np.float32, fixture + " UL")
+        same(LL, z["LL"], "MinPlus", np.float32, fixture + " LL")
+        O = OracleLU("MinPlus", np.float32, S).assemble(cp, rv, nz).factor()
+        B = np.full((n, 16), np.inf, np.float32, order="F")
+        B[np.arange(16) * 97 % n, np.arange(16)] = 0
+        same(pp.lmul_(F, B.copy(order="F")), O.lmul(B), "MinPlus", np.float32, fixture + " lmul")
+        R = np.asfortranarray(B.T)
+        same(pp.rmul_(R.copy(order="F"), F), O.rmul(R), "MinPlus", np.float32, fixture + " rmul")
+    finally:
+        F.close()

@@ -96,6 +96,12 @@ int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, const 
 int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, const int64_t *colptr, const int64_t *rowval,
                     const void *nzval, int32_t base);
 
+/* New weights for the pattern of the last pp_assemble (nzval in the same order, on the host or on this
+   handle's device), re-assembled on the device: refactorization with the same structure, the use of the
+   reference's plans (APSPPlan, ext/PATHPACKCUDAExt/api.jl:547-668; FactorPlan, chordal/sgetrf.jl:710-740).
+   Int32 MinPlus weights from device memory are not checked for the [0, INT32_MAX] domain. */
+int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t where);
+
 /* Upload already assembled factor arrays (host): LD, UD (|LD| values), LL, UL (|LL|), Nval (|Nval|). */
 int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, const void *LD, const void *LL, const void *UD,
                       const void *UL, const void *Nval);
@@ -124,6 +130,19 @@ int32_t pp_sync(pp_handle *h);
 
 /* Counters of the handle (sizes, pair counts, device times of the last calls). */
 int32_t pp_get_stats(pp_handle *h, pp_stats *s);
+
+/* Per-kernel-class device times: with profiling on, every launch of the handle is bracketed by CUDA events
+   on its stream and accumulated per class with its algorithmic bytes and (x)(+) pairs.  pp_set_profile
+   resets the totals. */
+typedef struct pp_kernel_class {
+    char name[32];
+    int64_t launches;
+    double ms;     /* summed device time of the launches */
+    double bytes;  /* algorithmic bytes moved by the launches */
+    double pairs;  /* (x)(+) pairs computed by the launches */
+} pp_kernel_class;
+int32_t pp_set_profile(pp_handle *h, int32_t on);
+int32_t pp_get_profile(pp_handle *h, pp_kernel_class *out, int32_t max, int32_t *count);
 
 /* The handle's CUDA stream (a cudaStream_t), for callers that order their own work after the handle's. */
 void *pp_stream(pp_handle *h);

@@ -44,6 +44,12 @@ const Ops *get_ops(int sr, int dt) {
 }
 }  // namespace pp
 
+namespace pp {
+const char *const KCLASS_NAMES[K_NCLASS] = {"front_small_kernel", "large_front_aux", "panel_kernel",
+                                            "gemm_kernel(trailing)", "sweep_kernel(forward)",
+                                            "sweep_kernel(backward)", "coupling", "permute", "assemble_kernel"};
+}
+
 using namespace pp;
 
 static thread_local std::string g_err;
@@ -88,8 +94,10 @@ struct pp_handle {
     // values and work
     DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val;
     int64_t nD = 0, nL = 0;
+    int64_t nnz_assembled = -1;
     size_t ws_esize = 0;
     pp_stats st{};
+    Profiler prof;
 };
 
 static int32_t fail(pp_handle *h, int32_t code, const char *fmt, ...) {
@@ -189,6 +197,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
     if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_set_structure: base must be 0 or 1");
     cudaSetDevice(h->device);
     h->have_structure = h->have_values = h->factored = false;
+    h->nnz_assembled = -1;
     HostPlan hp;
     hp.n = (int)n;
     hp.nf = (int)nf;
@@ -341,7 +350,17 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                     for (int64_t f = Fp[c]; f < Fp[c + 1]; f++) byh[height[f]].push_back((int)f);
                 for (int hh = 0; hh <= maxh; hh++) {
                     if (byh[hh].empty()) continue;
-                    sg.levels.push_back({(int64_t)sfronts.size(), (int)byh[hh].size()});
+                    SLevel lv;
+                    lv.off = (int64_t)sfronts.size();
+                    lv.count = (int)byh[hh].size();
+                    for (int f : byh[hh]) {
+                        const double nn = hp.nn[f], na = hp.na[f];
+                        lv.res_rows += nn;
+                        lv.sep_rows += na;
+                        lv.blk_elems += nn * nn + nn * na;
+                        lv.pairs_col += nn * (nn - 1) / 2 + nn * na;
+                    }
+                    sg.levels.push_back(lv);
                     sfronts.insert(sfronts.end(), byh[hh].begin(), byh[hh].end());
                 }
                 sg.voff = (int64_t)sverts.size();
@@ -459,6 +478,20 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
     return PP_OK;
 }
 
+// Algorithmic traffic (elements) and (x)(+) pairs of one front's factorization: read the assembled blocks
+// and the children's update matrices, write the factor blocks and the update matrix; the partial LU's pairs.
+static void front_cost(const HostPlan &hp, int f, FrontGroup &g) {
+    const double nn = hp.nn[f], na = hp.na[f], nj = nn + na;
+    double e = 4.0 * (nn * nn + nn * na) + na * na;
+    for (int c = hp.chdptr[f]; c < hp.chdptr[f + 1]; c++) {
+        const double nac = hp.na[hp.chdtgt[c]];
+        e += nac * nac;
+    }
+    auto S2 = [](double m) { return (m - 1) * m * (2 * m - 1) / 6; };
+    g.bytes += e;
+    g.pairs += S2(nj) - S2(na);
+}
+
 // Workspace layout for the element size of the values: fronts whose frontal matrix fits the one-CTA kernel's
 // shared memory keep a compact na x na update matrix; larger fronts keep their whole nj x nj frontal matrix,
 // and their update matrix is its trailing block.  Fronts of each level are grouped by size class.
@@ -510,6 +543,7 @@ static int32_t prepare_workspace(pp_handle *h) {
                 }
             }
             g.count = (int)(fronts.size() - g.off);
+            for (int64_t t = g.off; t < (int64_t)fronts.size(); t++) front_cost(hp, fronts[t], g);
             if (g.count) groups.push_back(g);
             lo = hi;
         }
@@ -525,6 +559,7 @@ static int32_t prepare_workspace(pp_handle *h) {
             }
         }
         g.count = (int)(fronts.size() - g.off);
+        for (int64_t t = g.off; t < (int64_t)fronts.size(); t++) front_cost(hp, fronts[t], g);
         if (g.count) groups.push_back(g);
         L.groups = std::move(groups);
     }
@@ -559,6 +594,8 @@ static int32_t set_semiring(pp_handle *h, int32_t sr, int32_t dt, const char *wh
     }
     h->sr = sr;
     h->dt = dt;
+    h->prof.esize = o->esize;
+    h->hp.prof = &h->prof;
     int32_t r = prepare_workspace(h);
     if (r != PP_OK) return r;
     const size_t es = o->esize;
@@ -629,9 +666,43 @@ extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, co
     CK(h, upload(h->csc_row, rv, st), "pp_assemble");
     CK(h, h->csc_val.ensure(es * std::max(cp[n], 1)), "pp_assemble");
     if (cp[n] > 0) CK(h, cudaMemcpyAsync(h->csc_val.p, nzval, es * cp[n], cudaMemcpyHostToDevice, st), "pp_assemble");
+    int pi = h->prof.begin(K_ASSEMBLE, st);
     CK(h, h->ops->assemble(h->hp, h->csc_ptr.as<int>(), h->csc_row.as<int>(), h->csc_val.p, values_of(h), st),
        "pp_assemble");
+    h->prof.end(pi, st, 2.0 * (h->nD + h->nL) + h->hp.nN + (double)cp[n] * (1.0 + 8.0 / es), 0);
     CK(h, cudaStreamSynchronize(st), "pp_assemble");
+    h->prof.collect();
+    h->nnz_assembled = cp[n];
+    h->have_values = true;
+    h->factored = false;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t where) {
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_update_values: null handle");
+    if (!h->have_structure || h->nnz_assembled < 0)
+        return fail(h, PP_ESTATE, "pp_update_values: no pattern (call pp_assemble first)");
+    if (where != PP_HOST && where != PP_DEVICE) return fail(h, PP_EINVAL, "pp_update_values: where");
+    const int64_t nnz = h->nnz_assembled;
+    if (nnz > 0 && !nzval) return fail(h, PP_EINVAL, "pp_update_values: null nzval");
+    cudaSetDevice(h->device);
+    const size_t es = h->ops->esize;
+    if (where == PP_HOST && h->sr == PP_MINPLUS && h->dt == PP_I32) {
+        const int32_t *a = static_cast<const int32_t *>(nzval);
+        for (int64_t p = 0; p < nnz; p++)
+            if (a[p] < 0) return fail(h, PP_EUNSUPPORTED, "pp_update_values: Int32 MinPlus takes weights in [0, INT32_MAX]");
+    }
+    cudaStream_t st = h->stream;
+    if (nnz > 0)
+        CK(h, cudaMemcpyAsync(h->csc_val.p, nzval, es * nnz, where == PP_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                              st), "pp_update_values");
+    int pi = h->prof.begin(K_ASSEMBLE, st);
+    CK(h, h->ops->assemble(h->hp, h->csc_ptr.as<int>(), h->csc_row.as<int>(), h->csc_val.p, values_of(h), st),
+       "pp_update_values");
+    h->prof.end(pi, st, 2.0 * (h->nD + h->nL) + h->hp.nN + (double)nnz * (1.0 + 8.0 / es), 0);
+    CK(h, cudaStreamSynchronize(st), "pp_update_values");
+    h->prof.collect();
     h->have_values = true;
     h->factored = false;
     ok(h);
@@ -677,6 +748,7 @@ extern "C" int32_t pp_factor(pp_handle *h) {
     CK(h, h->ops->factor(h->hp, values_of(h), st, &nl), "pp_factor");
     CK(h, cudaEventRecord(h->ev1, st), "pp_factor");
     CK(h, cudaEventSynchronize(h->ev1), "pp_factor");
+    h->prof.collect();
     float ms = 0;
     cudaEventElapsedTime(&ms, h->ev0, h->ev1);
     h->st.ms_factor = ms;
@@ -747,15 +819,19 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
     }
     int64_t nl = 0;
     CK(h, cudaEventRecord(h->ev0, st), who);
+    int pi = h->prof.begin(K_PERMUTE, st);
     if (left)
         CK(h, h->ops->rows_in(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
     else
         CK(h, h->ops->cols_in(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    h->prof.end(pi, st, 2.0 * n * k, 0);
     CK(h, h->ops->solve(h->hp, values_of(h), left, h->X.p, ldx, (int)k, st, &nl), who);
+    pi = h->prof.begin(K_PERMUTE, st);
     if (left)
         CK(h, h->ops->rows_out(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
     else
         CK(h, h->ops->cols_out(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    h->prof.end(pi, st, 2.0 * n * k, 0);
     CK(h, cudaEventRecord(h->ev1, st), who);
     if (where == PP_HOST) {
         if (left)
@@ -764,6 +840,7 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
             CK(h, cudaMemcpy2DAsync(B, es * ldb, Bd, es * k, es * k, n, cudaMemcpyDeviceToHost, st), who);
     }
     CK(h, cudaStreamSynchronize(st), who);
+    h->prof.collect();
     float ms = 0;
     cudaEventElapsedTime(&ms, h->ev0, h->ev1);
     h->st.ms_solve = ms;
@@ -817,7 +894,9 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
         CK(h, h->ops->solve(h->hp, values_of(h), 1, h->X.p, ldx, w, st, &nl), who);
         void *dst = where == PP_HOST ? h->stage_out.p : (void *)(static_cast<char *>(C) + es * (size_t)c0 * ldc);
         const int64_t lddst = where == PP_HOST ? n : ldc;
+        const int pi = h->prof.begin(K_PERMUTE, st);
         CK(h, h->ops->rows_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
+        h->prof.end(pi, st, 2.0 * n * w, 0);
         CK(h, cudaEventRecord(h->ev1, st), who);
         nl += 3;
         if (where == PP_HOST)
@@ -825,6 +904,7 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
                                     es * n, w, cudaMemcpyDeviceToHost, st),
                who);
         CK(h, cudaStreamSynchronize(st), who);
+        h->prof.collect();
         float ms = 0;
         cudaEventElapsedTime(&ms, h->ev0, h->ev1);
         total += ms;
@@ -855,6 +935,37 @@ extern "C" int32_t pp_get_stats(pp_handle *h, pp_stats *s) {
         bytes += (int64_t)b->bytes;
     h->st.device_bytes = bytes;
     *s = h->st;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_set_profile(pp_handle *h, int32_t on) {
+    if (!h) return fail(nullptr, PP_EINVAL, "pp_set_profile: null handle");
+    cudaSetDevice(h->device);
+    cudaStreamSynchronize(h->stream);
+    h->prof.reset();
+    h->prof.on = on != 0;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_get_profile(pp_handle *h, pp_kernel_class *out, int32_t max, int32_t *count) {
+    if (!h || (!out && max > 0)) return fail(h, PP_EINVAL, "pp_get_profile: null argument");
+    cudaSetDevice(h->device);
+    cudaStreamSynchronize(h->stream);
+    h->prof.collect();
+    int c = 0;
+    for (int k = 0; k < K_NCLASS && c < max; k++) {
+        if (h->prof.launches[k] == 0) continue;
+        pp_kernel_class &o = out[c++];
+        std::memset(&o, 0, sizeof o);
+        std::strncpy(o.name, KCLASS_NAMES[k], sizeof o.name - 1);
+        o.launches = h->prof.launches[k];
+        o.ms = h->prof.ms[k];
+        o.bytes = h->prof.bytes[k];
+        o.pairs = h->prof.pairs[k];
+    }
+    if (count) *count = c;
     ok(h);
     return PP_OK;
 }

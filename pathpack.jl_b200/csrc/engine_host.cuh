@@ -67,9 +67,11 @@ struct Engine {
             for (const FrontGroup &g : L.groups) {
                 if (!g.large) {
                     const size_t smem = (size_t)g.max_nj * g.max_nj * sizeof(T);
+                    const int pi = hp.prof ? hp.prof->begin(K_FRONT, st) : -1;
                     front_small_kernel<SR, T><<<g.count, threads_for(g.max_nj), smem, st>>>(
                         hp.d_ffronts + g.off, hp.dev, LD, LL, UD, UL, W);
                     PP_TRY(cudaGetLastError());
+                    if (pi >= 0) hp.prof->end(pi, st, g.bytes, g.pairs);
                     nl++;
                     continue;
                 }
@@ -88,8 +90,11 @@ struct Engine {
         const int nn = hp.nn[f], na = hp.na[f], nj = nn + na;
         T *F = W + hp.fws[f];
         const int64_t nj2 = (int64_t)nj * nj;
+        Profiler *pr = hp.prof;
+        int pi = pr ? pr->begin(K_LARGE_AUX, st) : -1;
         PP_TRY(fill_zero(F, nj2, st));
         (*nl)++;
+        double aux = (double)nj2;
         for (int c = hp.chdptr[f + 1] - 1; c >= hp.chdptr[f]; c--) {
             const int ch = hp.chdtgt[c];
             const int nac = hp.na[ch];
@@ -97,28 +102,39 @@ struct Engine {
                 F, nj, W + hp.mptr[ch], hp.mld[ch], hp.d_rel + hp.sptr[ch], nac);
             PP_TRY(cudaGetLastError());
             (*nl)++;
+            aux += 3.0 * nac * nac;
         }
         combine_kernel<SR, T><<<grid_for(nj2, 256), 256, 0, st>>>(F, nn, na, hp.dptr[f], hp.lptr[f], LD, LL, UD, UL);
         PP_TRY(cudaGetLastError());
         (*nl)++;
+        aux += 2.0 * nj2 + 2.0 * nn * nn + 2.0 * nn * na;
+        if (pi >= 0) pr->end(pi, st, aux, 0);
         for (int k = 0; k < nn; k += PANEL_NB) {
             const int b = std::min(PANEL_NB, nn - k);
             const int rem = nj - k - b;
             const int nca = (rem + PANEL_THREADS - 1) / PANEL_THREADS;
+            pi = pr ? pr->begin(K_PANEL, st) : -1;
             panel_kernel<SR, T><<<1 + 2 * nca, PANEL_THREADS, 0, st>>>(F, nj, nj, k, b, nca);
             PP_TRY(cudaGetLastError());
+            if (pi >= 0)
+                pr->end(pi, st, 2.0 * b * b + 4.0 * rem * b,
+                        (double)(b - 1) * b * (2.0 * b - 1) / 6 + (double)rem * b * (b - 1));
             (*nl)++;
             if (rem > 0) {
                 T *C = F + (k + b) + (int64_t)(k + b) * nj;
                 const T *A = F + (k + b) + (int64_t)k * nj;
                 const T *B = F + k + (int64_t)(k + b) * nj;
+                pi = pr ? pr->begin(K_GEMM, st) : -1;
                 PP_TRY((launch_gemm<SR, T>(rem, rem, b, C, nj, A, nj, B, nj, st)));
+                if (pi >= 0) pr->end(pi, st, 2.0 * rem * b + 2.0 * rem * (double)rem, (double)rem * rem * b);
                 (*nl)++;
             }
         }
+        pi = pr ? pr->begin(K_LARGE_AUX, st) : -1;
         extract_kernel<T><<<grid_for((int64_t)nj * nn + (int64_t)nn * na, 256), 256, 0, st>>>(
             F, nn, na, hp.dptr[f], hp.lptr[f], LD, LL, UD, UL);
         PP_TRY(cudaGetLastError());
+        if (pi >= 0) pr->end(pi, st, 2.0 * ((double)nj * nn + (double)nn * na), 0);
         (*nl)++;
         return cudaSuccess;
     }
@@ -129,12 +145,16 @@ struct Engine {
         const int ny = (k + 31) / 32;
         const int nlev = (int)sg.levels.size();
         for (int t = 0; t < nlev; t++) {
-            const auto &lv = sg.levels[ascending ? t : nlev - 1 - t];
-            if (lv.second == 0) continue;
-            dim3 grid((unsigned)lv.second, (unsigned)ny);
-            sweep_kernel<SR, T, FWD, TRANS><<<grid, 256, 0, st>>>(hp.d_sfronts + lv.first, hp.dev, Dv, Ov, X, ldx, k,
+            const SLevel &lv = sg.levels[ascending ? t : nlev - 1 - t];
+            if (lv.count == 0) continue;
+            dim3 grid((unsigned)lv.count, (unsigned)ny);
+            const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD : K_SWEEP_BWD, st) : -1;
+            sweep_kernel<SR, T, FWD, TRANS><<<grid, 256, 0, st>>>(hp.d_sfronts + lv.off, hp.dev, Dv, Ov, X, ldx, k,
                                                                  unit);
             PP_TRY(cudaGetLastError());
+            if (pi >= 0)
+                hp.prof->end(pi, st, (double)k * (2.0 * lv.res_rows + (FWD ? 2.0 : 1.0) * lv.sep_rows) + lv.blk_elems,
+                             (double)k * lv.pairs_col);
             (*nl)++;
         }
         return cudaSuccess;
@@ -155,18 +175,22 @@ struct Engine {
                 PP_TRY((sweep_levels<true, false>(hp, sg, true, LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_levels<false, false>(hp, sg, false, UD, UL, X, ldx, k, 0, st, &nl)));
                 if (sg.coupled && sg.nverts > 0) {
+                    const int pi = hp.prof ? hp.prof->begin(K_COUPLING, st) : -1;
                     coupling_scatter_kernel<SR, T><<<(sg.nverts + 7) / 8, 256, 0, st>>>(
                         hp.d_sverts + sg.voff, sg.nverts, hp.dev, Nv, X, ldx, k);
                     PP_TRY(cudaGetLastError());
+                    if (pi >= 0) hp.prof->end(pi, st, 0, 0);
                     nl++;
                 }
             }
         } else {
             for (const Stage &sg : hp.rstages) {
                 if (sg.coupled && sg.nverts > 0) {
+                    const int pi = hp.prof ? hp.prof->begin(K_COUPLING, st) : -1;
                     coupling_gather_kernel<SR, T><<<(sg.nverts + 7) / 8, 256, 0, st>>>(
                         hp.d_sverts + sg.voff, sg.nverts, hp.dev, Nv, X, ldx, k);
                     PP_TRY(cudaGetLastError());
+                    if (pi >= 0) hp.prof->end(pi, st, 0, 0);
                     nl++;
                 }
                 PP_TRY((sweep_levels<true, true>(hp, sg, true, UD, UL, X, ldx, k, 0, st, &nl)));

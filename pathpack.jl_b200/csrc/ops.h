@@ -10,6 +10,77 @@
 
 namespace pp {
 
+// Kernel classes the profiler separates.
+enum KClass { K_FRONT = 0, K_LARGE_AUX, K_PANEL, K_GEMM, K_SWEEP_FWD, K_SWEEP_BWD, K_COUPLING, K_PERMUTE, K_ASSEMBLE,
+              K_NCLASS };
+extern const char *const KCLASS_NAMES[K_NCLASS];
+
+// Optional per-launch timing with CUDA events on the launching stream; off unless pp_set_profile enabled it.
+struct Profiler {
+    bool on = false;
+    size_t esize = 0;
+    struct Rec {
+        int cls;
+        cudaEvent_t a, b;
+        double bytes, pairs;
+    };
+    std::vector<Rec> recs;
+    std::vector<cudaEvent_t> pool;
+    int64_t launches[K_NCLASS] = {};
+    double ms[K_NCLASS] = {}, bytes[K_NCLASS] = {}, pairs[K_NCLASS] = {};
+    int begin(int cls, cudaStream_t st) {
+        if (!on) return -1;
+        Rec r{cls, take(), take(), 0, 0};
+        cudaEventRecord(r.a, st);
+        recs.push_back(r);
+        return (int)recs.size() - 1;
+    }
+    void end(int i, cudaStream_t st, double elems, double prs) {
+        if (i < 0) return;
+        recs[i].bytes = elems * (double)esize;
+        recs[i].pairs = prs;
+        cudaEventRecord(recs[i].b, st);
+    }
+    cudaEvent_t take() {
+        if (pool.empty()) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            return e;
+        }
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    // after the stream is synchronised: add the recorded launches to the per-class totals
+    void collect() {
+        for (Rec &r : recs) {
+            float t = 0;
+            cudaEventElapsedTime(&t, r.a, r.b);
+            launches[r.cls]++;
+            ms[r.cls] += t;
+            bytes[r.cls] += r.bytes;
+            pairs[r.cls] += r.pairs;
+            pool.push_back(r.a);
+            pool.push_back(r.b);
+        }
+        recs.clear();
+    }
+    void reset() {
+        collect();
+        for (int c = 0; c < K_NCLASS; c++) {
+            launches[c] = 0;
+            ms[c] = bytes[c] = pairs[c] = 0;
+        }
+    }
+    ~Profiler() {
+        for (Rec &r : recs) {
+            cudaEventDestroy(r.a);
+            cudaEventDestroy(r.b);
+        }
+        for (cudaEvent_t e : pool) cudaEventDestroy(e);
+    }
+};
+
 // Host copy of the schedule and of the per-front sizes the drivers need, plus the device lists.
 struct HostPlan {
     int n = 0, nf = 0, nB = 0;
@@ -31,6 +102,7 @@ struct HostPlan {
     const int *d_sverts = nullptr;    // vertices of every stage (both schedules)
     const int *d_rel = nullptr;
     DevPlan dev{};
+    Profiler *prof = nullptr;
 };
 
 struct Values {

@@ -33,6 +33,15 @@ struct FrontGroup {
     int count;
     int max_nj;    // largest nn + na in the group
     bool large;    // blocked path, one front at a time
+    double bytes = 0, pairs = 0;  // algorithmic traffic (element count) and (x)(+) pairs of the group's launch
+};
+
+// One tree level of a solve stage: fronts d_sfronts[off .. off+count), with the per-right-hand-side sums the
+// profiler needs (residual rows, separator rows, factor-block elements, (x)(+) pairs).
+struct SLevel {
+    int64_t off = 0;
+    int count = 0;
+    double res_rows = 0, sep_rows = 0, blk_elems = 0, pairs_col = 0;
 };
 
 struct Level {
@@ -42,7 +51,7 @@ struct Level {
 // Solve schedule of one stage: components whose coupling predecessors (rmul) or successors (lmul) are all
 // in earlier stages.
 struct Stage {
-    std::vector<std::pair<int64_t, int>> levels;  // (offset, count) into the device solve-front list, by height
+    std::vector<SLevel> levels;  // by height
     int64_t voff = 0;                             // offset into the device vertex list of the stage
     int nverts = 0;
     bool coupled = false;                          // any coupling entries touch the stage

@@ -30,6 +30,11 @@ class pp_stats(C.Structure):
                 ("pairs_solve", C.c_double), ("device_bytes", C.c_int64), ("kernel_launches", C.c_int64)]
 
 
+class pp_kernel_class(C.Structure):
+    _fields_ = [("name", C.c_char * 32), ("launches", C.c_int64), ("ms", C.c_double), ("bytes", C.c_double),
+                ("pairs", C.c_double)]
+
+
 # every symbol the header declares, with its ctypes signature
 _P = C.c_void_p
 _I64P = C.POINTER(C.c_int64)
@@ -41,6 +46,7 @@ SIGNATURES = {
     "pp_destroy": (C.c_int32, [_P]),
     "pp_set_structure": (C.c_int32, [_P, C.c_int64, C.c_int64, C.c_int64] + [_I64P] * 8 + [C.c_int32]),
     "pp_assemble": (C.c_int32, [_P, C.c_int32, C.c_int32, _I64P, _I64P, _P, C.c_int32]),
+    "pp_update_values": (C.c_int32, [_P, _P, C.c_int32]),
     "pp_set_values": (C.c_int32, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "pp_factor": (C.c_int32, [_P]),
     "pp_get_factor": (C.c_int32, [_P, _P, _P, _P, _P]),
@@ -50,6 +56,8 @@ SIGNATURES = {
     "pp_sync": (C.c_int32, [_P]),
     "pp_get_stats": (C.c_int32, [_P, C.POINTER(pp_stats)]),
     "pp_stream": (_P, [_P]),
+    "pp_set_profile": (C.c_int32, [_P, C.c_int32]),
+    "pp_get_profile": (C.c_int32, [_P, C.POINTER(pp_kernel_class), C.c_int32, C.POINTER(C.c_int32)]),
     "pp_gemm": (C.c_int32, [C.c_int32, C.c_int32, C.c_int64, C.c_int64, C.c_int64, _P, C.c_int64, _P, C.c_int64,
                             _P, C.c_int64, _P]),
     "pp_getrf_batched": (C.c_int32, [C.c_int32, C.c_int32, C.c_int64, C.c_int64, _P, _P]),

@@ -87,6 +87,15 @@ class B200SLU:
         check(lib().pp_assemble(self._h, self.s.id, self._dt, i64ptr(cp), i64ptr(rv), vptr(nz), 0), self._h)
         return self
 
+    def update_values(self, nzval):
+        """New weights (host numpy array or CUDA tensor, in the order of the last assemble) for the same
+        pattern, re-assembled on the device; then factor() refactorizes."""
+        where = PP_DEVICE if hasattr(nzval, "data_ptr") else PP_HOST
+        if where == PP_HOST:
+            nzval = np.ascontiguousarray(nzval, dtype=self.dtype)
+        check(lib().pp_update_values(self._h, vptr(nzval), where), self._h)
+        return self
+
     def set_values(self, LD, LL, UD, UL, Nval):
         c = lambda a: np.ascontiguousarray(a, dtype=self.dtype)
         LD, LL, UD, UL, Nval = (c(a) for a in (LD, LL, UD, UL, Nval))
@@ -111,6 +120,24 @@ class B200SLU:
         st = pp_stats()
         check(lib().pp_get_stats(self._h, C.byref(st)), self._h)
         return {k: getattr(st, k) for k, _ in pp_stats._fields_}
+
+    def set_profile(self, on=True):
+        """Time every launch of this handle per kernel class (CUDA events on its stream); resets the totals."""
+        check(lib().pp_set_profile(self._h, 1 if on else 0), self._h)
+
+    def profile(self):
+        """{class: {launches, ms, bytes, pairs}} accumulated since set_profile."""
+        from ._lib import pp_kernel_class
+
+        arr = (pp_kernel_class * 16)()
+        cnt = C.c_int32()
+        check(lib().pp_get_profile(self._h, arr, 16, C.byref(cnt)), self._h)
+        return {arr[i].name.decode(): {"launches": arr[i].launches, "ms": arr[i].ms, "bytes": arr[i].bytes,
+                                       "pairs": arr[i].pairs} for i in range(cnt.value)}
+
+    def stream(self):
+        """The handle's CUDA stream (cudaStream_t as an integer)."""
+        return lib().pp_stream(self._h)
 
     def sync(self):
         check(lib().pp_sync(self._h), self._h)

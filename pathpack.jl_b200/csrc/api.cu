@@ -47,7 +47,9 @@ const Ops *get_ops(int sr, int dt) {
 namespace pp {
 const char *const KCLASS_NAMES[K_NCLASS] = {"front_small_kernel", "large_front_aux", "panel_kernel",
                                             "gemm_kernel(trailing)", "sweep_kernel(forward)",
-                                            "sweep_kernel(backward)", "coupling", "permute", "assemble_kernel"};
+                                            "sweep_kernel(backward)", "coupling", "permute", "assemble_kernel",
+                                            "factor_bottom_kernel", "sweep_bottom_kernel(fwd)",
+                                            "sweep_bottom_kernel(bwd)"};
 }
 
 using namespace pp;
@@ -90,7 +92,9 @@ struct pp_handle {
     std::vector<int> invp;
     // device structure
     DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
-        d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_ffronts, d_sfronts, d_sverts;
+        d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_ffronts, d_sfronts, d_sverts, d_pnt, d_fbottom,
+        d_fpending0, d_spending0, d_sdone0, d_sync;
+    std::vector<int> pnt, height;
     // values and work
     DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val;
     int64_t nD = 0, nL = 0;
@@ -98,6 +102,9 @@ struct pp_handle {
     size_t ws_esize = 0;
     pp_stats st{};
     Profiler prof;
+    std::vector<cudaStream_t> aux;
+    std::vector<cudaEvent_t> auxev;
+    int sm_count = 148;
 };
 
 static int32_t fail(pp_handle *h, int32_t code, const char *fmt, ...) {
@@ -161,6 +168,16 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev1);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->hp.levev, cudaEventDisableTiming);
+    for (int i = 0; i < 4 && e == cudaSuccess; i++) {
+        cudaStream_t s = nullptr;
+        cudaEvent_t ev = nullptr;
+        e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        if (s) h->aux.push_back(s);
+        if (ev) h->auxev.push_back(ev);
+    }
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) {
         pp_destroy(h);
         return cuda_fail(nullptr, e, "pp_create");
@@ -176,6 +193,12 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
+    for (cudaStream_t s : h->aux) {
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+    }
+    for (cudaEvent_t e : h->auxev) cudaEventDestroy(e);
+    if (h->hp.levev) cudaEventDestroy(h->hp.levev);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;  // DevBuf destructors free the device memory
     return PP_OK;
@@ -335,19 +358,54 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                     const int a = comp_of_vertex[ntgt[p]];
                     lstage[a] = std::max(lstage[a], lstage[c] + 1);
                 }
+        // bottom of the tree for the persistent sweeps: nn <= SWEEP_NNW in the whole subtree
+        std::vector<char> sbot(nf, 0), allbot(nf, 1);
+        for (int64_t f = 0; f < nf; f++) {
+            sbot[f] = (hp.nn[f] <= SWEEP_NNW) && allbot[f];
+            if (!sbot[f] && pnt[f] >= 0) allbot[pnt[f]] = 0;
+        }
+        std::vector<int> spending0(nf, 0), sdone0(nf, 1);
+        for (int64_t f = 0; f < nf; f++) {
+            if (sbot[f]) sdone0[f] = 0;
+            if (sbot[f] && pnt[f] >= 0) spending0[pnt[f]]++;
+        }
         auto build_stages = [&](const std::vector<int> &stage_of, std::vector<Stage> &out, std::vector<int> &sfronts,
-                                std::vector<int> &sverts) {
+                                std::vector<int> &sverts, std::vector<std::pair<int64_t, int>> &bfwd,
+                                std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost) {
             int ns = 0;
             for (int64_t c = 0; c < nB; c++) ns = std::max(ns, stage_of[c] + 1);
             if (nB == 0) ns = 0;
             std::vector<std::vector<int>> comps(ns);
             for (int64_t c = 0; c < nB; c++) comps[stage_of[c]].push_back((int)c);
             out.clear();
+            bfwd.clear();
+            bbwd.clear();
+            bcost.clear();
             for (int s = 0; s < ns; s++) {
                 Stage sg;
-                std::vector<std::vector<int>> byh(maxh + 1);
+                std::vector<std::vector<int>> byh(maxh + 1), bot(maxh + 1);
                 for (int c : comps[s])
-                    for (int64_t f = Fp[c]; f < Fp[c + 1]; f++) byh[height[f]].push_back((int)f);
+                    for (int64_t f = Fp[c]; f < Fp[c + 1]; f++) (sbot[f] ? bot : byh)[height[f]].push_back((int)f);
+                SLevel bc;
+                std::pair<int64_t, int> fw{(int64_t)sfronts.size(), 0};
+                for (int hh = 0; hh <= maxh; hh++)
+                    for (int f : bot[hh]) {
+                        sfronts.push_back(f);
+                        const double nn = hp.nn[f], na = hp.na[f];
+                        bc.count++;
+                        bc.res_rows += nn;
+                        bc.sep_rows += na;
+                        bc.blk_elems += nn * nn + nn * na;
+                        bc.pairs_col += nn * (nn - 1) / 2 + nn * na;
+                    }
+                fw.second = (int)(sfronts.size() - fw.first);
+                std::pair<int64_t, int> bw{(int64_t)sfronts.size(), 0};
+                for (int hh = maxh; hh >= 0; hh--)
+                    for (int f : bot[hh]) sfronts.push_back(f);
+                bw.second = (int)(sfronts.size() - bw.first);
+                bfwd.push_back(fw);
+                bbwd.push_back(bw);
+                bcost.push_back(bc);
                 for (int hh = 0; hh <= maxh; hh++) {
                     if (byh[hh].empty()) continue;
                     SLevel lv;
@@ -373,9 +431,9 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
             }
         };
         std::vector<int> sfronts, sverts;
-        build_stages(lstage, hp.lstages, sfronts, sverts);
+        build_stages(lstage, hp.lstages, sfronts, sverts, hp.sb_fwd, hp.sb_bwd, hp.sb_cost_l);
         // rmul stages: the gather concerns the stage's own columns j (rows of earlier components feed them)
-        build_stages(rstage, hp.rstages, sfronts, sverts);
+        build_stages(rstage, hp.rstages, sfronts, sverts, hp.sb_fwd_r, hp.sb_bwd_r, hp.sb_cost_r);
         (void)ccoupled;
         // factorization levels (classified per element size in prepare_workspace)
         hp.flevels.assign(maxh + 1, Level());
@@ -401,6 +459,10 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         CK(h, upload(h->d_fcc, fcc, st), "upload");
         CK(h, upload(h->d_sfronts, sfronts, st), "upload");
         CK(h, upload(h->d_sverts, sverts, st), "upload");
+        CK(h, upload(h->d_pnt, pnt, st), "upload");
+        CK(h, upload(h->d_spending0, spending0, st), "upload");
+        CK(h, upload(h->d_sdone0, sdone0, st), "upload");
+        CK(h, h->d_sync.ensure(sizeof(int) * (nf + 16)), "upload");
         CK(h, cudaStreamSynchronize(st), "upload");
         DevPlan &d = hp.dev;
         d.n = (int)n;
@@ -423,13 +485,23 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         d.idx = h->d_idx.as<int>();
         d.bptr = h->d_bptr.as<int>();
         d.fcc = h->d_fcc.as<int>();
+        d.pnt = h->d_pnt.as<int>();
         d.mptr = nullptr;
         d.mld = nullptr;
         d.fws = nullptr;
         hp.d_sfronts = h->d_sfronts.as<int>();
         hp.d_sverts = h->d_sverts.as<int>();
         hp.d_rel = h->d_rel.as<int>();
+        hp.d_spending0 = h->d_spending0.as<int>();
+        hp.d_sdone0 = h->d_sdone0.as<int>();
+        hp.d_sync = h->d_sync.as<int>();
+        hp.aux = h->aux;
+        hp.auxev = h->auxev;
+        hp.levev = h->hp.levev;
+        hp.sm_count = h->sm_count;
         h->invp = invp;
+        h->pnt = pnt;
+        h->height = height;
         // factorization heights, kept for prepare_workspace
         h->hp = std::move(hp);
         h->hp.mld.clear();
@@ -519,13 +591,46 @@ static int32_t prepare_workspace(pp_handle *h) {
         off = (off + 3) & ~(int64_t)3;  // 16-byte alignment of every block
     }
     hp.ws_elems = off;
-    // size classes per level
+    // bottom of the tree for the persistent factorization: nn + na within 32 KB of shared memory, whole subtree
+    int fb_limit = 1;
+    while ((size_t)(fb_limit + 1) * (fb_limit + 1) * h->ops->esize <= 32 * 1024) fb_limit++;
+    std::vector<char> fbot(nf, 0), allbot(nf, 1);
+    for (int f = 0; f < nf; f++) {
+        fbot[f] = (hp.nn[f] + hp.na[f] <= fb_limit) && allbot[f];
+        if (!fbot[f] && h->pnt[f] >= 0) allbot[h->pnt[f]] = 0;
+    }
+    {
+        const int maxh = (int)hp.flevels.size() - 1;
+        std::vector<std::vector<int>> byh(maxh + 1);
+        std::vector<int> pending0(nf, 0);
+        FrontGroup acc;
+        hp.fb_maxnj = 0;
+        for (int f = 0; f < nf; f++)
+            if (fbot[f]) {
+                byh[h->height[f]].push_back(f);
+                if (h->pnt[f] >= 0) pending0[h->pnt[f]]++;
+                hp.fb_maxnj = std::max(hp.fb_maxnj, hp.nn[f] + hp.na[f]);
+                front_cost(hp, f, acc);
+            }
+        std::vector<int> wl;
+        for (int hh = 0; hh <= maxh; hh++) wl.insert(wl.end(), byh[hh].begin(), byh[hh].end());
+        hp.fb_count = (int)wl.size();
+        hp.fb_bytes = acc.bytes;
+        hp.fb_pairs = acc.pairs;
+        CK(h, upload(h->d_fbottom, wl, h->stream), "upload");
+        CK(h, upload(h->d_fpending0, pending0, h->stream), "upload");
+        hp.d_fbottom = h->d_fbottom.as<int>();
+        hp.d_fpending0 = h->d_fpending0.as<int>();
+    }
+    // the remaining fronts by level, in size classes
     std::vector<int> fronts;
     const int classes[5] = {16, 32, 64, 128, limit};
-    for (Level &L : hp.flevels) {
-        std::vector<int> ids;
-        for (const FrontGroup &g : L.groups)
-            for (int t = 0; t < g.count; t++) ids.push_back(hp.h_ffronts[g.off + t]);
+    std::vector<std::vector<int>> top_by_h(hp.flevels.size());
+    for (int f = 0; f < nf; f++)
+        if (!fbot[f]) top_by_h[h->height[f]].push_back(f);
+    for (size_t hh = 0; hh < hp.flevels.size(); hh++) {
+        Level &L = hp.flevels[hh];
+        const std::vector<int> &ids = top_by_h[hh];
         std::vector<FrontGroup> groups;
         int lo = 0;
         for (int c = 0; c < 5; c++) {

@@ -100,12 +100,18 @@ __device__ __forceinline__ void store_entry(T v, int i, int j, int nn, int na, i
     }
 }
 
-template <int SR, typename T>
-__global__ void front_small_kernel(const int *__restrict__ fronts, DevPlan P, T *LD, T *LL, T *UD, T *UL, T *W) {
+// Load through L2 only (ld.global.cg): data another CTA wrote during the same kernel must not come from a
+// stale L1 line.
+template <typename T>
+__device__ __forceinline__ T ld_cg(const T *p) {
+    return __ldcg(p);
+}
+
+// One front in shared memory (F: nj x nj, leading dimension nj), executed by the whole CTA.  COHERENT reads
+// the children's update matrices through L2 (they may have been written by other CTAs of the same kernel).
+template <int SR, typename T, bool COHERENT>
+__device__ __forceinline__ void front_body(int f, const DevPlan &P, T *F, T *LD, T *LL, T *UD, T *UL, T *W) {
     using S = Sem<SR, T>;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    T *F = reinterpret_cast<T *>(smem_raw);
-    const int f = fronts[blockIdx.x];
     const int nn = P.nn[f], na = P.na[f], nj = nn + na, ld = nj;
     const int tid = threadIdx.x, bd = blockDim.x;
     const int nj2 = nj * nj;
@@ -121,7 +127,8 @@ __global__ void front_small_kernel(const int *__restrict__ fronts, DevPlan P, T 
         for (int e = tid; e < nac * nac; e += bd) {
             const int v = e % nac, w = e / nac;
             const int o = rel[v] + rel[w] * ld;
-            F[o] = S::add(F[o], M[v + (int64_t)w * mld]);
+            const T m = COHERENT ? ld_cg(M + v + (int64_t)w * mld) : M[v + (int64_t)w * mld];
+            F[o] = S::add(F[o], m);
         }
         __syncthreads();
     }
@@ -141,6 +148,12 @@ __global__ void front_small_kernel(const int *__restrict__ fronts, DevPlan P, T 
         else
             Mf[(i - nn) + (int64_t)(j - nn) * na] = v;
     }
+}
+
+template <int SR, typename T>
+__global__ void front_small_kernel(const int *__restrict__ fronts, DevPlan P, T *LD, T *LL, T *UD, T *UL, T *W) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    front_body<SR, T, false>(fronts[blockIdx.x], P, reinterpret_cast<T *>(smem_raw), LD, LL, UD, UL, W);
 }
 
 // dense blocks: in-place LU of the star of count independent n x n blocks (sgetrf! per block)

@@ -1,11 +1,18 @@
 // engine_host.cuh — host drivers of the device kernels, templated on the semiring; instantiated once per
 // (semiring, element type) in ops_*.cu.
+//
+// Factorization: one persistent launch for the bottom of the tree (factor_bottom_kernel), then the remaining
+// levels bottom-up: a front_small_kernel launch per size class, and the large fronts of the level on
+// concurrent streams (diag_lu_kernel, panel_solve_kernel and the trailing GEMM per 64-pivot block).
+// Solves: per coupling stage, the bottom fronts in one persistent launch per direction and the rest level by
+// level with sweep_kernel.
 #pragma once
 
 #include <algorithm>
 
-#include "engine.cuh"
 #include "ops.h"
+#include "persist.cuh"
+#include "sweep_tiled.cuh"
 
 namespace pp {
 
@@ -51,19 +58,55 @@ struct Engine {
 
     static int threads_for(int nj) { return nj <= 16 ? 64 : (nj <= 32 ? 128 : 256); }
 
-    static cudaError_t factor(const HostPlan &hp, const Values &v, cudaStream_t st, int64_t *launches) {
-        T *LD = static_cast<T *>(v.LD), *LL = static_cast<T *>(v.LL), *UD = static_cast<T *>(v.UD),
-          *UL = static_cast<T *>(v.UL), *W = static_cast<T *>(v.W);
-        int64_t nl = 0;
+    static cudaError_t set_attrs() {
         int dev = 0;
         cudaGetDevice(&dev);
         static bool attr[64] = {};
         if (dev < 64 && !attr[dev]) {
             PP_TRY(cudaFuncSetAttribute(front_small_kernel<SR, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)SMALL_FRONT_SMEM));
+            PP_TRY(cudaFuncSetAttribute(factor_bottom_kernel<SR, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)SMALL_FRONT_SMEM));
             attr[dev] = true;
         }
+        return cudaSuccess;
+    }
+
+    // the error word of a persistent launch: a bounded wait expired
+    static cudaError_t check_err(const HostPlan &hp, cudaStream_t st) {
+        int err = 0;
+        PP_TRY(cudaMemcpyAsync(&err, hp.d_sync + hp.nf + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
+        PP_TRY(cudaStreamSynchronize(st));
+        return err ? cudaErrorLaunchTimeout : cudaSuccess;
+    }
+
+    static cudaError_t reset_sync(const HostPlan &hp, const int *init, cudaStream_t st) {
+        PP_TRY(cudaMemcpyAsync(hp.d_sync, init, sizeof(int) * hp.nf, cudaMemcpyDeviceToDevice, st));
+        return cudaMemsetAsync(hp.d_sync + hp.nf, 0, 2 * sizeof(int), st);
+    }
+
+    static cudaError_t factor(const HostPlan &hp, const Values &v, cudaStream_t st, int64_t *launches) {
+        T *LD = static_cast<T *>(v.LD), *LL = static_cast<T *>(v.LL), *UD = static_cast<T *>(v.UD),
+          *UL = static_cast<T *>(v.UL), *W = static_cast<T *>(v.W);
+        int64_t nl = 0;
+        PP_TRY(set_attrs());
+        if (hp.fb_count > 0) {
+            PP_TRY(reset_sync(hp, hp.d_fpending0, st));
+            const size_t smem = (size_t)hp.fb_maxnj * hp.fb_maxnj * sizeof(T);
+            int per_sm = 1;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, factor_bottom_kernel<SR, T>, 128, smem);
+            const int grid = std::max(1, std::min(hp.fb_count, std::max(per_sm, 1) * hp.sm_count));
+            const int pi = hp.prof ? hp.prof->begin(K_FRONT_BOTTOM, st) : -1;
+            factor_bottom_kernel<SR, T><<<grid, 128, smem, st>>>(hp.d_fbottom, hp.fb_count, hp.dev, LD, LL, UD, UL, W,
+                                                                 hp.d_sync, hp.d_sync + hp.nf, hp.d_sync + hp.nf + 1);
+            PP_TRY(cudaGetLastError());
+            if (pi >= 0) hp.prof->end(pi, st, hp.fb_bytes, hp.fb_pairs);
+            nl++;
+            PP_TRY(check_err(hp, st));
+        }
+        const int naux = (int)hp.aux.size();
         for (const Level &L : hp.flevels) {
+            int nlarge = 0;
             for (const FrontGroup &g : L.groups) {
                 if (!g.large) {
                     const size_t smem = (size_t)g.max_nj * g.max_nj * sizeof(T);
@@ -75,10 +118,21 @@ struct Engine {
                     nl++;
                     continue;
                 }
-                // large fronts one at a time (their ids are on the host in the same order)
+                // the large fronts of the level are independent: spread them over the auxiliary streams
+                if (naux > 0) PP_TRY(cudaEventRecord(hp.levev, st));
                 for (int t = 0; t < g.count; t++) {
-                    PP_TRY(factor_large(hp, hp.h_ffronts[g.off + t], LD, LL, UD, UL, W, st, &nl));
+                    cudaStream_t s = st;
+                    if (naux > 0) {
+                        s = hp.aux[t % naux];
+                        if (t < naux) PP_TRY(cudaStreamWaitEvent(s, hp.levev, 0));
+                    }
+                    PP_TRY(factor_large(hp, hp.h_ffronts[g.off + t], LD, LL, UD, UL, W, s, &nl));
                 }
+                nlarge = g.count;
+            }
+            for (int j = 0; j < std::min(nlarge, naux); j++) {
+                PP_TRY(cudaEventRecord(hp.auxev[j], hp.aux[j]));
+                PP_TRY(cudaStreamWaitEvent(st, hp.auxev[j], 0));
             }
         }
         if (launches) *launches += nl;
@@ -112,14 +166,19 @@ struct Engine {
         for (int k = 0; k < nn; k += PANEL_NB) {
             const int b = std::min(PANEL_NB, nn - k);
             const int rem = nj - k - b;
-            const int nca = (rem + PANEL_THREADS - 1) / PANEL_THREADS;
             pi = pr ? pr->begin(K_PANEL, st) : -1;
-            panel_kernel<SR, T><<<1 + 2 * nca, PANEL_THREADS, 0, st>>>(F, nj, nj, k, b, nca);
+            diag_lu_kernel<SR, T><<<1, 256, 0, st>>>(F, nj, k, b);
             PP_TRY(cudaGetLastError());
+            (*nl)++;
+            if (rem > 0) {
+                const int nrow = (rem + 7) / 8;
+                panel_solve_kernel<SR, T><<<2 * nrow, 256, 0, st>>>(F, nj, nj, k, b, nrow);
+                PP_TRY(cudaGetLastError());
+                (*nl)++;
+            }
             if (pi >= 0)
                 pr->end(pi, st, 2.0 * b * b + 4.0 * rem * b,
                         (double)(b - 1) * b * (2.0 * b - 1) / 6 + (double)rem * b * (b - 1));
-            (*nl)++;
             if (rem > 0) {
                 T *C = F + (k + b) + (int64_t)(k + b) * nj;
                 const T *A = F + (k + b) + (int64_t)k * nj;
@@ -142,15 +201,24 @@ struct Engine {
     template <bool FWD, bool TRANS>
     static cudaError_t sweep_levels(const HostPlan &hp, const Stage &sg, bool ascending, const T *Dv, const T *Ov,
                                     T *X, int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
-        const int ny = (k + 31) / 32;
+        const int ny = (k + ST_CT - 1) / ST_CT;
         const int nlev = (int)sg.levels.size();
+        constexpr size_t smem = sweep_tiled_smem<T>();
+        int dev = 0;
+        cudaGetDevice(&dev);
+        static bool attr[64] = {};
+        if (dev < 64 && !attr[dev]) {
+            PP_TRY(cudaFuncSetAttribute(sweep_tiled_kernel<SR, T, FWD, TRANS>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attr[dev] = true;
+        }
         for (int t = 0; t < nlev; t++) {
             const SLevel &lv = sg.levels[ascending ? t : nlev - 1 - t];
             if (lv.count == 0) continue;
             dim3 grid((unsigned)lv.count, (unsigned)ny);
             const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD : K_SWEEP_BWD, st) : -1;
-            sweep_kernel<SR, T, FWD, TRANS><<<grid, 256, 0, st>>>(hp.d_sfronts + lv.off, hp.dev, Dv, Ov, X, ldx, k,
-                                                                 unit);
+            sweep_tiled_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_sfronts + lv.off, hp.dev, Dv, Ov, X,
+                                                                          ldx, k, unit);
             PP_TRY(cudaGetLastError());
             if (pi >= 0)
                 hp.prof->end(pi, st, (double)k * (2.0 * lv.res_rows + (FWD ? 2.0 : 1.0) * lv.sep_rows) + lv.blk_elems,
@@ -158,6 +226,27 @@ struct Engine {
             (*nl)++;
         }
         return cudaSuccess;
+    }
+
+    template <bool FWD, bool TRANS>
+    static cudaError_t sweep_bottom(const HostPlan &hp, const std::pair<int64_t, int> &wl, const SLevel &cost,
+                                    const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
+                                    int64_t *nl) {
+        if (wl.second == 0) return cudaSuccess;
+        PP_TRY(reset_sync(hp, FWD ? hp.d_spending0 : hp.d_sdone0, st));
+        int per_sm = 1;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_bottom_kernel<SR, T, FWD, TRANS>, 256, 0);
+        const int grid = std::max(1, std::min(wl.second, std::max(per_sm, 1) * hp.sm_count));
+        const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_BOTTOM : K_SWEEP_BWD_BOTTOM, st) : -1;
+        sweep_bottom_kernel<SR, T, FWD, TRANS><<<grid, 256, 0, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev, Dv,
+                                                                     Ov, X, ldx, k, unit, hp.d_sync,
+                                                                     hp.d_sync + hp.nf, hp.d_sync + hp.nf + 1);
+        PP_TRY(cudaGetLastError());
+        if (pi >= 0)
+            hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
+                         (double)k * cost.pairs_col);
+        (*nl)++;
+        return check_err(hp, st);
     }
 
     // left: lmul! (X <- A* X: per stage L* forward, U* backward, then the coupling scatter);
@@ -171,9 +260,12 @@ struct Engine {
         T *X = static_cast<T *>(Xv);
         int64_t nl = 0;
         if (left) {
-            for (const Stage &sg : hp.lstages) {
+            for (size_t s = 0; s < hp.lstages.size(); s++) {
+                const Stage &sg = hp.lstages[s];
+                PP_TRY((sweep_bottom<true, false>(hp, hp.sb_fwd[s], hp.sb_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_levels<true, false>(hp, sg, true, LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_levels<false, false>(hp, sg, false, UD, UL, X, ldx, k, 0, st, &nl)));
+                PP_TRY((sweep_bottom<false, false>(hp, hp.sb_bwd[s], hp.sb_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 if (sg.coupled && sg.nverts > 0) {
                     const int pi = hp.prof ? hp.prof->begin(K_COUPLING, st) : -1;
                     coupling_scatter_kernel<SR, T><<<(sg.nverts + 7) / 8, 256, 0, st>>>(
@@ -184,7 +276,8 @@ struct Engine {
                 }
             }
         } else {
-            for (const Stage &sg : hp.rstages) {
+            for (size_t s = 0; s < hp.rstages.size(); s++) {
+                const Stage &sg = hp.rstages[s];
                 if (sg.coupled && sg.nverts > 0) {
                     const int pi = hp.prof ? hp.prof->begin(K_COUPLING, st) : -1;
                     coupling_gather_kernel<SR, T><<<(sg.nverts + 7) / 8, 256, 0, st>>>(
@@ -193,8 +286,10 @@ struct Engine {
                     if (pi >= 0) hp.prof->end(pi, st, 0, 0);
                     nl++;
                 }
+                PP_TRY((sweep_bottom<true, true>(hp, hp.sb_fwd_r[s], hp.sb_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_levels<true, true>(hp, sg, true, UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_levels<false, true>(hp, sg, false, LD, LL, X, ldx, k, 1, st, &nl)));
+                PP_TRY((sweep_bottom<false, true>(hp, hp.sb_bwd_r[s], hp.sb_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
             }
         }
         if (launches) *launches += nl;

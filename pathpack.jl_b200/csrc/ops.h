@@ -12,7 +12,7 @@ namespace pp {
 
 // Kernel classes the profiler separates.
 enum KClass { K_FRONT = 0, K_LARGE_AUX, K_PANEL, K_GEMM, K_SWEEP_FWD, K_SWEEP_BWD, K_COUPLING, K_PERMUTE, K_ASSEMBLE,
-              K_NCLASS };
+              K_FRONT_BOTTOM, K_SWEEP_FWD_BOTTOM, K_SWEEP_BWD_BOTTOM, K_NCLASS };
 extern const char *const KCLASS_NAMES[K_NCLASS];
 
 // Optional per-launch timing with CUDA events on the launching stream; off unless pp_set_profile enabled it.
@@ -103,6 +103,24 @@ struct HostPlan {
     const int *d_rel = nullptr;
     DevPlan dev{};
     Profiler *prof = nullptr;
+    // bottom of the tree for the persistent kernels: factorization (fronts with nn + na <= the bottom limit
+    // whose whole subtree is such) and solves (nn <= SWEEP_NNW, whole subtree)
+    int fb_count = 0, fb_maxnj = 0;
+    double fb_bytes = 0, fb_pairs = 0;
+    const int *d_fbottom = nullptr;    // work list, height ascending
+    const int *d_fpending0 = nullptr;  // children per front (counter template)
+    // per stage: bottom work lists of the solves in d_sfronts (forward ascending, backward descending)
+    std::vector<std::pair<int64_t, int>> sb_fwd, sb_bwd;  // indexed like lstages / rstages: [stage] -> (off, count)
+    std::vector<std::pair<int64_t, int>> sb_fwd_r, sb_bwd_r;
+    std::vector<SLevel> sb_cost_l, sb_cost_r;  // per stage: sums over the bottom fronts (profiler)
+    const int *d_spending0 = nullptr;  // bottom children per front (forward counters)
+    const int *d_sdone0 = nullptr;     // 1 for fronts outside the bottom, 0 inside (backward flags)
+    int *d_sync = nullptr;             // scratch: [0, nf) counters / flags, nf: next, nf + 1: error
+    // concurrency for the large fronts of one level
+    std::vector<cudaStream_t> aux;
+    std::vector<cudaEvent_t> auxev;
+    cudaEvent_t levev = nullptr;
+    int sm_count = 148;
 };
 
 struct Values {

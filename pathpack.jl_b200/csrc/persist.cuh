@@ -1,0 +1,257 @@
+// persist.cuh — dependency-driven kernels for the bottom of the elimination tree, and the panel kernels of
+// the large-front LU.
+//
+// The bottom of the tree (the fronts whose whole subtree is small) is processed by ONE persistent launch per
+// sweep instead of one launch per tree level: CTAs take fronts from a work list ordered by height (children
+// before parents, so every front a CTA waits for was taken earlier by a running CTA and the lowest unfinished
+// front can always proceed), wait for a per-front counter, process the front and signal its parent.  The
+// reference level-schedules the same work (ext/PATHPACKCUDAExt/chordal/sgetrf.jl:324-343, batched/sweep.jl:9-21)
+// with a launch per level.
+//
+// Every wait is bounded: after WAIT_LIMIT polls the kernel records the failure in *err and returns, and the
+// host reports PP_ETIMEOUT.  Data written by other CTAs during the same launch is read through L2
+// (ld.global.cg) and published with __threadfence() before the counter update.
+#pragma once
+
+#include "engine.cuh"
+
+namespace pp {
+
+constexpr long long WAIT_LIMIT = 20000000;  // polls of ~100 ns each: about two seconds
+
+// thread 0 of the CTA polls *p until it satisfies the predicate (or the limit expires); broadcast result
+__device__ __forceinline__ bool cta_wait(const int *p, bool for_zero, int *err) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        long long it = 0;
+        int ok = 1;
+        while (true) {
+            const int v = *(volatile const int *)p;
+            if (for_zero ? (v == 0) : (v != 0)) break;
+            if (*(volatile const int *)err) {
+                ok = 0;
+                break;
+            }
+            if (++it > WAIT_LIMIT) {
+                atomicExch(err, 1);
+                ok = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+__device__ __forceinline__ int cta_take(int *next) {
+    __shared__ int s_task;
+    if (threadIdx.x == 0) s_task = atomicAdd(next, 1);
+    __syncthreads();
+    const int t = s_task;
+    __syncthreads();
+    return t;
+}
+
+// ---------------------------------------------------------------- factorization of the bottom fronts
+
+template <int SR, typename T>
+__global__ void __launch_bounds__(128) factor_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P, T *LD,
+                                                            T *LL, T *UD, T *UL, T *W, int *pending, int *next,
+                                                            int *err) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T *F = reinterpret_cast<T *>(smem_raw);
+    while (true) {
+        const int t = cta_take(next);
+        if (t >= count) return;
+        const int f = wl[t];
+        if (!cta_wait(pending + f, true, err)) return;
+        front_body<SR, T, true>(f, P, F, LD, LL, UD, UL, W);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const int p = P.pnt[f];
+            if (p >= 0) atomicSub(pending + p, 1);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- sweeps of the bottom fronts
+//
+// A CTA per front, warp w handles the 32-column tiles w, w + 8, ...; lane = right-hand side.  The front's
+// residual (nn <= SWEEP_NNW) lives in registers, so the triangular solve needs no barrier.  Element reads of
+// the factor blocks are warp-uniform (broadcast).  FWD: wait for the children (counter), solve, (+)-scatter
+// to the separator with atomics, signal the parent.  Backward: wait for the parent's flag, gather from the
+// separator, solve, set the front's flag.  Same per-element dataflow as sweep_kernel.
+
+template <int SR, typename T, bool FWD, bool TRANS>
+__device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &P, const T *__restrict__ Dv,
+                                                const T *__restrict__ Ov, T *X, int64_t ldx, int k, int unit) {
+    using S = Sem<SR, T>;
+    constexpr int NW = SWEEP_NNW;
+    const int lane = threadIdx.x & 31;
+    const int col = tile * 32 + lane;
+    const bool ok = col < k;
+    const int rlo = P.rlo[f], nn = P.nn[f], na = P.na[f];
+    const T *D = Dv + P.dptr[f];
+    const T *O = Ov + P.lptr[f];
+    const int *sep = P.stgt + P.sptr[f];
+    T *Xc = X + (ok ? col : 0);
+    const T z = S::zero();
+    const bool scale = !unit && !S::integral;
+    auto Te = [&](int r, int c) -> T { return TRANS ? __ldg(D + c + (int64_t)r * nn) : __ldg(D + r + (int64_t)c * nn); };
+    T x[NW];
+#pragma unroll
+    for (int p = 0; p < NW; p++)
+        if (p < nn) x[p] = ok ? ld_cg(Xc + (int64_t)(rlo + p) * ldx) : z;
+    if (FWD) {
+#pragma unroll
+        for (int p = 0; p < NW; p++) {
+            if (p < nn) {
+                if (scale) x[p] = S::mul(x[p], S::star(Te(p, p)));
+#pragma unroll
+                for (int q = p + 1; q < NW; q++)
+                    if (q < nn) x[q] = S::muladd(Te(q, p), x[p], x[q]);
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < NW; p++)
+            if (p < nn && ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, x[p]);
+        for (int i = 0; i < na; i++) {
+            T a = z;
+#pragma unroll
+            for (int p = 0; p < NW; p++)
+                if (p < nn) {
+                    const T o = TRANS ? __ldg(O + p + (int64_t)i * nn) : __ldg(O + i + (int64_t)p * na);
+                    a = S::muladd(o, x[p], a);
+                }
+            if (ok) S::atomic_add(Xc + (int64_t)sep[i] * ldx, a);
+        }
+    } else {
+        for (int i = 0; i < na; i++) {
+            const T xi = ok ? ld_cg(Xc + (int64_t)sep[i] * ldx) : z;
+#pragma unroll
+            for (int p = 0; p < NW; p++)
+                if (p < nn) {
+                    const T o = TRANS ? __ldg(O + i + (int64_t)p * na) : __ldg(O + p + (int64_t)i * nn);
+                    x[p] = S::muladd(o, xi, x[p]);
+                }
+        }
+#pragma unroll
+        for (int pp = 0; pp < NW; pp++) {
+            const int p = NW - 1 - pp;
+            if (p < nn) {
+                if (scale) x[p] = S::mul(S::star(Te(p, p)), x[p]);
+#pragma unroll
+                for (int q = 0; q < NW; q++)
+                    if (q < p) x[q] = S::muladd(Te(q, p), x[p], x[q]);
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < NW; p++)
+            if (p < nn && ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, x[p]);
+    }
+}
+
+template <int SR, typename T, bool FWD, bool TRANS>
+__global__ void __launch_bounds__(256, 2) sweep_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P,
+                                                           const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
+                                                           int64_t ldx, int k, int unit, int *flags, int *next,
+                                                           int *err) {
+    const int ntiles = (k + 31) / 32;
+    const int w = threadIdx.x >> 5;
+    while (true) {
+        const int t = cta_take(next);
+        if (t >= count) return;
+        const int f = wl[t];
+        if (FWD) {
+            if (!cta_wait(flags + f, true, err)) return;
+        } else {
+            const int p = P.pnt[f];
+            if (p >= 0 && !cta_wait(flags + p, false, err)) return;
+        }
+        for (int tile = w; tile < ntiles; tile += 8) warp_front_tile<SR, T, FWD, TRANS>(f, tile, P, Dv, Ov, X, ldx, k, unit);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (FWD) {
+                const int p = P.pnt[f];
+                if (p >= 0) atomicSub(flags + p, 1);
+            } else {
+                atomicExch(flags + f, 1);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- panels of the large-front LU
+
+// LU of the b x b diagonal block at (k, k) of F in shared memory, written back (one CTA).
+template <int SR, typename T>
+__global__ void __launch_bounds__(256) diag_lu_kernel(T *__restrict__ F, int64_t ld, int k, int b) {
+    constexpr int NB = PANEL_NB;
+    __shared__ T D[NB * NB];
+    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
+        const int i = e % b, j = e / b;
+        D[i + j * NB] = F[(k + i) + (int64_t)(k + j) * ld];
+    }
+    __syncthreads();
+    lu_smem<SR, T>(D, NB, b, b);
+    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
+        const int i = e % b, j = e / b;
+        F[(k + i) + (int64_t)(k + j) * ld] = D[i + j * NB];
+    }
+}
+
+// The column panel (rows k+b .. nj-1 of columns k .. k+b-1: x <- x U*, strsx2! :R :U :N) and the row panel
+// (columns k+b .. nj-1 of rows k .. k+b-1: x <- L* x, strsx2! :L :L :U) against the factored diagonal block.
+// A warp per panel row (or column): lane l holds x[l] and x[l + 32]; pivot p's final value is broadcast by a
+// shuffle from its lane, and every lane updates its own later entries, so the pivot loop needs no barrier.
+// CTAs 0 .. nrow-1 take 8 rows each, the rest 8 columns each.
+template <int SR, typename T>
+__global__ void __launch_bounds__(256) panel_solve_kernel(T *__restrict__ F, int64_t ld, int nj, int k, int b,
+                                                          int nrow) {
+    using S = Sem<SR, T>;
+    constexpr int NB = PANEL_NB;
+    __shared__ T D[NB * NB];
+    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
+        const int i = e % b, j = e / b;
+        D[i + j * NB] = F[(k + i) + (int64_t)(k + j) * ld];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const bool rowp = (int)blockIdx.x < nrow;
+    const int idx = k + b + ((rowp ? blockIdx.x : blockIdx.x - nrow) * 8 + w);
+    if (idx >= nj) return;
+    const int q0 = lane, q1 = lane + 32;
+    T x0 = S::zero(), x1 = S::zero();
+    if (rowp) {
+        if (q0 < b) x0 = F[idx + (int64_t)(k + q0) * ld];
+        if (q1 < b) x1 = F[idx + (int64_t)(k + q1) * ld];
+        for (int p = 0; p < b; p++) {
+            T xp = __shfl_sync(0xffffffffu, p < 32 ? x0 : x1, p & 31);
+            if (!S::integral) xp = S::mul(xp, S::star(D[p + p * NB]));
+            if (p == q0) x0 = xp;
+            if (p == q1) x1 = xp;
+            if (q0 > p && q0 < b) x0 = S::muladd(xp, D[p + q0 * NB], x0);
+            if (q1 > p && q1 < b) x1 = S::muladd(xp, D[p + q1 * NB], x1);
+        }
+        if (q0 < b) F[idx + (int64_t)(k + q0) * ld] = x0;
+        if (q1 < b) F[idx + (int64_t)(k + q1) * ld] = x1;
+    } else {
+        T *col = F + (int64_t)idx * ld + k;
+        if (q0 < b) x0 = col[q0];
+        if (q1 < b) x1 = col[q1];
+        for (int p = 0; p < b; p++) {
+            const T xp = __shfl_sync(0xffffffffu, p < 32 ? x0 : x1, p & 31);
+            if (q0 > p && q0 < b) x0 = S::muladd(D[q0 + p * NB], xp, x0);
+            if (q1 > p && q1 < b) x1 = S::muladd(D[q1 + p * NB], xp, x1);
+        }
+        if (q0 < b) col[q0] = x0;
+        if (q1 < b) col[q1] = x1;
+    }
+}
+
+}  // namespace pp

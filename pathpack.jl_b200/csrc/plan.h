@@ -8,6 +8,9 @@
 
 namespace pp {
 
+// largest residual of a front in the register-resident warp sweep of the bottom of the tree
+constexpr int SWEEP_NNW = 16;
+
 // Device arrays of a structure (0-based, positions = permuted labels).  Per front f: the residual is
 // rlo[f] .. rlo[f]+nn[f]-1, the separator stgt[sptr[f] .. sptr[f+1]-1] with rel[] its positions in the
 // parent's bag, the blocks of the factor arrays start at dptr[f] (nn x nn) and lptr[f] (nn x na / na x nn),
@@ -25,6 +28,7 @@ struct DevPlan {
     const int64_t *nptr;
     const int *ntgt;
     const int *perm, *invp, *idx, *bptr, *fcc;
+    const int *pnt;  // parent front, -1 for a root
 };
 
 // A group of fronts launched together: one size class of one tree level.

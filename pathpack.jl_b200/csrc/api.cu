@@ -49,7 +49,8 @@ const char *const KCLASS_NAMES[K_NCLASS] = {"front_small_kernel", "large_front_a
                                             "gemm_kernel(trailing)", "sweep_kernel(forward)",
                                             "sweep_kernel(backward)", "coupling", "permute", "assemble_kernel",
                                             "factor_bottom_kernel", "sweep_bottom_kernel(fwd)",
-                                            "sweep_bottom_kernel(bwd)"};
+                                            "sweep_bottom_kernel(bwd)", "sweep_subtree_kernel(fwd)",
+                                            "sweep_subtree_kernel(bwd)"};
 }
 
 using namespace pp;
@@ -93,7 +94,7 @@ struct pp_handle {
     // device structure
     DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
         d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_ffronts, d_sfronts, d_sverts, d_pnt, d_fbottom,
-        d_fpending0, d_spending0, d_sdone0, d_sync;
+        d_fpending0, d_spending0, d_sdone0, d_sync, d_sroots, d_fdsc, d_slot;
     std::vector<int> pnt, height;
     // values and work
     DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val;
@@ -364,14 +365,54 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
             sbot[f] = (hp.nn[f] <= SWEEP_NNW) && allbot[f];
             if (!sbot[f] && pnt[f] >= 0) allbot[pnt[f]] = 0;
         }
+        // subtrees solved in shared memory: the whole subtree is in the bottom and its residual range plus the
+        // root's separator fit SUBTREE_ROWS rows; maximal such subtrees are disjoint
+        std::vector<int> fdsc(nf);
+        for (int64_t f = 0; f < nf; f++) fdsc[f] = (int)f;
+        for (int64_t f = 0; f < nf; f++)
+            if (pnt[f] >= 0) fdsc[pnt[f]] = std::min(fdsc[pnt[f]], fdsc[f]);
+        std::vector<char> qual(nf, 0), covered(nf, 0);
+        for (int64_t f = 0; f < nf; f++)
+            qual[f] = sbot[f] && (R[f + 1] - R[fdsc[f]] + hp.na[f] <= SUBTREE_ROWS);
+        std::vector<int> sroot_of(nf, -1);
+        for (int64_t f = nf - 1; f >= 0; f--) {
+            if (!qual[f]) continue;
+            if (pnt[f] >= 0 && qual[pnt[f]]) {
+                sroot_of[f] = sroot_of[pnt[f]];
+            } else {
+                sroot_of[f] = (int)f;
+            }
+            covered[f] = 1;
+        }
+        std::vector<int> slot(std::max<int64_t>(nS, 1), 0);
+        for (int64_t f = 0; f < nf; f++) {
+            if (!covered[f]) continue;
+            const int r = sroot_of[f];
+            const int64_t rlo0 = R[fdsc[r]], rhi = R[r + 1] - 1, nres = rhi - rlo0 + 1;
+            for (int64_t q = Sp[f]; q < Sp[f + 1]; q++) {
+                const int v = stgt[q];
+                if (v <= rhi) {
+                    slot[q] = (int)(v - rlo0);
+                } else {
+                    const int *b0 = stgt.data() + Sp[r], *b1 = stgt.data() + Sp[r + 1];
+                    const int *it = std::lower_bound(b0, b1, v);
+                    if (it == b1 || *it != v)
+                        return fail(h, PP_EINVAL, "pp_set_structure: separator of front %lld leaves its subtree",
+                                    (long long)f);
+                    slot[q] = (int)(nres + (it - b0));
+                }
+            }
+        }
         std::vector<int> spending0(nf, 0), sdone0(nf, 1);
         for (int64_t f = 0; f < nf; f++) {
-            if (sbot[f]) sdone0[f] = 0;
-            if (sbot[f] && pnt[f] >= 0) spending0[pnt[f]]++;
+            const bool mid = sbot[f] && !covered[f];
+            if (mid) sdone0[f] = 0;
+            if (mid && pnt[f] >= 0) spending0[pnt[f]]++;
         }
         auto build_stages = [&](const std::vector<int> &stage_of, std::vector<Stage> &out, std::vector<int> &sfronts,
                                 std::vector<int> &sverts, std::vector<std::pair<int64_t, int>> &bfwd,
-                                std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost) {
+                                std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost,
+                                std::vector<SubtreeList> &subs, std::vector<int> &sroots) {
             int ns = 0;
             for (int64_t c = 0; c < nB; c++) ns = std::max(ns, stage_of[c] + 1);
             if (nB == 0) ns = 0;
@@ -381,11 +422,22 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
             bfwd.clear();
             bbwd.clear();
             bcost.clear();
+            subs.clear();
             for (int s = 0; s < ns; s++) {
                 Stage sg;
                 std::vector<std::vector<int>> byh(maxh + 1), bot(maxh + 1);
+                SubtreeList sl;
+                sl.off = (int64_t)sroots.size();
                 for (int c : comps[s])
-                    for (int64_t f = Fp[c]; f < Fp[c + 1]; f++) (sbot[f] ? bot : byh)[height[f]].push_back((int)f);
+                    for (int64_t f = Fp[c]; f < Fp[c + 1]; f++) {
+                        if (covered[f]) {
+                            if (sroot_of[f] == f) sroots.push_back((int)f);
+                            continue;
+                        }
+                        (sbot[f] ? bot : byh)[height[f]].push_back((int)f);
+                    }
+                sl.count = (int)(sroots.size() - sl.off);
+                subs.push_back(sl);
                 SLevel bc;
                 std::pair<int64_t, int> fw{(int64_t)sfronts.size(), 0};
                 for (int hh = 0; hh <= maxh; hh++)
@@ -430,10 +482,10 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 out.push_back(std::move(sg));
             }
         };
-        std::vector<int> sfronts, sverts;
-        build_stages(lstage, hp.lstages, sfronts, sverts, hp.sb_fwd, hp.sb_bwd, hp.sb_cost_l);
+        std::vector<int> sfronts, sverts, sroots;
+        build_stages(lstage, hp.lstages, sfronts, sverts, hp.sb_fwd, hp.sb_bwd, hp.sb_cost_l, hp.sub_l, sroots);
         // rmul stages: the gather concerns the stage's own columns j (rows of earlier components feed them)
-        build_stages(rstage, hp.rstages, sfronts, sverts, hp.sb_fwd_r, hp.sb_bwd_r, hp.sb_cost_r);
+        build_stages(rstage, hp.rstages, sfronts, sverts, hp.sb_fwd_r, hp.sb_bwd_r, hp.sb_cost_r, hp.sub_r, sroots);
         (void)ccoupled;
         // factorization levels (classified per element size in prepare_workspace)
         hp.flevels.assign(maxh + 1, Level());
@@ -460,9 +512,12 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         CK(h, upload(h->d_sfronts, sfronts, st), "upload");
         CK(h, upload(h->d_sverts, sverts, st), "upload");
         CK(h, upload(h->d_pnt, pnt, st), "upload");
+        CK(h, upload(h->d_sroots, sroots, st), "upload");
+        CK(h, upload(h->d_fdsc, fdsc, st), "upload");
+        CK(h, upload(h->d_slot, slot, st), "upload");
         CK(h, upload(h->d_spending0, spending0, st), "upload");
         CK(h, upload(h->d_sdone0, sdone0, st), "upload");
-        CK(h, h->d_sync.ensure(sizeof(int) * (nf + 16)), "upload");
+        CK(h, h->d_sync.ensure(sizeof(int) * (32 * nf + 16)), "upload");
         CK(h, cudaStreamSynchronize(st), "upload");
         DevPlan &d = hp.dev;
         d.n = (int)n;
@@ -493,8 +548,12 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         hp.d_sverts = h->d_sverts.as<int>();
         hp.d_rel = h->d_rel.as<int>();
         hp.d_spending0 = h->d_spending0.as<int>();
+        hp.d_sroots = h->d_sroots.as<int>();
+        hp.d_fdsc = h->d_fdsc.as<int>();
+        hp.d_slot = h->d_slot.as<int>();
         hp.d_sdone0 = h->d_sdone0.as<int>();
         hp.d_sync = h->d_sync.as<int>();
+        hp.sync_cap = 32 * nf + 16;
         hp.aux = h->aux;
         hp.auxev = h->auxev;
         hp.levev = h->hp.levev;
@@ -887,6 +946,19 @@ static double solve_pairs_per_rhs(const HostPlan &hp) {
     return s + (double)hp.nN;
 }
 
+// the per-(tile, front) counters of the persistent sweeps for k right-hand sides
+static int32_t ensure_sync(pp_handle *h, int64_t k) {
+    const int64_t need = ((k + 31) / 32) * (int64_t)h->hp.nf + 16;
+    if (need <= h->hp.sync_cap) return PP_OK;
+    if (need_memory(h, sizeof(int) * need, "sweep counters") != PP_OK) return PP_ENOMEM;
+    h->d_sync.release();
+    cudaError_t e = h->d_sync.ensure(sizeof(int) * need);
+    if (e != cudaSuccess) return cuda_fail(h, e, "sweep counters");
+    h->hp.d_sync = h->d_sync.as<int>();
+    h->hp.sync_cap = need;
+    return PP_OK;
+}
+
 // lmul! / rmul! on the device layout X[position][rhs]
 static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where, int left, const char *who) {
     if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
@@ -908,6 +980,7 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
     size_t need = (xbytes > h->X.bytes ? xbytes : 0) + (where == PP_HOST && bbytes > h->stage_in.bytes ? bbytes : 0);
     if (need_memory(h, need, who) != PP_OK) return PP_ENOMEM;
     CK(h, h->X.ensure(xbytes), who);
+    if (ensure_sync(h, k) != PP_OK) return PP_ENOMEM;
     cudaStream_t st = h->stream;
     void *Bd = B;
     int64_t ldbd = ldb;
@@ -988,6 +1061,7 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
         return PP_ENOMEM;
     CK(h, h->X.ensure(xbytes), who);
     if (sbytes) CK(h, h->stage_out.ensure(sbytes), who);
+    if (ensure_sync(h, pw) != PP_OK) return PP_ENOMEM;
     cudaStream_t st = h->stream;
     int64_t nl = 0;
     float total = 0;

@@ -75,14 +75,17 @@ struct Engine {
     // the error word of a persistent launch: a bounded wait expired
     static cudaError_t check_err(const HostPlan &hp, cudaStream_t st) {
         int err = 0;
-        PP_TRY(cudaMemcpyAsync(&err, hp.d_sync + hp.nf + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
+        PP_TRY(cudaMemcpyAsync(&err, hp.d_sync + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
         PP_TRY(cudaStreamSynchronize(st));
         return err ? cudaErrorLaunchTimeout : cudaSuccess;
     }
 
-    static cudaError_t reset_sync(const HostPlan &hp, const int *init, cudaStream_t st) {
-        PP_TRY(cudaMemcpyAsync(hp.d_sync, init, sizeof(int) * hp.nf, cudaMemcpyDeviceToDevice, st));
-        return cudaMemsetAsync(hp.d_sync + hp.nf, 0, 2 * sizeof(int), st);
+    // scratch layout: d_sync[0] task counter, d_sync[1] error word, d_sync + 16 the per-(tile, front) counters
+    static cudaError_t reset_sync(const HostPlan &hp, const int *init, int ntiles, cudaStream_t st) {
+        PP_TRY(cudaMemsetAsync(hp.d_sync, 0, 2 * sizeof(int), st));
+        if (ntiles == 1) return cudaMemcpyAsync(hp.d_sync + 16, init, sizeof(int) * hp.nf, cudaMemcpyDeviceToDevice, st);
+        init_flags_kernel<<<grid_for((int64_t)hp.nf * ntiles, 256), 256, 0, st>>>(hp.d_sync + 16, init, hp.nf, ntiles);
+        return cudaGetLastError();
     }
 
     static cudaError_t factor(const HostPlan &hp, const Values &v, cudaStream_t st, int64_t *launches) {
@@ -91,14 +94,14 @@ struct Engine {
         int64_t nl = 0;
         PP_TRY(set_attrs());
         if (hp.fb_count > 0) {
-            PP_TRY(reset_sync(hp, hp.d_fpending0, st));
+            PP_TRY(reset_sync(hp, hp.d_fpending0, 1, st));
             const size_t smem = (size_t)hp.fb_maxnj * hp.fb_maxnj * sizeof(T);
             int per_sm = 1;
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, factor_bottom_kernel<SR, T>, 128, smem);
             const int grid = std::max(1, std::min(hp.fb_count, std::max(per_sm, 1) * hp.sm_count));
             const int pi = hp.prof ? hp.prof->begin(K_FRONT_BOTTOM, st) : -1;
             factor_bottom_kernel<SR, T><<<grid, 128, smem, st>>>(hp.d_fbottom, hp.fb_count, hp.dev, LD, LL, UD, UL, W,
-                                                                 hp.d_sync, hp.d_sync + hp.nf, hp.d_sync + hp.nf + 1);
+                                                                 hp.d_sync + 16, hp.d_sync, hp.d_sync + 1);
             PP_TRY(cudaGetLastError());
             if (pi >= 0) hp.prof->end(pi, st, hp.fb_bytes, hp.fb_pairs);
             nl++;
@@ -233,20 +236,45 @@ struct Engine {
                                     const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
                                     int64_t *nl) {
         if (wl.second == 0) return cudaSuccess;
-        PP_TRY(reset_sync(hp, FWD ? hp.d_spending0 : hp.d_sdone0, st));
+        const int ntiles = (k + 31) / 32;
+        PP_TRY(reset_sync(hp, FWD ? hp.d_spending0 : hp.d_sdone0, ntiles, st));
         int per_sm = 1;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_bottom_kernel<SR, T, FWD, TRANS>, 256, 0);
-        const int grid = std::max(1, std::min(wl.second, std::max(per_sm, 1) * hp.sm_count));
+        const int64_t tasks = (int64_t)wl.second * ntiles;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((tasks + 7) / 8, std::max(per_sm, 1) * hp.sm_count));
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_BOTTOM : K_SWEEP_BWD_BOTTOM, st) : -1;
         sweep_bottom_kernel<SR, T, FWD, TRANS><<<grid, 256, 0, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev, Dv,
-                                                                     Ov, X, ldx, k, unit, hp.d_sync,
-                                                                     hp.d_sync + hp.nf, hp.d_sync + hp.nf + 1);
+                                                                     Ov, X, ldx, k, unit, hp.d_sync + 16,
+                                                                     hp.d_sync, hp.d_sync + 1);
         PP_TRY(cudaGetLastError());
         if (pi >= 0)
             hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
                          (double)k * cost.pairs_col);
         (*nl)++;
         return check_err(hp, st);
+    }
+
+    template <bool FWD, bool TRANS>
+    static cudaError_t sweep_subtrees(const HostPlan &hp, const SubtreeList &sl, const T *Dv, const T *Ov, T *X,
+                                      int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
+        if (sl.count == 0) return cudaSuccess;
+        constexpr size_t smem = sizeof(T) * 4 * SUBTREE_ROWS * 32;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        static bool attr[64] = {};
+        if (dev < 64 && !attr[dev]) {
+            PP_TRY(cudaFuncSetAttribute(sweep_subtree_kernel<SR, T, FWD, TRANS>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attr[dev] = true;
+        }
+        const int64_t tasks = (int64_t)sl.count * ((k + 31) / 32);
+        const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_SUBTREE : K_SWEEP_BWD_SUBTREE, st) : -1;
+        sweep_subtree_kernel<SR, T, FWD, TRANS><<<(unsigned)((tasks + 3) / 4), 128, smem, st>>>(
+            hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit);
+        PP_TRY(cudaGetLastError());
+        if (pi >= 0) hp.prof->end(pi, st, 0, 0);
+        (*nl)++;
+        return cudaSuccess;
     }
 
     // left: lmul! (X <- A* X: per stage L* forward, U* backward, then the coupling scatter);
@@ -262,10 +290,12 @@ struct Engine {
         if (left) {
             for (size_t s = 0; s < hp.lstages.size(); s++) {
                 const Stage &sg = hp.lstages[s];
+                PP_TRY((sweep_subtrees<true, false>(hp, hp.sub_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_bottom<true, false>(hp, hp.sb_fwd[s], hp.sb_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_levels<true, false>(hp, sg, true, LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_levels<false, false>(hp, sg, false, UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_bottom<false, false>(hp, hp.sb_bwd[s], hp.sb_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
+                PP_TRY((sweep_subtrees<false, false>(hp, hp.sub_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 if (sg.coupled && sg.nverts > 0) {
                     const int pi = hp.prof ? hp.prof->begin(K_COUPLING, st) : -1;
                     coupling_scatter_kernel<SR, T><<<(sg.nverts + 7) / 8, 256, 0, st>>>(
@@ -286,10 +316,12 @@ struct Engine {
                     if (pi >= 0) hp.prof->end(pi, st, 0, 0);
                     nl++;
                 }
+                PP_TRY((sweep_subtrees<true, true>(hp, hp.sub_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_bottom<true, true>(hp, hp.sb_fwd_r[s], hp.sb_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_levels<true, true>(hp, sg, true, UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_levels<false, true>(hp, sg, false, LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_bottom<false, true>(hp, hp.sb_bwd_r[s], hp.sb_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
+                PP_TRY((sweep_subtrees<false, true>(hp, hp.sub_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
             }
         }
         if (launches) *launches += nl;

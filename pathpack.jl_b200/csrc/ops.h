@@ -12,7 +12,8 @@ namespace pp {
 
 // Kernel classes the profiler separates.
 enum KClass { K_FRONT = 0, K_LARGE_AUX, K_PANEL, K_GEMM, K_SWEEP_FWD, K_SWEEP_BWD, K_COUPLING, K_PERMUTE, K_ASSEMBLE,
-              K_FRONT_BOTTOM, K_SWEEP_FWD_BOTTOM, K_SWEEP_BWD_BOTTOM, K_NCLASS };
+              K_FRONT_BOTTOM, K_SWEEP_FWD_BOTTOM, K_SWEEP_BWD_BOTTOM, K_SWEEP_FWD_SUBTREE, K_SWEEP_BWD_SUBTREE,
+              K_NCLASS };
 extern const char *const KCLASS_NAMES[K_NCLASS];
 
 // Optional per-launch timing with CUDA events on the launching stream; off unless pp_set_profile enabled it.
@@ -114,8 +115,12 @@ struct HostPlan {
     std::vector<std::pair<int64_t, int>> sb_fwd_r, sb_bwd_r;
     std::vector<SLevel> sb_cost_l, sb_cost_r;  // per stage: sums over the bottom fronts (profiler)
     const int *d_spending0 = nullptr;  // bottom children per front (forward counters)
+    // subtrees solved in shared memory (per stage), their roots, first descendants and separator slots
+    std::vector<SubtreeList> sub_l, sub_r;
+    const int *d_sroots = nullptr, *d_fdsc = nullptr, *d_slot = nullptr;
     const int *d_sdone0 = nullptr;     // 1 for fronts outside the bottom, 0 inside (backward flags)
-    int *d_sync = nullptr;             // scratch: [0, nf) counters / flags, nf: next, nf + 1: error
+    int *d_sync = nullptr;             // scratch: [0] task counter, [1] error word, [16, 16 + nf * tiles) counters
+    int64_t sync_cap = 0;              // ints allocated at d_sync
     // concurrency for the large fronts of one level
     std::vector<cudaStream_t> aux;
     std::vector<cudaEvent_t> auxev;

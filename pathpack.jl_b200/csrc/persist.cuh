@@ -88,9 +88,9 @@ __global__ void __launch_bounds__(128) factor_bottom_kernel(const int *__restric
 
 template <int SR, typename T, bool FWD, bool TRANS>
 __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &P, const T *__restrict__ Dv,
-                                                const T *__restrict__ Ov, T *X, int64_t ldx, int k, int unit) {
+                                                const T *__restrict__ Ov, T *X, int64_t ldx, int k, int unit,
+                                                T *xg /* this lane's column of a SWEEP_NNW x 32 scratch */) {
     using S = Sem<SR, T>;
-    constexpr int NW = SWEEP_NNW;
     const int lane = threadIdx.x & 31;
     const int col = tile * 32 + lane;
     const bool ok = col < k;
@@ -101,89 +101,197 @@ __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &
     T *Xc = X + (ok ? col : 0);
     const T z = S::zero();
     const bool scale = !unit && !S::integral;
-    auto Te = [&](int r, int c) -> T { return TRANS ? __ldg(D + c + (int64_t)r * nn) : __ldg(D + r + (int64_t)c * nn); };
-    T x[NW];
-#pragma unroll
-    for (int p = 0; p < NW; p++)
-        if (p < nn) x[p] = ok ? ld_cg(Xc + (int64_t)(rlo + p) * ldx) : z;
+    const int64_t drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;  // Te(r, c) = D[r * drs + c * dcs]
+    for (int p = 0; p < nn; p++) xg[32 * p] = ok ? ld_cg(Xc + (int64_t)(rlo + p) * ldx) : z;
     if (FWD) {
-#pragma unroll
-        for (int p = 0; p < NW; p++) {
-            if (p < nn) {
-                if (scale) x[p] = S::mul(x[p], S::star(Te(p, p)));
-#pragma unroll
-                for (int q = p + 1; q < NW; q++)
-                    if (q < nn) x[q] = S::muladd(Te(q, p), x[p], x[q]);
+        const int64_t ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
+        for (int p = 0; p < nn; p++) {
+            T xp = xg[32 * p];
+            if (scale) {
+                xp = S::mul(xp, S::star(__ldg(D + p * (drs + dcs))));
+                xg[32 * p] = xp;
             }
+            for (int q = p + 1; q < nn; q++) xg[32 * q] = S::muladd(__ldg(D + q * drs + p * dcs), xp, xg[32 * q]);
         }
-#pragma unroll
-        for (int p = 0; p < NW; p++)
-            if (p < nn && ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, x[p]);
+        for (int p = 0; p < nn; p++)
+            if (ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, xg[32 * p]);
         for (int i = 0; i < na; i++) {
             T a = z;
-#pragma unroll
-            for (int p = 0; p < NW; p++)
-                if (p < nn) {
-                    const T o = TRANS ? __ldg(O + p + (int64_t)i * nn) : __ldg(O + i + (int64_t)p * na);
-                    a = S::muladd(o, x[p], a);
-                }
+            for (int p = 0; p < nn; p++) a = S::muladd(__ldg(O + i * ors + p * ocs), xg[32 * p], a);
             if (ok) S::atomic_add(Xc + (int64_t)sep[i] * ldx, a);
         }
     } else {
+        const int64_t ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
         for (int i = 0; i < na; i++) {
             const T xi = ok ? ld_cg(Xc + (int64_t)sep[i] * ldx) : z;
-#pragma unroll
-            for (int p = 0; p < NW; p++)
-                if (p < nn) {
-                    const T o = TRANS ? __ldg(O + i + (int64_t)p * na) : __ldg(O + p + (int64_t)i * nn);
-                    x[p] = S::muladd(o, xi, x[p]);
-                }
+            for (int p = 0; p < nn; p++) xg[32 * p] = S::muladd(__ldg(O + p * ors + i * ocs), xi, xg[32 * p]);
         }
-#pragma unroll
-        for (int pp = 0; pp < NW; pp++) {
-            const int p = NW - 1 - pp;
-            if (p < nn) {
-                if (scale) x[p] = S::mul(S::star(Te(p, p)), x[p]);
-#pragma unroll
-                for (int q = 0; q < NW; q++)
-                    if (q < p) x[q] = S::muladd(Te(q, p), x[p], x[q]);
+        for (int p = nn - 1; p >= 0; p--) {
+            T xp = xg[32 * p];
+            if (scale) {
+                xp = S::mul(S::star(__ldg(D + p * (drs + dcs))), xp);
+                xg[32 * p] = xp;
             }
+            for (int q = 0; q < p; q++) xg[32 * q] = S::muladd(__ldg(D + q * drs + p * dcs), xp, xg[32 * q]);
         }
-#pragma unroll
-        for (int p = 0; p < NW; p++)
-            if (p < nn && ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, x[p]);
+        for (int p = 0; p < nn; p++)
+            if (ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, xg[32 * p]);
     }
 }
 
+// lane 0 of the warp polls *p until it satisfies the predicate (or the limit expires); broadcast result
+__device__ __forceinline__ bool warp_wait(const int *p, bool for_zero, int *err) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) {
+        long long it = 0;
+        while (true) {
+            const int v = *(volatile const int *)p;
+            if (for_zero ? (v == 0) : (v != 0)) break;
+            if (*(volatile const int *)err) {
+                ok = 0;
+                break;
+            }
+            if (++it > WAIT_LIMIT) {
+                atomicExch(err, 1);
+                ok = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
+
+// Independent warp tasks (front, 32-column tile), in work-list order with the tiles innermost.  flags holds one
+// counter (forward: children not yet done) or flag (backward: done) per (tile, front): flags[tile * nf + f].
 template <int SR, typename T, bool FWD, bool TRANS>
 __global__ void __launch_bounds__(256, 2) sweep_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P,
-                                                           const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
-                                                           int64_t ldx, int k, int unit, int *flags, int *next,
-                                                           int *err) {
+                                                              const T *__restrict__ Dv, const T *__restrict__ Ov,
+                                                              T *X, int64_t ldx, int k, int unit, int *flags,
+                                                              int *next, int *err) {
+    __shared__ T scratch[8][SWEEP_NNW * 32];
     const int ntiles = (k + 31) / 32;
-    const int w = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    T *xg = &scratch[threadIdx.x >> 5][lane];
+    const int nf = P.nf;
+    const int64_t ntask = (int64_t)count * ntiles;
     while (true) {
-        const int t = cta_take(next);
-        if (t >= count) return;
-        const int f = wl[t];
+        int t = 0;
+        if (lane == 0) t = atomicAdd(next, 1);
+        t = __shfl_sync(0xffffffffu, t, 0);
+        if (t >= ntask) return;
+        const int idx = t / ntiles, tile = t - idx * ntiles;
+        const int f = wl[idx];
+        int *fl = flags + (int64_t)tile * nf;
+        const int p = P.pnt[f];
         if (FWD) {
-            if (!cta_wait(flags + f, true, err)) return;
-        } else {
-            const int p = P.pnt[f];
-            if (p >= 0 && !cta_wait(flags + p, false, err)) return;
+            if (!warp_wait(fl + f, true, err)) return;
+        } else if (p >= 0) {
+            if (!warp_wait(fl + p, false, err)) return;
         }
-        for (int tile = w; tile < ntiles; tile += 8) warp_front_tile<SR, T, FWD, TRANS>(f, tile, P, Dv, Ov, X, ldx, k, unit);
-        __syncthreads();
-        if (threadIdx.x == 0) {
+        warp_front_tile<SR, T, FWD, TRANS>(f, tile, P, Dv, Ov, X, ldx, k, unit, xg);
+        __syncwarp();
+        if (lane == 0) {
             __threadfence();
             if (FWD) {
-                const int p = P.pnt[f];
-                if (p >= 0) atomicSub(flags + p, 1);
+                if (p >= 0) atomicSub(fl + p, 1);
             } else {
-                atomicExch(flags + f, 1);
+                atomicExch(fl + f, 1);
             }
         }
     }
+}
+
+// ---------------------------------------------------------------- subtrees of the bottom in shared memory
+//
+// A subtree rooted at r touches only its residual rows, the contiguous positions rlo(fd(r)) .. rhi(r), and the
+// separator of r (the running-intersection property of the clique tree: a separator vertex of a front in the
+// subtree is either in the subtree or in sep(r)).  A warp task (subtree, 32-column tile) loads those rows once
+// into shared memory, runs every front of the subtree in postorder (forward) or reverse postorder (backward)
+// there, and writes back once; the forward sweep (+)-scatters the accumulated separator rows with atomics.
+// slot[Sptr[g] + i] is the shared-memory row of the i-th separator vertex of front g.  Each lane touches only
+// its own column, so a task needs no barrier.
+
+template <int SR, typename T, bool FWD, bool TRANS>
+__global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restrict__ roots, int nroots, DevPlan P,
+                                                            const int *__restrict__ fdsc, const int *__restrict__ slot,
+                                                            const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
+                                                            int64_t ldx, int k, int unit) {
+    using S = Sem<SR, T>;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    T *xs = reinterpret_cast<T *>(smem_raw) + (size_t)w * SUBTREE_ROWS * 32 + lane;  // row s at xs[32 * s]
+    const int ntiles = (k + 31) / 32;
+    const int64_t t = (int64_t)blockIdx.x * 4 + w;
+    if (t >= (int64_t)nroots * ntiles) return;
+    const int r = roots[t / ntiles], tile = (int)(t % ntiles);
+    const int col = tile * 32 + lane;
+    const bool ok = col < k;
+    T *Xc = X + (ok ? col : 0);
+    const T z = S::zero();
+    const bool scale = !unit && !S::integral;
+    const int f0 = fdsc[r];
+    const int rlo0 = P.rlo[f0];
+    const int nres = P.rlo[r] + P.nn[r] - rlo0;
+    const int nsep = P.na[r];
+    const int *sepr = P.stgt + P.sptr[r];
+    for (int s = 0; s < nres; s++) xs[32 * s] = ok ? Xc[(int64_t)(rlo0 + s) * ldx] : z;
+    for (int i = 0; i < nsep; i++) xs[32 * (nres + i)] = (FWD || !ok) ? z : Xc[(int64_t)sepr[i] * ldx];
+    for (int gg = 0; gg <= r - f0; gg++) {
+        const int g = FWD ? f0 + gg : r - gg;
+        const int nn = P.nn[g], na = P.na[g];
+        T *xg = xs + 32 * (P.rlo[g] - rlo0);  // the front's residual rows: xg[32 * p]
+        const T *D = Dv + P.dptr[g];
+        const T *O = Ov + P.lptr[g];
+        const int *sl = slot + P.sptr[g];
+        // (r, c) of the triangle and (sep i, residual p) of the off-diagonal block as read by this sweep
+        const int64_t drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;
+        if (FWD) {
+            const int64_t ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
+            for (int p = 0; p < nn; p++) {
+                T xp = xg[32 * p];
+                if (scale) {
+                    xp = S::mul(xp, S::star(__ldg(D + p * (drs + dcs))));
+                    xg[32 * p] = xp;
+                }
+                for (int q = p + 1; q < nn; q++) xg[32 * q] = S::muladd(__ldg(D + q * drs + p * dcs), xp, xg[32 * q]);
+            }
+            for (int i = 0; i < na; i++) {
+                T a = z;
+                for (int p = 0; p < nn; p++) a = S::muladd(__ldg(O + i * ors + p * ocs), xg[32 * p], a);
+                T &c = xs[32 * sl[i]];
+                c = S::add(c, a);
+            }
+        } else {
+            const int64_t ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
+            for (int i = 0; i < na; i++) {
+                const T xi = xs[32 * sl[i]];
+                for (int p = 0; p < nn; p++) xg[32 * p] = S::muladd(__ldg(O + p * ors + i * ocs), xi, xg[32 * p]);
+            }
+            for (int p = nn - 1; p >= 0; p--) {
+                T xp = xg[32 * p];
+                if (scale) {
+                    xp = S::mul(S::star(__ldg(D + p * (drs + dcs))), xp);
+                    xg[32 * p] = xp;
+                }
+                for (int q = 0; q < p; q++) xg[32 * q] = S::muladd(__ldg(D + q * drs + p * dcs), xp, xg[32 * q]);
+            }
+        }
+    }
+    if (!ok) return;
+    for (int s = 0; s < nres; s++) Xc[(int64_t)(rlo0 + s) * ldx] = xs[32 * s];
+    if (FWD)
+        for (int i = 0; i < nsep; i++) S::atomic_add(Xc + (int64_t)sepr[i] * ldx, xs[32 * (nres + i)]);
+}
+
+// flags[t * nf + f] = init[f] for every tile t
+static __global__ void init_flags_kernel(int *flags, const int *init, int nf, int ntiles) {
+    const int64_t tot = (int64_t)nf * ntiles;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < tot; i += (int64_t)gridDim.x * blockDim.x)
+        flags[i] = init[i % nf];
 }
 
 // ---------------------------------------------------------------- panels of the large-front LU

@@ -10,6 +10,8 @@ namespace pp {
 
 // largest residual of a front in the register-resident warp sweep of the bottom of the tree
 constexpr int SWEEP_NNW = 16;
+// rows (residual range + root separator) of a subtree solved in shared memory by one warp
+constexpr int SUBTREE_ROWS = 96;
 
 // Device arrays of a structure (0-based, positions = permuted labels).  Per front f: the residual is
 // rlo[f] .. rlo[f]+nn[f]-1, the separator stgt[sptr[f] .. sptr[f+1]-1] with rel[] its positions in the
@@ -29,6 +31,12 @@ struct DevPlan {
     const int *ntgt;
     const int *perm, *invp, *idx, *bptr, *fcc;
     const int *pnt;  // parent front, -1 for a root
+};
+
+// subtree tasks of one stage: roots[off .. off+count)
+struct SubtreeList {
+    int64_t off = 0;
+    int count = 0;
 };
 
 // A group of fronts launched together: one size class of one tree level.

@@ -10,7 +10,7 @@
 //   2. per component (scliquetree, src/CPU/chordal_ssymbolic.jl:59-184): one front for components of one or
 //      two vertices, otherwise a fill-reducing ordering of the symmetrised component (nested dissection by
 //      breadth-first level structures, minimum degree inside the small pieces; CliqueTrees' default AMF is
-//      not available here) and its clique tree of fundamental supernodes, fronts in postorder;
+//      not available here) and its clique tree of maximal supernodes, fronts in postorder;
 //   3. the coupling graph N between components (soffd, src/CPU/chordal_ssymbolic.jl:212-269).
 //
 // Output layout (0-based, permuted labels), as pp_set_structure takes it after the shift from 1-based:
@@ -305,7 +305,7 @@ struct Ordering {
 
 // ---------------------------------------------------------------- clique tree of one component
 // Input: symmetric adjacency (local labels), an elimination order.  Output: postordered fronts of
-// fundamental supernodes, the final local order (position -> local vertex), res pointers and separators
+// maximal supernodes, the final local order (position -> local vertex), res pointers and separators
 // in positions.
 struct Fronts {
     std::vector<i32> order;       // position -> local vertex
@@ -402,10 +402,11 @@ Fronts cliquetree(const Graph &g, const std::vector<i32> &elim) {
             }
         }
     }
-    // fundamental supernodes: q joins q - 1's supernode when q - 1 is its only child and counts nest
+    // maximal supernodes: q joins q - 1's supernode when q - 1 is a child of q and the column counts nest
+    // (q's structure is q - 1's minus q - 1), whatever q's other children
     std::vector<i32> snode_start;
     for (i32 q = 0; q < m; q++) {
-        const bool join = q > 0 && par[q - 1] == q && nchild[q] == 1 && cc[q - 1] == cc[q] + 1;
+        const bool join = q > 0 && par[q - 1] == q && cc[q - 1] == cc[q] + 1;
         if (!join) snode_start.push_back(q);
     }
     const i32 nf = (i32)snode_start.size();

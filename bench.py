@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """bench.py — the headline benchmark: (x)(+) pairs/s of mlu + lmul! on BASELINE config 2.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|1|3|4|5a|5b-f32|5b-i32|5b-f64]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-cpu-baseline]
 
 Workload (config 2, the configuration the metric is quoted on that fits one GPU): mlu(MinPlus(), A) then
 lmul!(F, B) in Float64 on a 256 x 256 4-connected grid digraph (65,536 vertices, 261,120 arcs with independent

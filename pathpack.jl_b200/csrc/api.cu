@@ -1032,6 +1032,84 @@ extern "C" int32_t pp_lmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_
     return run_solve(h, B, ldb, k, where, 1, "pp_lmul");
 }
 
+// lmul! on device-resident B with the caller's scratch instead of the handle's: the right-hand-side
+// workspace first, the sweep counters after it.  Allocates nothing (no device memory, no profiler events);
+// the counters are reset by the sweeps themselves before each persistent launch, so the scratch may hold
+// anything on entry.
+int32_t pp_internal_lmul_scratch(pp_handle *h, void *B, int64_t ldb, int64_t k, void *scratch, size_t cap,
+                                 const char *who) {
+    if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
+    if (!h->factored) return fail(h, PP_ESTATE, "%s: no factorization (call pp_factor)", who);
+    const int n = h->hp.n;
+    if (k < 0 || k >= INT32_MAX / 2) return fail(h, PP_EINVAL, "%s: k = %lld", who, (long long)k);
+    if (k == 0 || n == 0) {
+        ok(h);
+        return PP_OK;
+    }
+    if (!B) return fail(h, PP_EINVAL, "%s: null B", who);
+    if (ldb < n) return fail(h, PP_EINVAL, "%s: leading dimension %lld < n = %d", who, (long long)ldb, n);
+    const size_t need = pp_internal_lmul_scratch_bytes(h, k);
+    if (need > cap)
+        return fail(h, PP_EINVAL,
+                    "%s: n = %d and k = %lld need %zu bytes of scratch, the static scratch holds %zu; "
+                    "use pp_lmul or fewer right-hand sides per call",
+                    who, n, (long long)k, need, cap);
+    CK(h, cudaSetDevice(h->device), who);
+    cudaPointerAttributes pa{};
+    CK(h, cudaPointerGetAttributes(&pa, B), who);
+    if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
+        return fail(h, PP_EINVAL, "%s: B must be device memory", who);
+    const size_t es = h->ops->esize;
+    const int64_t ldx = (k + 3) & ~(int64_t)3;
+    const size_t xbytes = ((es * (size_t)n * ldx) + 255) & ~(size_t)255;
+    void *X = scratch;
+    int *sync = reinterpret_cast<int *>(static_cast<unsigned char *>(scratch) + xbytes);
+    // borrow the counters and switch the profiler off for this call; both are put back before returning
+    int *const save_sync = h->hp.d_sync;
+    const int64_t save_cap = h->hp.sync_cap;
+    Profiler *const save_prof = h->hp.prof;
+    h->hp.d_sync = sync;
+    h->hp.sync_cap = (int64_t)((cap - xbytes) / sizeof(int));
+    h->hp.prof = nullptr;
+    cudaStream_t st = h->stream;
+    int64_t nl = 0;
+    cudaError_t e = cudaEventRecord(h->ev0, st);
+    if (e == cudaSuccess) e = h->ops->rows_in(B, ldb, X, ldx, h->hp.dev.invp, n, (int)k, st);
+    if (e == cudaSuccess) e = h->ops->solve(h->hp, values_of(h), 1, X, ldx, (int)k, st, &nl);
+    if (e == cudaSuccess) e = h->ops->rows_out(B, ldb, X, ldx, h->hp.dev.invp, n, (int)k, st);
+    if (e == cudaSuccess) e = cudaEventRecord(h->ev1, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    h->hp.d_sync = save_sync;
+    h->hp.sync_cap = save_cap;
+    h->hp.prof = save_prof;
+    if (e != cudaSuccess) return cuda_fail(h, e, who);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+    h->st.ms_solve = ms;
+    h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)k;
+    h->st.kernel_launches = nl + 2;
+    ok(h);
+    return PP_OK;
+}
+
+int32_t pp_internal_device(const pp_handle *h, int *device) {
+    if (!h || !device) return PP_EINVAL;
+    *device = h->device;
+    return PP_OK;
+}
+
+int32_t pp_internal_fail(pp_handle *h, int32_t code, const char *msg) { return fail(h, code, "%s", msg); }
+
+// scratch bytes of pp_internal_lmul_scratch for k right-hand sides: the workspace (rounded to 256 bytes)
+// and the counters of ensure_sync
+size_t pp_internal_lmul_scratch_bytes(const pp_handle *h, int64_t k) {
+    if (!h || !h->ops || k <= 0) return 0;
+    const int64_t ldx = (k + 3) & ~(int64_t)3;
+    const size_t xbytes = ((h->ops->esize * (size_t)h->hp.n * ldx) + 255) & ~(size_t)255;
+    const int64_t counters = ((k + 31) / 32) * (int64_t)h->hp.nf + 16;
+    return xbytes + sizeof(int) * (size_t)counters;
+}
+
 extern "C" int32_t pp_rmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where) {
     return run_solve(h, B, ldb, k, where, 0, "pp_rmul");
 }

@@ -143,6 +143,21 @@ class B200SLU:
         check(lib().pp_sync(self._h), self._h)
 
     # --- solves
+    def lmul_static(self, B):
+        """B <- A* B for a column-major CUDA tensor B, through pp_lmul_static: the solve allocates nothing and
+        uses the library's static per-device scratch (PP_STATIC_SCRATCH_BYTES), so n x k must fit in it."""
+        n = self.S.n
+        if not hasattr(B, "data_ptr") or not B.is_cuda or B.dtype.itemsize != self.dtype.itemsize:
+            raise TypeError("B must be a CUDA tensor of the factor's element type")
+        if B.dim() == 1:
+            k, ld = 1, n
+        else:
+            if B.stride(0) != 1:
+                raise ValueError("B must be column-major (stride(0) == 1)")
+            k, ld = B.shape[1], B.stride(1)
+        check(lib().pp_lmul_static(self._h, vptr(B), ld, k), self._h)
+        return B
+
     def _solve(self, B, left):
         n = self.S.n
         fn = lib().pp_lmul if left else lib().pp_rmul

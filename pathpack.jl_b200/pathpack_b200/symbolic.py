@@ -2,7 +2,7 @@
 (src/CPU/chordal_ssymbolic.jl:1-8) plus the permutation, as numpy arrays.
 
 In PATHPACK.jl this comes from `ssymbolic(A; alg)` (Julia + CliqueTrees.jl).  `ssymbolic` here calls the
-library's host stand-in (pp_symbolic: the reference's SCC walk, nested dissection, fundamental supernodes);
+library's host stand-in (pp_symbolic: the reference's SCC walk, nested dissection, maximal supernodes);
 `Structure.from_arrays` takes a structure computed elsewhere, e.g. by Julia, 0- or 1-based.
 """
 import ctypes as C

@@ -157,3 +157,21 @@ def test_reference_structures(gpu, fixture):
         same(pp.rmul_(R.copy(order="F"), F), O.rmul(R), "MinPlus", np.float32, fixture + " rmul")
     finally:
         F.close()
+
+
+@pytest.mark.parametrize("name,dtype", [("MinPlus", np.float64), ("MaxMin", np.float32)])
+def test_star_panels(gpu, name, dtype):
+    """The column panels of pathpack_b200.panels (one per rank of a multi-GPU star) put together are the whole
+    star, bit for bit."""
+    from pathpack_b200.panels import star_panel
+
+    n, S, F, O = factor_both("sprand", name, dtype)
+    try:
+        full = pp.Matrix(F)
+        for world in (2, 3, 8):
+            parts = [star_panel(F, r, world) for r in range(world)]
+            C = np.concatenate([c for _, c in parts], axis=1)
+            assert [c0 for c0, _ in parts] == sorted(c0 for c0, _ in parts)
+            same(C, full, name, dtype, "star from %d panels" % world)
+    finally:
+        F.close()

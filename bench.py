@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """bench.py — the headline benchmark: (x)(+) pairs/s of mlu + lmul! on BASELINE config 2.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-cpu-baseline]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-cpu-baseline] [--once]
 
 Workload (config 2, the configuration the metric is quoted on that fits one GPU): mlu(MinPlus(), A) then
 lmul!(F, B) in Float64 on a 256 x 256 4-connected grid digraph (65,536 vertices, 261,120 arcs with independent
@@ -148,6 +148,26 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_once():
+    """The workload's step twice (warm-up, then the step an ncu capture selects with -s / -c), nothing timed."""
+    import torch
+
+    import pathpack_b200 as pp
+
+    w = config2(0)
+    F = pp.B200SLU(pp.MinPlus(), np.float64, w["S"], device=0)
+    nz_d = torch.from_numpy(w["nz"]).to("cuda:0")
+    B0 = torch.from_numpy(np.ascontiguousarray(w["B"].T)).to("cuda:0")
+    F.assemble_csc(w["cp"], w["rv"], w["nz"])
+    for _ in range(2):
+        F.update_values(nz_d)
+        F.factor()
+        Bw = B0.clone()
+        pp.lmul_(F, Bw.T)
+    torch.cuda.synchronize()
+    F.close()
+
+
 def run_ours(args, rank, world, local):
     import torch
 
@@ -278,12 +298,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--once", action="store_true",
+                    help="one warm-up step and one step of the workload, no timing line (for ncu captures)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.once:
+        run_once()
         return
     if world > 1:
         import datetime

@@ -45,9 +45,8 @@ const Ops *get_ops(int sr, int dt) {
 }  // namespace pp
 
 namespace pp {
-const char *const KCLASS_NAMES[K_NCLASS] = {"front_small_kernel", "large_front_aux", "panel_kernel",
-                                            "gemm_kernel(trailing)", "sweep_kernel(forward)",
-                                            "sweep_kernel(backward)", "coupling", "permute", "assemble_kernel",
+const char *const KCLASS_NAMES[K_NCLASS] = {"factor_top_kernel", "sweep_tiled_kernel(fwd)",
+                                            "sweep_tiled_kernel(bwd)", "coupling", "permute", "assemble_kernel",
                                             "factor_bottom_kernel", "sweep_bottom_kernel(fwd)",
                                             "sweep_bottom_kernel(bwd)", "sweep_subtree_kernel(fwd)",
                                             "sweep_subtree_kernel(bwd)"};
@@ -93,9 +92,10 @@ struct pp_handle {
     std::vector<int> invp;
     // device structure
     DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
-        d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_ffronts, d_sfronts, d_sverts, d_pnt, d_fbottom,
-        d_fpending0, d_spending0, d_sdone0, d_sync, d_sroots, d_fdsc, d_slot;
+        d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_sfronts, d_sverts, d_pnt, d_fbottom,
+        d_fpending0, d_spending0, d_sdone0, d_sync, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags;
     std::vector<int> pnt, height;
+    int maxh = 0;
     // values and work
     DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val;
     int64_t nD = 0, nL = 0;
@@ -103,8 +103,6 @@ struct pp_handle {
     size_t ws_esize = 0;
     pp_stats st{};
     Profiler prof;
-    std::vector<cudaStream_t> aux;
-    std::vector<cudaEvent_t> auxev;
     int sm_count = 148;
 };
 
@@ -169,15 +167,6 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev1);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->hp.levev, cudaEventDisableTiming);
-    for (int i = 0; i < 4 && e == cudaSuccess; i++) {
-        cudaStream_t s = nullptr;
-        cudaEvent_t ev = nullptr;
-        e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-        if (s) h->aux.push_back(s);
-        if (ev) h->auxev.push_back(ev);
-    }
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) {
         pp_destroy(h);
@@ -194,12 +183,6 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
-    for (cudaStream_t s : h->aux) {
-        cudaStreamSynchronize(s);
-        cudaStreamDestroy(s);
-    }
-    for (cudaEvent_t e : h->auxev) cudaEventDestroy(e);
-    if (h->hp.levev) cudaEventDestroy(h->hp.levev);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;  // DevBuf destructors free the device memory
     return PP_OK;
@@ -487,8 +470,6 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         // rmul stages: the gather concerns the stage's own columns j (rows of earlier components feed them)
         build_stages(rstage, hp.rstages, sfronts, sverts, hp.sb_fwd_r, hp.sb_bwd_r, hp.sb_cost_r, hp.sub_r, sroots);
         (void)ccoupled;
-        // factorization levels (classified per element size in prepare_workspace)
-        hp.flevels.assign(maxh + 1, Level());
         std::vector<int64_t> Np64(Np.begin(), Np.end());
         // device uploads
         cudaStream_t st = h->stream;
@@ -554,30 +535,14 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         hp.d_sdone0 = h->d_sdone0.as<int>();
         hp.d_sync = h->d_sync.as<int>();
         hp.sync_cap = 32 * nf + 16;
-        hp.aux = h->aux;
-        hp.auxev = h->auxev;
-        hp.levev = h->hp.levev;
         hp.sm_count = h->sm_count;
         h->invp = invp;
         h->pnt = pnt;
-        h->height = height;
-        // factorization heights, kept for prepare_workspace
+        h->height = height;  // factorization heights, kept for prepare_workspace
+        h->maxh = maxh;
         h->hp = std::move(hp);
         h->hp.mld.clear();
         h->hp.esize = 0;
-        // stash heights in flevels via a temporary: store front ids by height (classified later)
-        h->hp.h_ffronts.clear();
-        std::vector<std::vector<int>> byh(maxh + 1);
-        for (int64_t f = 0; f < nf; f++) byh[height[f]].push_back((int)f);
-        for (int hh = 0; hh <= maxh; hh++) {
-            FrontGroup g;
-            g.off = (int64_t)h->hp.h_ffronts.size();
-            g.count = (int)byh[hh].size();
-            g.max_nj = 0;
-            g.large = false;
-            h->hp.flevels[hh].groups.assign(1, g);
-            h->hp.h_ffronts.insert(h->hp.h_ffronts.end(), byh[hh].begin(), byh[hh].end());
-        }
         h->nD = h->hp.dptr[nf];
         h->nL = h->hp.lptr[nf];
         h->ws_esize = 0;
@@ -611,7 +576,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
 
 // Algorithmic traffic (elements) and (x)(+) pairs of one front's factorization: read the assembled blocks
 // and the children's update matrices, write the factor blocks and the update matrix; the partial LU's pairs.
-static void front_cost(const HostPlan &hp, int f, FrontGroup &g) {
+static void front_cost(const HostPlan &hp, int f, Cost &g) {
     const double nn = hp.nn[f], na = hp.na[f], nj = nn + na;
     double e = 4.0 * (nn * nn + nn * na) + na * na;
     for (int c = hp.chdptr[f]; c < hp.chdptr[f + 1]; c++) {
@@ -623,21 +588,29 @@ static void front_cost(const HostPlan &hp, int f, FrontGroup &g) {
     g.pairs += S2(nj) - S2(na);
 }
 
-// Workspace layout for the element size of the values: fronts whose frontal matrix fits the one-CTA kernel's
-// shared memory keep a compact na x na update matrix; larger fronts keep their whole nj x nj frontal matrix,
-// and their update matrix is its trailing block.  Fronts of each level are grouped by size class.
+// Workspace layout and the factorization schedule.  The bottom of the tree (fronts with nn + na within 32 KB
+// of shared memory whose whole subtree is such) is one persistent launch, front by front; each bottom front
+// keeps a compact na x na update matrix.  Every other front keeps its whole nj x nj frontal matrix (its update
+// matrix is the trailing block, read in place by the parent) and is factored by the tile tasks of top.cuh:
+// per front, by height, the assembly of each column block and then the tiles in (min(I, J), max(I, J)) order.
 static int32_t prepare_workspace(pp_handle *h) {
     HostPlan &hp = h->hp;
     if (h->ws_esize == h->ops->esize && !hp.mld.empty()) return PP_OK;
-    const int limit = h->ops->small_limit;
     const int nf = hp.nf;
+    int fb_limit = 1;
+    while ((size_t)(fb_limit + 1) * (fb_limit + 1) * h->ops->esize <= 32 * 1024) fb_limit++;
+    std::vector<char> fbot(nf, 0), allbot(nf, 1);
+    for (int f = 0; f < nf; f++) {
+        fbot[f] = (hp.nn[f] + hp.na[f] <= fb_limit) && allbot[f];
+        if (!fbot[f] && h->pnt[f] >= 0) allbot[h->pnt[f]] = 0;
+    }
     hp.mptr.assign(nf, 0);
     hp.fws.assign(nf, -1);
     hp.mld.assign(nf, 1);
     int64_t off = 0;
     for (int f = 0; f < nf; f++) {
         const int nn = hp.nn[f], na = hp.na[f], nj = nn + na;
-        if (nj <= limit) {
+        if (fbot[f]) {
             hp.mptr[f] = off;
             hp.mld[f] = std::max(na, 1);
             off += (int64_t)na * na;
@@ -650,19 +623,12 @@ static int32_t prepare_workspace(pp_handle *h) {
         off = (off + 3) & ~(int64_t)3;  // 16-byte alignment of every block
     }
     hp.ws_elems = off;
-    // bottom of the tree for the persistent factorization: nn + na within 32 KB of shared memory, whole subtree
-    int fb_limit = 1;
-    while ((size_t)(fb_limit + 1) * (fb_limit + 1) * h->ops->esize <= 32 * 1024) fb_limit++;
-    std::vector<char> fbot(nf, 0), allbot(nf, 1);
-    for (int f = 0; f < nf; f++) {
-        fbot[f] = (hp.nn[f] + hp.na[f] <= fb_limit) && allbot[f];
-        if (!fbot[f] && h->pnt[f] >= 0) allbot[h->pnt[f]] = 0;
-    }
+    const int maxh = h->maxh;
+    cudaStream_t st = h->stream;
     {
-        const int maxh = (int)hp.flevels.size() - 1;
         std::vector<std::vector<int>> byh(maxh + 1);
         std::vector<int> pending0(nf, 0);
-        FrontGroup acc;
+        Cost acc;
         hp.fb_maxnj = 0;
         for (int f = 0; f < nf; f++)
             if (fbot[f]) {
@@ -676,68 +642,56 @@ static int32_t prepare_workspace(pp_handle *h) {
         hp.fb_count = (int)wl.size();
         hp.fb_bytes = acc.bytes;
         hp.fb_pairs = acc.pairs;
-        CK(h, upload(h->d_fbottom, wl, h->stream), "upload");
-        CK(h, upload(h->d_fpending0, pending0, h->stream), "upload");
+        CK(h, upload(h->d_fbottom, wl, st), "upload");
+        CK(h, upload(h->d_fpending0, pending0, st), "upload");
         hp.d_fbottom = h->d_fbottom.as<int>();
         hp.d_fpending0 = h->d_fpending0.as<int>();
     }
-    // the remaining fronts by level, in size classes
-    std::vector<int> fronts;
-    const int classes[5] = {16, 32, 64, 128, limit};
-    std::vector<std::vector<int>> top_by_h(hp.flevels.size());
-    for (int f = 0; f < nf; f++)
-        if (!fbot[f]) top_by_h[h->height[f]].push_back(f);
-    for (size_t hh = 0; hh < hp.flevels.size(); hh++) {
-        Level &L = hp.flevels[hh];
-        const std::vector<int> &ids = top_by_h[hh];
-        std::vector<FrontGroup> groups;
-        int lo = 0;
-        for (int c = 0; c < 5; c++) {
-            const int hi = classes[c];
-            if (hi <= lo) continue;
-            FrontGroup g;
-            g.off = (int64_t)fronts.size();
-            g.max_nj = 0;
-            g.large = false;
-            for (int f : ids) {
-                const int nj = hp.nn[f] + hp.na[f];
-                if (nj > lo && nj <= hi) {
-                    fronts.push_back(f);
-                    g.max_nj = std::max(g.max_nj, nj);
-                }
+    {
+        std::vector<std::vector<int>> byh(maxh + 1);
+        for (int f = 0; f < nf; f++)
+            if (!fbot[f]) byh[h->height[f]].push_back(f);
+        std::vector<int> tasks;
+        std::vector<int64_t> foff(nf, 0);
+        int64_t nflags = 16;
+        Cost acc;
+        std::vector<std::pair<int, int>> tiles;
+        for (int hh = 0; hh <= maxh; hh++)
+            for (int f : byh[hh]) {
+                const int kb = (hp.nn[f] + TOP_TILE - 1) / TOP_TILE, nbt = kb + (hp.na[f] + TOP_TILE - 1) / TOP_TILE;
+                foff[f] = nflags;
+                nflags += nbt + (int64_t)nbt * nbt + 1;
+                for (int J = 0; J < nbt; J++) tasks.insert(tasks.end(), {f, 0, J, 0});
+                tiles.clear();
+                for (int I = 0; I < nbt; I++)
+                    for (int J = 0; J < nbt; J++) tiles.push_back({I, J});
+                std::stable_sort(tiles.begin(), tiles.end(), [](const std::pair<int, int> &a,
+                                                                 const std::pair<int, int> &b) {
+                    const int a0 = std::min(a.first, a.second), b0 = std::min(b.first, b.second);
+                    if (a0 != b0) return a0 < b0;
+                    return std::max(a.first, a.second) < std::max(b.first, b.second);
+                });
+                for (const auto &t : tiles) tasks.insert(tasks.end(), {f, t.first, t.second, 1});
+                front_cost(hp, f, acc);
             }
-            g.count = (int)(fronts.size() - g.off);
-            for (int64_t t = g.off; t < (int64_t)fronts.size(); t++) front_cost(hp, fronts[t], g);
-            if (g.count) groups.push_back(g);
-            lo = hi;
-        }
-        FrontGroup g;
-        g.off = (int64_t)fronts.size();
-        g.large = true;
-        g.max_nj = 0;
-        for (int f : ids) {
-            const int nj = hp.nn[f] + hp.na[f];
-            if (nj > limit) {
-                fronts.push_back(f);
-                g.max_nj = std::max(g.max_nj, nj);
-            }
-        }
-        g.count = (int)(fronts.size() - g.off);
-        for (int64_t t = g.off; t < (int64_t)fronts.size(); t++) front_cost(hp, fronts[t], g);
-        if (g.count) groups.push_back(g);
-        L.groups = std::move(groups);
+        hp.top_ntasks = (int)(tasks.size() / 4);
+        hp.top_cost = acc;
+        hp.tflags_n = nflags;
+        if (tasks.empty()) tasks.assign(4, 0);
+        CK(h, upload(h->d_ttasks, tasks, st), "upload");
+        CK(h, upload(h->d_tfoff, foff, st), "upload");
+        CK(h, h->d_tflags.ensure(sizeof(int) * (size_t)nflags), "upload");
+        hp.d_ttasks = reinterpret_cast<const int4 *>(h->d_ttasks.p);
+        hp.d_tfoff = h->d_tfoff.as<int64_t>();
+        hp.d_tflags = h->d_tflags.as<int>();
     }
-    hp.h_ffronts = fronts;
-    cudaStream_t st = h->stream;
     CK(h, upload(h->d_mptr, hp.mptr, st), "upload");
     CK(h, upload(h->d_mld, hp.mld, st), "upload");
     CK(h, upload(h->d_fws, hp.fws, st), "upload");
-    CK(h, upload(h->d_ffronts, fronts, st), "upload");
     CK(h, cudaStreamSynchronize(st), "upload");
     hp.dev.mptr = h->d_mptr.as<int64_t>();
     hp.dev.mld = h->d_mld.as<int>();
     hp.dev.fws = h->d_fws.as<int64_t>();
-    hp.d_ffronts = h->d_ffronts.as<int>();
     h->ws_esize = h->ops->esize;
     return PP_OK;
 }
@@ -1186,7 +1140,7 @@ extern "C" int32_t pp_get_stats(pp_handle *h, pp_stats *s) {
     int64_t bytes = 0;
     for (DevBuf *b : {&h->d_rlo, &h->d_nn, &h->d_na, &h->d_sptr, &h->d_stgt, &h->d_rel, &h->d_dptr, &h->d_lptr,
                       &h->d_chdptr, &h->d_chdtgt, &h->d_mptr, &h->d_mld, &h->d_fws, &h->d_nptr, &h->d_ntgt,
-                      &h->d_perm, &h->d_invp, &h->d_idx, &h->d_bptr, &h->d_fcc, &h->d_ffronts, &h->d_sfronts,
+                      &h->d_perm, &h->d_invp, &h->d_idx, &h->d_bptr, &h->d_fcc, &h->d_sfronts,
                       &h->d_sverts, &h->LD, &h->LL, &h->UD, &h->UL, &h->Nval, &h->W, &h->X, &h->stage_in,
                       &h->stage_out, &h->csc_ptr, &h->csc_row, &h->csc_val})
         bytes += (int64_t)b->bytes;

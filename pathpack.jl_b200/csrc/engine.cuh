@@ -1,22 +1,15 @@
-// engine.cuh — the device kernels of the factorization and the solves, templated on the semiring.
+// engine.cuh — device building blocks of the factorization and the solves, templated on the semiring.
 //
-//   front_small_kernel   one CTA per front, the whole frontal matrix in shared memory: extend-add of the
-//                        children's update matrices, combination with the assembled entries, partial LU over
-//                        the front's pivots, write-back of the factor blocks and the update matrix.  Replaces
-//                        sgetrf_loop!/sgetrf_loop_1!/sgetrf_send! (src/CPU/chordal/sgetrf.jl:35-290) and the
-//                        reference GPU's front_diag_kernel!/extend-add kernels (batched/sgetrf.jl:11-286).
-//   large-front path     frontal matrix in global memory: extend_add / combine kernels, then a blocked
-//                        right-looking partial LU (panel_kernel: 64-pivot diagonal block in shared memory plus
-//                        the column and row panels; the semiring GEMM for the trailing update, which includes
-//                        the Schur complement), then extract_kernel.  Replaces factor_front_gpu!
-//                        (ext/PATHPACKCUDAExt/chordal/sgetrf.jl:915-992) and dense/sgetrf.jl:31-176.
-//   sweep_kernel         one CTA per (front, 32 right-hand sides): a blocked triangular solve on the front's
-//                        residual rows and the (+)-scatter to (forward) or gather from (backward) its separator
-//                        rows.  Replaces the per-front chordal solves (src/CPU/chordal/strsx.jl:130-1188) and
-//                        the reference GPU sweeps (batched/sweep.jl:9-265, chordal/sgetrs.jl:536-1004).
+//   front_body           one front in shared memory, executed by one CTA: extend-add of the children's update
+//                        matrices, combination with the assembled entries, partial LU over the front's pivots,
+//                        write-back of the factor blocks and the update matrix (sgetrf_loop!/sgetrf_loop_1!/
+//                        sgetrf_send!, src/CPU/chordal/sgetrf.jl:35-290); the bottom of the tree uses it.
+//   lu_smem              right-looking partial LU of the star of a block in shared memory (sgetrf2!'s scalar
+//                        path, src/CPU/dense/sgetrf.jl:151-175); also pp_getrf_batched.
 //   coupling kernels     the products with the coupling N between components (src/CPU/sparse/sgemx.jl:101-213).
 //   permutation kernels  permuterows!/permutecols! (src/CPU/utils.jl:207-257) fused with the transpose into
 //                        the internal layout X[position][rhs] (right-hand sides contiguous).
+//   assemble_kernel      copyto!(F, A) on the device (src/CPU/chordal_slu.jl:221-321).
 //
 // Every (x)(+) operation follows the per-element dataflow of the reference's CPU path (same operands, same
 // stored intermediates), so idempotent semirings give the reference's bits.
@@ -26,10 +19,6 @@
 #include "plan.h"
 
 namespace pp {
-
-constexpr int SWEEP_CH = 64;     // residual rows per chunk of the sweep
-constexpr int PANEL_NB = 64;     // pivots per block of the large-front LU
-constexpr int PANEL_THREADS = 128;
 
 template <typename T>
 __global__ void fill_kernel(T *__restrict__ p, int64_t n, T v) {
@@ -150,12 +139,6 @@ __device__ __forceinline__ void front_body(int f, const DevPlan &P, T *F, T *LD,
     }
 }
 
-template <int SR, typename T>
-__global__ void front_small_kernel(const int *__restrict__ fronts, DevPlan P, T *LD, T *LL, T *UD, T *UL, T *W) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    front_body<SR, T, false>(fronts[blockIdx.x], P, reinterpret_cast<T *>(smem_raw), LD, LL, UD, UL, W);
-}
-
 // dense blocks: in-place LU of the star of count independent n x n blocks (sgetrf! per block)
 template <int SR, typename T>
 __global__ void getrf_batched_kernel(int n, T *A) {
@@ -169,114 +152,6 @@ __global__ void getrf_batched_kernel(int n, T *A) {
     for (int e = threadIdx.x; e < n2; e += blockDim.x) Ab[e] = F[e];
 }
 
-// ---------------------------------------------------------------- large fronts
-
-template <int SR, typename T>
-__global__ void extend_add_kernel(T *__restrict__ F, int ld, const T *__restrict__ M, int mld,
-                                  const int *__restrict__ rel, int nac) {
-    using S = Sem<SR, T>;
-    const int64_t tot = (int64_t)nac * nac;
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < tot; e += (int64_t)gridDim.x * blockDim.x) {
-        const int v = (int)(e % nac), w = (int)(e / nac);
-        const int64_t o = rel[v] + (int64_t)rel[w] * ld;
-        F[o] = S::add(F[o], M[v + (int64_t)w * mld]);
-    }
-}
-
-template <int SR, typename T>
-__global__ void combine_kernel(T *__restrict__ F, int nn, int na, int64_t Dp, int64_t Lp, const T *LD,
-                               const T *LL, const T *UD, const T *UL) {
-    const int nj = nn + na;
-    const int64_t tot = (int64_t)nj * nj;
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < tot; e += (int64_t)gridDim.x * blockDim.x) {
-        const int i = (int)(e % nj), j = (int)(e / nj);
-        F[e] = combine_entry<SR, T>(F[e], i, j, nn, na, Dp, Lp, LD, LL, UD, UL);
-    }
-}
-
-template <typename T>
-__global__ void extract_kernel(const T *__restrict__ F, int nn, int na, int64_t Dp, int64_t Lp, T *LD, T *LL,
-                               T *UD, T *UL) {
-    const int nj = nn + na;
-    const int64_t tot = (int64_t)nj * nn + (int64_t)nn * na;  // the first nn columns, then the first nn rows
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < tot; e += (int64_t)gridDim.x * blockDim.x) {
-        int i, j;
-        if (e < (int64_t)nj * nn) {
-            i = (int)(e % nj);
-            j = (int)(e / nj);
-        } else {
-            const int64_t r = e - (int64_t)nj * nn;
-            i = (int)(r % nn);
-            j = nn + (int)(r / nn);
-        }
-        store_entry<T>(F[i + (int64_t)j * nj], i, j, nn, na, Dp, Lp, LD, LL, UD, UL);
-    }
-}
-
-// One block step of the right-looking partial LU of a frontal matrix F (nj x nj, leading dimension ld):
-// every CTA factors the b x b diagonal block at (k, k) in shared memory (the same deterministic result);
-// CTA 0 writes it back, CTAs 1..nca solve row chunks of the column panel (x <- x U*, strsx2! :R :U :N) and the
-// rest column chunks of the row panel (x <- L* x, strsx2! :L :L :U).
-template <int SR, typename T>
-__global__ void __launch_bounds__(PANEL_THREADS) panel_kernel(T *__restrict__ F, int64_t ld, int nj, int k, int b,
-                                                                int nca) {
-    using S = Sem<SR, T>;
-    constexpr int NB = PANEL_NB;
-    __shared__ T D[NB * NB];
-    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
-        const int i = e % b, j = e / b;
-        D[i + j * NB] = F[(k + i) + (int64_t)(k + j) * ld];
-    }
-    __syncthreads();
-    lu_smem<SR, T>(D, NB, b, b);
-    const int g = blockIdx.x;
-    if (g == 0) {
-        for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
-            const int i = e % b, j = e / b;
-            F[(k + i) + (int64_t)(k + j) * ld] = D[i + j * NB];
-        }
-        return;
-    }
-    T x[NB];
-    if (g <= nca) {
-        const int r = k + b + (g - 1) * PANEL_THREADS + threadIdx.x;
-        if (r >= nj) return;
-#pragma unroll
-        for (int p = 0; p < NB; p++)
-            if (p < b) x[p] = F[r + (int64_t)(k + p) * ld];
-#pragma unroll
-        for (int p = 0; p < NB; p++) {
-            if (p < b) {
-                if (!S::integral) x[p] = S::mul(x[p], S::star(D[p + p * NB]));
-#pragma unroll
-                for (int q = p + 1; q < NB; q++)
-                    if (q < b) x[q] = S::muladd(x[p], D[p + q * NB], x[q]);
-            }
-        }
-#pragma unroll
-        for (int p = 0; p < NB; p++)
-            if (p < b) F[r + (int64_t)(k + p) * ld] = x[p];
-    } else {
-        const int c = k + b + (g - 1 - nca) * PANEL_THREADS + threadIdx.x;
-        if (c >= nj) return;
-        T *col = F + (int64_t)c * ld + k;
-#pragma unroll
-        for (int p = 0; p < NB; p++)
-            if (p < b) x[p] = col[p];
-#pragma unroll
-        for (int p = 0; p < NB; p++) {
-            if (p < b) {
-#pragma unroll
-                for (int q = p + 1; q < NB; q++)
-                    if (q < b) x[q] = S::muladd(D[q + p * NB], x[p], x[q]);
-            }
-        }
-#pragma unroll
-        for (int p = 0; p < NB; p++)
-            if (p < b) col[p] = x[p];
-    }
-}
-
 // ---------------------------------------------------------------- solves
 //
 // X[position][rhs] with leading dimension ldx (right-hand sides contiguous).  TRANS selects how the stored
@@ -284,135 +159,6 @@ __global__ void __launch_bounds__(PANEL_THREADS) panel_kernel(T *__restrict__ F,
 // transposed solves, B <- B U* and B <- B L* on the rows of B).  FWD is the forward sweep with the (+)-scatter
 // to the separator; otherwise the backward sweep gathering from it.  unit = diag :U (no star on the diagonal).
 
-template <int SR, typename T, bool FWD, bool TRANS>
-__global__ void __launch_bounds__(256) sweep_kernel(const int *__restrict__ fronts, DevPlan P,
-                                                    const T *__restrict__ Dv, const T *__restrict__ Ov,
-                                                    T *__restrict__ X, int64_t ldx, int k, int unit) {
-    using S = Sem<SR, T>;
-    constexpr int CH = SWEEP_CH, RPW = CH / 8;
-    __shared__ T xs[CH][33];
-    const int f = fronts[blockIdx.x];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int col = blockIdx.y * 32 + lane;
-    const bool ok = col < k;
-    const int rlo = P.rlo[f], nn = P.nn[f], na = P.na[f];
-    const T *D = Dv + P.dptr[f];
-    const T *O = Ov + P.lptr[f];
-    const int *sep = P.stgt + P.sptr[f];
-    T *Xc = X + (ok ? col : 0);
-    const T z = S::zero();
-    const bool scale = !unit && !S::integral;
-    auto Te = [&](int r, int c) -> T { return TRANS ? D[c + (int64_t)r * nn] : D[r + (int64_t)c * nn]; };
-    auto xg = [&](int row) -> T { return ok ? Xc[(int64_t)row * ldx] : z; };
-
-    if (FWD) {
-        for (int c0 = 0; c0 < nn; c0 += CH) {
-            const int c1 = min(c0 + CH, nn);
-            T acc[RPW];
-#pragma unroll
-            for (int t = 0; t < RPW; t++) {
-                const int r = c0 + w + 8 * t;
-                acc[t] = (r < c1) ? xg(rlo + r) : z;
-            }
-            for (int p = 0; p < c0; p++) {
-                const T xp = xg(rlo + p);
-#pragma unroll
-                for (int t = 0; t < RPW; t++) {
-                    const int r = c0 + w + 8 * t;
-                    if (r < c1) acc[t] = S::muladd(Te(r, p), xp, acc[t]);
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < RPW; t++) {
-                const int r = c0 + w + 8 * t;
-                if (r < c1) xs[r - c0][lane] = acc[t];
-            }
-            __syncthreads();
-            for (int p = c0; p < c1; p++) {
-                if (scale) {
-                    if (w == 0) xs[p - c0][lane] = S::mul(xs[p - c0][lane], S::star(Te(p, p)));
-                    __syncthreads();
-                }
-                const T xp = xs[p - c0][lane];
-                for (int q = p + 1 + w; q < c1; q += 8) xs[q - c0][lane] = S::muladd(Te(q, p), xp, xs[q - c0][lane]);
-                __syncthreads();
-            }
-            for (int r = c0 + w; r < c1; r += 8)
-                if (ok) Xc[(int64_t)(rlo + r) * ldx] = xs[r - c0][lane];
-            __syncthreads();
-        }
-        // separator: X[sep_i] <- X[sep_i] (+) (L21 x)_i
-        for (int i0 = w * 4; i0 < na; i0 += 32) {
-            T a4[4] = {z, z, z, z};
-            for (int p = 0; p < nn; p++) {
-                const T xp = (nn <= CH) ? xs[p][lane] : xg(rlo + p);
-#pragma unroll
-                for (int t = 0; t < 4; t++) {
-                    const int i = i0 + t;
-                    if (i < na) {
-                        const T o = TRANS ? O[p + (int64_t)i * nn] : O[i + (int64_t)p * na];
-                        a4[t] = S::muladd(o, xp, a4[t]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const int i = i0 + t;
-                if (i < na && ok) S::atomic_add(Xc + (int64_t)sep[i] * ldx, a4[t]);
-            }
-        }
-    } else {
-        for (int c1 = nn; c1 > 0; c1 -= CH) {
-            const int c0 = max(0, c1 - CH);
-            T acc[RPW];
-#pragma unroll
-            for (int t = 0; t < RPW; t++) {
-                const int r = c0 + w + 8 * t;
-                acc[t] = (r < c1) ? xg(rlo + r) : z;
-            }
-            for (int i = 0; i < na; i++) {
-                const T xi = xg(sep[i]);
-#pragma unroll
-                for (int t = 0; t < RPW; t++) {
-                    const int r = c0 + w + 8 * t;
-                    if (r < c1) {
-                        const T o = TRANS ? O[i + (int64_t)r * na] : O[r + (int64_t)i * nn];
-                        acc[t] = S::muladd(o, xi, acc[t]);
-                    }
-                }
-            }
-            for (int p = nn - 1; p >= c1; p--) {
-                const T xp = xg(rlo + p);
-#pragma unroll
-                for (int t = 0; t < RPW; t++) {
-                    const int r = c0 + w + 8 * t;
-                    if (r < c1) acc[t] = S::muladd(Te(r, p), xp, acc[t]);
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < RPW; t++) {
-                const int r = c0 + w + 8 * t;
-                if (r < c1) xs[r - c0][lane] = acc[t];
-            }
-            __syncthreads();
-            for (int p = c1 - 1; p >= c0; p--) {
-                if (scale) {
-                    if (w == 0) xs[p - c0][lane] = S::mul(S::star(Te(p, p)), xs[p - c0][lane]);
-                    __syncthreads();
-                }
-                const T xp = xs[p - c0][lane];
-                for (int q = c0 + w; q < p; q += 8) xs[q - c0][lane] = S::muladd(Te(q, p), xp, xs[q - c0][lane]);
-                __syncthreads();
-            }
-            for (int r = c0 + w; r < c1; r += 8)
-                if (ok) Xc[(int64_t)(rlo + r) * ldx] = xs[r - c0][lane];
-            __syncthreads();
-        }
-    }
-}
-
-// lmul!: after the solve of a component, X[i] <- X[i] (+) N[i, j] (x) X[j] for its positions j
-// (sgemx_sparse_st!, src/CPU/sparse/sgemx.jl:193-213); a warp per position, atomics as several j share rows i
 template <int SR, typename T>
 __global__ void coupling_scatter_kernel(const int *__restrict__ js, int cnt, DevPlan P, const T *__restrict__ Nval,
                                         T *X, int64_t ldx, int k) {

@@ -1,11 +1,10 @@
 // engine_host.cuh — host drivers of the device kernels, templated on the semiring; instantiated once per
 // (semiring, element type) in ops_*.cu.
 //
-// Factorization: one persistent launch for the bottom of the tree (factor_bottom_kernel), then the remaining
-// levels bottom-up: a front_small_kernel launch per size class, and the large fronts of the level on
-// concurrent streams (diag_lu_kernel, panel_solve_kernel and the trailing GEMM per 64-pivot block).
-// Solves: per coupling stage, the bottom fronts in one persistent launch per direction and the rest level by
-// level with sweep_kernel.
+// Factorization: one persistent launch for the bottom of the tree (factor_bottom_kernel), then one for the
+// rest (factor_top_kernel, tile tasks).  Solves: per coupling stage, the subtrees that fit shared memory and
+// the other bottom fronts in one persistent launch each per direction, the rest level by level with
+// sweep_tiled_kernel.
 #pragma once
 
 #include <algorithm>
@@ -13,6 +12,7 @@
 #include "ops.h"
 #include "persist.cuh"
 #include "sweep_tiled.cuh"
+#include "top.cuh"
 
 namespace pp {
 
@@ -56,15 +56,13 @@ struct Engine {
         return cudaGetLastError();
     }
 
-    static int threads_for(int nj) { return nj <= 16 ? 64 : (nj <= 32 ? 128 : 256); }
-
     static cudaError_t set_attrs() {
         int dev = 0;
         cudaGetDevice(&dev);
         static bool attr[64] = {};
         if (dev < 64 && !attr[dev]) {
-            PP_TRY(cudaFuncSetAttribute(front_small_kernel<SR, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)SMALL_FRONT_SMEM));
+            PP_TRY(cudaFuncSetAttribute(factor_top_kernel<SR, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)factor_top_smem<T>()));
             PP_TRY(cudaFuncSetAttribute(factor_bottom_kernel<SR, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)SMALL_FRONT_SMEM));
             attr[dev] = true;
@@ -73,9 +71,9 @@ struct Engine {
     }
 
     // the error word of a persistent launch: a bounded wait expired
-    static cudaError_t check_err(const HostPlan &hp, cudaStream_t st) {
+    static cudaError_t check_err(const int *word, cudaStream_t st) {
         int err = 0;
-        PP_TRY(cudaMemcpyAsync(&err, hp.d_sync + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
+        PP_TRY(cudaMemcpyAsync(&err, word, sizeof(int), cudaMemcpyDeviceToHost, st));
         PP_TRY(cudaStreamSynchronize(st));
         return err ? cudaErrorLaunchTimeout : cudaSuccess;
     }
@@ -105,99 +103,23 @@ struct Engine {
             PP_TRY(cudaGetLastError());
             if (pi >= 0) hp.prof->end(pi, st, hp.fb_bytes, hp.fb_pairs);
             nl++;
-            PP_TRY(check_err(hp, st));
+            PP_TRY(check_err(hp.d_sync + 1, st));
         }
-        const int naux = (int)hp.aux.size();
-        for (const Level &L : hp.flevels) {
-            int nlarge = 0;
-            for (const FrontGroup &g : L.groups) {
-                if (!g.large) {
-                    const size_t smem = (size_t)g.max_nj * g.max_nj * sizeof(T);
-                    const int pi = hp.prof ? hp.prof->begin(K_FRONT, st) : -1;
-                    front_small_kernel<SR, T><<<g.count, threads_for(g.max_nj), smem, st>>>(
-                        hp.d_ffronts + g.off, hp.dev, LD, LL, UD, UL, W);
-                    PP_TRY(cudaGetLastError());
-                    if (pi >= 0) hp.prof->end(pi, st, g.bytes, g.pairs);
-                    nl++;
-                    continue;
-                }
-                // the large fronts of the level are independent: spread them over the auxiliary streams
-                if (naux > 0) PP_TRY(cudaEventRecord(hp.levev, st));
-                for (int t = 0; t < g.count; t++) {
-                    cudaStream_t s = st;
-                    if (naux > 0) {
-                        s = hp.aux[t % naux];
-                        if (t < naux) PP_TRY(cudaStreamWaitEvent(s, hp.levev, 0));
-                    }
-                    PP_TRY(factor_large(hp, hp.h_ffronts[g.off + t], LD, LL, UD, UL, W, s, &nl));
-                }
-                nlarge = g.count;
-            }
-            for (int j = 0; j < std::min(nlarge, naux); j++) {
-                PP_TRY(cudaEventRecord(hp.auxev[j], hp.aux[j]));
-                PP_TRY(cudaStreamWaitEvent(st, hp.auxev[j], 0));
-            }
+        if (hp.top_ntasks > 0) {
+            constexpr size_t smem = factor_top_smem<T>();
+            PP_TRY(cudaMemsetAsync(hp.d_tflags, 0, sizeof(int) * (size_t)hp.tflags_n, st));
+            int per_sm = 1;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, factor_top_kernel<SR, T>, 256, smem);
+            const int grid = std::max(1, std::min(hp.top_ntasks, std::max(per_sm, 1) * hp.sm_count));
+            const int pi = hp.prof ? hp.prof->begin(K_FACTOR_TOP, st) : -1;
+            factor_top_kernel<SR, T><<<grid, 256, smem, st>>>(hp.d_ttasks, hp.top_ntasks, hp.dev, hp.d_tfoff, LD, LL,
+                                                              UD, UL, W, hp.d_tflags);
+            PP_TRY(cudaGetLastError());
+            if (pi >= 0) hp.prof->end(pi, st, hp.top_cost.bytes, hp.top_cost.pairs);
+            nl++;
+            PP_TRY(check_err(hp.d_tflags + 1, st));
         }
         if (launches) *launches += nl;
-        return cudaSuccess;
-    }
-
-    static cudaError_t factor_large(const HostPlan &hp, int f, T *LD, T *LL, T *UD, T *UL, T *W, cudaStream_t st,
-                                    int64_t *nl) {
-        const int nn = hp.nn[f], na = hp.na[f], nj = nn + na;
-        T *F = W + hp.fws[f];
-        const int64_t nj2 = (int64_t)nj * nj;
-        Profiler *pr = hp.prof;
-        int pi = pr ? pr->begin(K_LARGE_AUX, st) : -1;
-        PP_TRY(fill_zero(F, nj2, st));
-        (*nl)++;
-        double aux = (double)nj2;
-        for (int c = hp.chdptr[f + 1] - 1; c >= hp.chdptr[f]; c--) {
-            const int ch = hp.chdtgt[c];
-            const int nac = hp.na[ch];
-            extend_add_kernel<SR, T><<<grid_for((int64_t)nac * nac, 256), 256, 0, st>>>(
-                F, nj, W + hp.mptr[ch], hp.mld[ch], hp.d_rel + hp.sptr[ch], nac);
-            PP_TRY(cudaGetLastError());
-            (*nl)++;
-            aux += 3.0 * nac * nac;
-        }
-        combine_kernel<SR, T><<<grid_for(nj2, 256), 256, 0, st>>>(F, nn, na, hp.dptr[f], hp.lptr[f], LD, LL, UD, UL);
-        PP_TRY(cudaGetLastError());
-        (*nl)++;
-        aux += 2.0 * nj2 + 2.0 * nn * nn + 2.0 * nn * na;
-        if (pi >= 0) pr->end(pi, st, aux, 0);
-        for (int k = 0; k < nn; k += PANEL_NB) {
-            const int b = std::min(PANEL_NB, nn - k);
-            const int rem = nj - k - b;
-            pi = pr ? pr->begin(K_PANEL, st) : -1;
-            diag_lu_kernel<SR, T><<<1, 256, 0, st>>>(F, nj, k, b);
-            PP_TRY(cudaGetLastError());
-            (*nl)++;
-            if (rem > 0) {
-                const int nrow = (rem + 7) / 8;
-                panel_solve_kernel<SR, T><<<2 * nrow, 256, 0, st>>>(F, nj, nj, k, b, nrow);
-                PP_TRY(cudaGetLastError());
-                (*nl)++;
-            }
-            if (pi >= 0)
-                pr->end(pi, st, 2.0 * b * b + 4.0 * rem * b,
-                        (double)(b - 1) * b * (2.0 * b - 1) / 6 + (double)rem * b * (b - 1));
-            if (rem > 0) {
-                T *C = F + (k + b) + (int64_t)(k + b) * nj;
-                const T *A = F + (k + b) + (int64_t)k * nj;
-                const T *B = F + k + (int64_t)(k + b) * nj;
-                pi = pr ? pr->begin(K_GEMM, st) : -1;
-                PP_TRY((launch_gemm<SR, T>(rem, rem, b, C, nj, A, nj, B, nj, st)));
-                if (pi >= 0) pr->end(pi, st, 2.0 * rem * b + 2.0 * rem * (double)rem, (double)rem * rem * b);
-                (*nl)++;
-            }
-        }
-        pi = pr ? pr->begin(K_LARGE_AUX, st) : -1;
-        extract_kernel<T><<<grid_for((int64_t)nj * nn + (int64_t)nn * na, 256), 256, 0, st>>>(
-            F, nn, na, hp.dptr[f], hp.lptr[f], LD, LL, UD, UL);
-        PP_TRY(cudaGetLastError());
-        if (pi >= 0) pr->end(pi, st, 2.0 * ((double)nj * nn + (double)nn * na), 0);
-        (*nl)++;
         return cudaSuccess;
     }
 
@@ -251,7 +173,7 @@ struct Engine {
             hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
                          (double)k * cost.pairs_col);
         (*nl)++;
-        return check_err(hp, st);
+        return check_err(hp.d_sync + 1, st);
     }
 
     template <bool FWD, bool TRANS>

@@ -11,9 +11,8 @@
 namespace pp {
 
 // Kernel classes the profiler separates.
-enum KClass { K_FRONT = 0, K_LARGE_AUX, K_PANEL, K_GEMM, K_SWEEP_FWD, K_SWEEP_BWD, K_COUPLING, K_PERMUTE, K_ASSEMBLE,
-              K_FRONT_BOTTOM, K_SWEEP_FWD_BOTTOM, K_SWEEP_BWD_BOTTOM, K_SWEEP_FWD_SUBTREE, K_SWEEP_BWD_SUBTREE,
-              K_NCLASS };
+enum KClass { K_FACTOR_TOP = 0, K_SWEEP_FWD, K_SWEEP_BWD, K_COUPLING, K_PERMUTE, K_ASSEMBLE, K_FRONT_BOTTOM,
+              K_SWEEP_FWD_BOTTOM, K_SWEEP_BWD_BOTTOM, K_SWEEP_FWD_SUBTREE, K_SWEEP_BWD_SUBTREE, K_NCLASS };
 extern const char *const KCLASS_NAMES[K_NCLASS];
 
 // Optional per-launch timing with CUDA events on the launching stream; off unless pp_set_profile enabled it.
@@ -92,10 +91,13 @@ struct HostPlan {
     std::vector<int64_t> mptr, fws;
     std::vector<int> mld;
     int64_t ws_elems = 0;
-    // factorization schedule: tree levels by height, each split into size classes
-    std::vector<Level> flevels;
-    std::vector<int> h_ffronts;
-    const int *d_ffronts = nullptr;
+    // top of the tree: the tile tasks of the persistent factorization (top.cuh), fronts by height
+    int top_ntasks = 0;
+    const int4 *d_ttasks = nullptr;   // (front, I, J, kind: 0 = assembly of column block J, 1 = tile)
+    const int64_t *d_tfoff = nullptr;  // per front: first of its flags in d_tflags
+    int *d_tflags = nullptr;           // [0] task counter, [1] error word, then the fronts' flags
+    int64_t tflags_n = 0;
+    Cost top_cost;
     int64_t nN = 0;
     // solve schedules (lmul: components after their coupling successors; rmul: after their predecessors)
     std::vector<Stage> lstages, rstages;
@@ -121,10 +123,6 @@ struct HostPlan {
     const int *d_sdone0 = nullptr;     // 1 for fronts outside the bottom, 0 inside (backward flags)
     int *d_sync = nullptr;             // scratch: [0] task counter, [1] error word, [16, 16 + nf * tiles) counters
     int64_t sync_cap = 0;              // ints allocated at d_sync
-    // concurrency for the large fronts of one level
-    std::vector<cudaStream_t> aux;
-    std::vector<cudaEvent_t> auxev;
-    cudaEvent_t levev = nullptr;
     int sm_count = 148;
 };
 
@@ -135,7 +133,7 @@ struct Values {
 struct Ops {
     int sr, dt;
     size_t esize;
-    int small_limit;  // largest nn + na of a front factored in shared memory
+    int small_limit;  // largest block of pp_getrf_batched (shared memory)
     cudaError_t (*fill_zero)(void *p, int64_t n, cudaStream_t st);
     cudaError_t (*assemble)(const HostPlan &hp, const int *colptr, const int *rowval, const void *nzval,
                             const Values &v, cudaStream_t st);
@@ -158,7 +156,7 @@ struct Ops {
 
 const Ops *get_ops(int sr, int dt);
 
-// shared-memory budget of the one-CTA front kernel
+// shared-memory budget of the one-CTA dense LU of pp_getrf_batched
 constexpr size_t SMALL_FRONT_SMEM = 160 * 1024;
 
 }  // namespace pp

@@ -1,5 +1,4 @@
-// persist.cuh — dependency-driven kernels for the bottom of the elimination tree, and the panel kernels of
-// the large-front LU.
+// persist.cuh — dependency-driven kernels for the bottom of the elimination tree.
 //
 // The bottom of the tree (the fronts whose whole subtree is small) is processed by ONE persistent launch per
 // sweep instead of one launch per tree level: CTAs take fronts from a work list ordered by height (children
@@ -43,7 +42,9 @@ __device__ __forceinline__ bool cta_wait(const int *p, bool for_zero, int *err) 
         s_ok = ok;
     }
     __syncthreads();
-    return s_ok != 0;
+    const bool res = s_ok != 0;
+    __syncthreads();  // s_ok is reused by the next wait
+    return res;
 }
 
 __device__ __forceinline__ int cta_take(int *next) {
@@ -84,7 +85,7 @@ __global__ void __launch_bounds__(128) factor_bottom_kernel(const int *__restric
 // residual (nn <= SWEEP_NNW) lives in registers, so the triangular solve needs no barrier.  Element reads of
 // the factor blocks are warp-uniform (broadcast).  FWD: wait for the children (counter), solve, (+)-scatter
 // to the separator with atomics, signal the parent.  Backward: wait for the parent's flag, gather from the
-// separator, solve, set the front's flag.  Same per-element dataflow as sweep_kernel.
+// separator, solve, set the front's flag.  Same per-element dataflow as sweep_tiled_kernel.
 
 template <int SR, typename T, bool FWD, bool TRANS>
 __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &P, const T *__restrict__ Dv,
@@ -292,74 +293,6 @@ static __global__ void init_flags_kernel(int *flags, const int *init, int nf, in
     const int64_t tot = (int64_t)nf * ntiles;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < tot; i += (int64_t)gridDim.x * blockDim.x)
         flags[i] = init[i % nf];
-}
-
-// ---------------------------------------------------------------- panels of the large-front LU
-
-// LU of the b x b diagonal block at (k, k) of F in shared memory, written back (one CTA).
-template <int SR, typename T>
-__global__ void __launch_bounds__(256) diag_lu_kernel(T *__restrict__ F, int64_t ld, int k, int b) {
-    constexpr int NB = PANEL_NB;
-    __shared__ T D[NB * NB];
-    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
-        const int i = e % b, j = e / b;
-        D[i + j * NB] = F[(k + i) + (int64_t)(k + j) * ld];
-    }
-    __syncthreads();
-    lu_smem<SR, T>(D, NB, b, b);
-    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
-        const int i = e % b, j = e / b;
-        F[(k + i) + (int64_t)(k + j) * ld] = D[i + j * NB];
-    }
-}
-
-// The column panel (rows k+b .. nj-1 of columns k .. k+b-1: x <- x U*, strsx2! :R :U :N) and the row panel
-// (columns k+b .. nj-1 of rows k .. k+b-1: x <- L* x, strsx2! :L :L :U) against the factored diagonal block.
-// A warp per panel row (or column): lane l holds x[l] and x[l + 32]; pivot p's final value is broadcast by a
-// shuffle from its lane, and every lane updates its own later entries, so the pivot loop needs no barrier.
-// CTAs 0 .. nrow-1 take 8 rows each, the rest 8 columns each.
-template <int SR, typename T>
-__global__ void __launch_bounds__(256) panel_solve_kernel(T *__restrict__ F, int64_t ld, int nj, int k, int b,
-                                                          int nrow) {
-    using S = Sem<SR, T>;
-    constexpr int NB = PANEL_NB;
-    __shared__ T D[NB * NB];
-    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
-        const int i = e % b, j = e / b;
-        D[i + j * NB] = F[(k + i) + (int64_t)(k + j) * ld];
-    }
-    __syncthreads();
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const bool rowp = (int)blockIdx.x < nrow;
-    const int idx = k + b + ((rowp ? blockIdx.x : blockIdx.x - nrow) * 8 + w);
-    if (idx >= nj) return;
-    const int q0 = lane, q1 = lane + 32;
-    T x0 = S::zero(), x1 = S::zero();
-    if (rowp) {
-        if (q0 < b) x0 = F[idx + (int64_t)(k + q0) * ld];
-        if (q1 < b) x1 = F[idx + (int64_t)(k + q1) * ld];
-        for (int p = 0; p < b; p++) {
-            T xp = __shfl_sync(0xffffffffu, p < 32 ? x0 : x1, p & 31);
-            if (!S::integral) xp = S::mul(xp, S::star(D[p + p * NB]));
-            if (p == q0) x0 = xp;
-            if (p == q1) x1 = xp;
-            if (q0 > p && q0 < b) x0 = S::muladd(xp, D[p + q0 * NB], x0);
-            if (q1 > p && q1 < b) x1 = S::muladd(xp, D[p + q1 * NB], x1);
-        }
-        if (q0 < b) F[idx + (int64_t)(k + q0) * ld] = x0;
-        if (q1 < b) F[idx + (int64_t)(k + q1) * ld] = x1;
-    } else {
-        T *col = F + (int64_t)idx * ld + k;
-        if (q0 < b) x0 = col[q0];
-        if (q1 < b) x1 = col[q1];
-        for (int p = 0; p < b; p++) {
-            const T xp = __shfl_sync(0xffffffffu, p < 32 ? x0 : x1, p & 31);
-            if (q0 > p && q0 < b) x0 = S::muladd(D[q0 + p * NB], xp, x0);
-            if (q1 > p && q1 < b) x1 = S::muladd(D[q1 + p * NB], xp, x1);
-        }
-        if (q0 < b) col[q0] = x0;
-        if (q1 < b) col[q1] = x1;
-    }
 }
 
 }  // namespace pp

@@ -12,6 +12,8 @@ namespace pp {
 constexpr int SWEEP_NNW = 16;
 // rows (residual range + root separator) of a subtree solved in shared memory by one warp
 constexpr int SUBTREE_ROWS = 96;
+// tile edge of the persistent factorization of the top of the tree
+constexpr int TOP_TILE = 64;
 
 // Device arrays of a structure (0-based, positions = permuted labels).  Per front f: the residual is
 // rlo[f] .. rlo[f]+nn[f]-1, the separator stgt[sptr[f] .. sptr[f+1]-1] with rel[] its positions in the
@@ -26,7 +28,7 @@ struct DevPlan {
     const int *chdptr, *chdtgt;
     const int64_t *mptr;
     const int *mld;
-    const int64_t *fws;  // frontal matrix of a large front (elements), -1 for small fronts
+    const int64_t *fws;  // frontal matrix of a top front (elements), -1 for the bottom fronts
     const int64_t *nptr;
     const int *ntgt;
     const int *perm, *invp, *idx, *bptr, *fcc;
@@ -39,13 +41,9 @@ struct SubtreeList {
     int count = 0;
 };
 
-// A group of fronts launched together: one size class of one tree level.
-struct FrontGroup {
-    int64_t off;   // offset into the device front list
-    int count;
-    int max_nj;    // largest nn + na in the group
-    bool large;    // blocked path, one front at a time
-    double bytes = 0, pairs = 0;  // algorithmic traffic (element count) and (x)(+) pairs of the group's launch
+// Algorithmic traffic (element count) and (x)(+) pairs of a set of fronts' factorization (profiler).
+struct Cost {
+    double bytes = 0, pairs = 0;
 };
 
 // One tree level of a solve stage: fronts d_sfronts[off .. off+count), with the per-right-hand-side sums the
@@ -54,10 +52,6 @@ struct SLevel {
     int64_t off = 0;
     int count = 0;
     double res_rows = 0, sep_rows = 0, blk_elems = 0, pairs_col = 0;
-};
-
-struct Level {
-    std::vector<FrontGroup> groups;
 };
 
 // Solve schedule of one stage: components whose coupling predecessors (rmul) or successors (lmul) are all

@@ -45,8 +45,8 @@ const Ops *get_ops(int sr, int dt) {
 }  // namespace pp
 
 namespace pp {
-const char *const KCLASS_NAMES[K_NCLASS] = {"factor_top_kernel", "sweep_tiled_kernel(fwd)",
-                                            "sweep_tiled_kernel(bwd)", "coupling", "permute", "assemble_kernel",
+const char *const KCLASS_NAMES[K_NCLASS] = {"factor_top_kernel", "sweep_top_kernel(fwd)",
+                                            "sweep_top_kernel(bwd)", "coupling", "permute", "assemble_kernel",
                                             "factor_bottom_kernel", "sweep_bottom_kernel(fwd)",
                                             "sweep_bottom_kernel(bwd)", "sweep_subtree_kernel(fwd)",
                                             "sweep_subtree_kernel(bwd)"};
@@ -93,8 +93,9 @@ struct pp_handle {
     // device structure
     DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
         d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_sfronts, d_sverts, d_pnt, d_fbottom,
-        d_fpending0, d_spending0, d_sdone0, d_sync, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags;
-    std::vector<int> pnt, height;
+        d_fpending0, d_spending0, d_sdone0, d_tpending0, d_sync, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags, d_croff,
+        d_crng;
+    std::vector<int> pnt, height, rel;
     int maxh = 0;
     // values and work
     DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val;
@@ -386,16 +387,19 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 }
             }
         }
-        std::vector<int> spending0(nf, 0), sdone0(nf, 1);
+        std::vector<int> spending0(nf, 0), sdone0(nf, 1), tpending0(nf, 0);
         for (int64_t f = 0; f < nf; f++) {
             const bool mid = sbot[f] && !covered[f];
             if (mid) sdone0[f] = 0;
             if (mid && pnt[f] >= 0) spending0[pnt[f]]++;
+            if (!sbot[f] && pnt[f] >= 0) tpending0[pnt[f]]++;  // top children (the top sweep's counters)
         }
         auto build_stages = [&](const std::vector<int> &stage_of, std::vector<Stage> &out, std::vector<int> &sfronts,
                                 std::vector<int> &sverts, std::vector<std::pair<int64_t, int>> &bfwd,
                                 std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost,
-                                std::vector<SubtreeList> &subs, std::vector<int> &sroots) {
+                                std::vector<SubtreeList> &subs, std::vector<int> &sroots,
+                                std::vector<std::pair<int64_t, int>> &tfwd, std::vector<std::pair<int64_t, int>> &tbwd,
+                                std::vector<SLevel> &tcost) {
             int ns = 0;
             for (int64_t c = 0; c < nB; c++) ns = std::max(ns, stage_of[c] + 1);
             if (nB == 0) ns = 0;
@@ -406,6 +410,9 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
             bbwd.clear();
             bcost.clear();
             subs.clear();
+            tfwd.clear();
+            tbwd.clear();
+            tcost.clear();
             for (int s = 0; s < ns; s++) {
                 Stage sg;
                 std::vector<std::vector<int>> byh(maxh + 1), bot(maxh + 1);
@@ -441,21 +448,27 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 bfwd.push_back(fw);
                 bbwd.push_back(bw);
                 bcost.push_back(bc);
-                for (int hh = 0; hh <= maxh; hh++) {
-                    if (byh[hh].empty()) continue;
-                    SLevel lv;
-                    lv.off = (int64_t)sfronts.size();
-                    lv.count = (int)byh[hh].size();
+                // the top fronts: one work list per direction (height ascending / descending)
+                SLevel tc;
+                std::pair<int64_t, int> tf{(int64_t)sfronts.size(), 0};
+                for (int hh = 0; hh <= maxh; hh++)
                     for (int f : byh[hh]) {
+                        sfronts.push_back(f);
                         const double nn = hp.nn[f], na = hp.na[f];
-                        lv.res_rows += nn;
-                        lv.sep_rows += na;
-                        lv.blk_elems += nn * nn + nn * na;
-                        lv.pairs_col += nn * (nn - 1) / 2 + nn * na;
+                        tc.count++;
+                        tc.res_rows += nn;
+                        tc.sep_rows += na;
+                        tc.blk_elems += nn * nn + nn * na;
+                        tc.pairs_col += nn * (nn - 1) / 2 + nn * na;
                     }
-                    sg.levels.push_back(lv);
-                    sfronts.insert(sfronts.end(), byh[hh].begin(), byh[hh].end());
-                }
+                tf.second = (int)(sfronts.size() - tf.first);
+                std::pair<int64_t, int> tb{(int64_t)sfronts.size(), 0};
+                for (int hh = maxh; hh >= 0; hh--)
+                    for (int f : byh[hh]) sfronts.push_back(f);
+                tb.second = (int)(sfronts.size() - tb.first);
+                tfwd.push_back(tf);
+                tbwd.push_back(tb);
+                tcost.push_back(tc);
                 sg.voff = (int64_t)sverts.size();
                 for (int c : comps[s])
                     for (int64_t j = Bp[c]; j < Bp[c + 1]; j++)
@@ -466,9 +479,11 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
             }
         };
         std::vector<int> sfronts, sverts, sroots;
-        build_stages(lstage, hp.lstages, sfronts, sverts, hp.sb_fwd, hp.sb_bwd, hp.sb_cost_l, hp.sub_l, sroots);
+        build_stages(lstage, hp.lstages, sfronts, sverts, hp.sb_fwd, hp.sb_bwd, hp.sb_cost_l, hp.sub_l, sroots,
+                     hp.st_fwd, hp.st_bwd, hp.st_cost_l);
         // rmul stages: the gather concerns the stage's own columns j (rows of earlier components feed them)
-        build_stages(rstage, hp.rstages, sfronts, sverts, hp.sb_fwd_r, hp.sb_bwd_r, hp.sb_cost_r, hp.sub_r, sroots);
+        build_stages(rstage, hp.rstages, sfronts, sverts, hp.sb_fwd_r, hp.sb_bwd_r, hp.sb_cost_r, hp.sub_r, sroots,
+                     hp.st_fwd_r, hp.st_bwd_r, hp.st_cost_r);
         (void)ccoupled;
         std::vector<int64_t> Np64(Np.begin(), Np.end());
         // device uploads
@@ -498,6 +513,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         CK(h, upload(h->d_slot, slot, st), "upload");
         CK(h, upload(h->d_spending0, spending0, st), "upload");
         CK(h, upload(h->d_sdone0, sdone0, st), "upload");
+        CK(h, upload(h->d_tpending0, tpending0, st), "upload");
         CK(h, h->d_sync.ensure(sizeof(int) * (32 * nf + 16)), "upload");
         CK(h, cudaStreamSynchronize(st), "upload");
         DevPlan &d = hp.dev;
@@ -533,12 +549,14 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         hp.d_fdsc = h->d_fdsc.as<int>();
         hp.d_slot = h->d_slot.as<int>();
         hp.d_sdone0 = h->d_sdone0.as<int>();
+        hp.d_tpending0 = h->d_tpending0.as<int>();
         hp.d_sync = h->d_sync.as<int>();
         hp.sync_cap = 32 * nf + 16;
         hp.sm_count = h->sm_count;
         h->invp = invp;
         h->pnt = pnt;
-        h->height = height;  // factorization heights, kept for prepare_workspace
+        h->height = height;  // factorization heights and rel, kept for prepare_workspace
+        h->rel = rel;
         h->maxh = maxh;
         h->hp = std::move(hp);
         h->hp.mld.clear();
@@ -592,7 +610,7 @@ static void front_cost(const HostPlan &hp, int f, Cost &g) {
 // of shared memory whose whole subtree is such) is one persistent launch, front by front; each bottom front
 // keeps a compact na x na update matrix.  Every other front keeps its whole nj x nj frontal matrix (its update
 // matrix is the trailing block, read in place by the parent) and is factored by the tile tasks of top.cuh:
-// per front, by height, the assembly of each column block and then the tiles in (min(I, J), max(I, J)) order.
+// per front, by height, its tiles in (min(I, J), max(I, J)) order.
 static int32_t prepare_workspace(pp_handle *h) {
     HostPlan &hp = h->hp;
     if (h->ws_esize == h->ops->esize && !hp.mld.empty()) return PP_OK;
@@ -651,17 +669,29 @@ static int32_t prepare_workspace(pp_handle *h) {
         std::vector<std::vector<int>> byh(maxh + 1);
         for (int f = 0; f < nf; f++)
             if (!fbot[f]) byh[h->height[f]].push_back(f);
-        std::vector<int> tasks;
-        std::vector<int64_t> foff(nf, 0);
+        std::vector<int> tasks, crng;
+        std::vector<int64_t> foff(nf, 0), croff(std::max<size_t>(hp.chdtgt.size(), 1), 0);
         int64_t nflags = 16;
         Cost acc;
         std::vector<std::pair<int, int>> tiles;
+        std::vector<int> bounds;
         for (int hh = 0; hh <= maxh; hh++)
             for (int f : byh[hh]) {
-                const int kb = (hp.nn[f] + TOP_TILE - 1) / TOP_TILE, nbt = kb + (hp.na[f] + TOP_TILE - 1) / TOP_TILE;
+                const int nn = hp.nn[f], na = hp.na[f];
+                const int kb = (nn + TOP_TILE - 1) / TOP_TILE, nbt = kb + (na + TOP_TILE - 1) / TOP_TILE;
                 foff[f] = nflags;
-                nflags += nbt + (int64_t)nbt * nbt + 1;
-                for (int J = 0; J < nbt; J++) tasks.insert(tasks.end(), {f, 0, J, 0});
+                nflags += (int64_t)nbt * nbt + 1;
+                // tile block boundaries of the front, and where each child's separator crosses them
+                bounds.clear();
+                for (int b = 0; b < kb; b++) bounds.push_back(b * TOP_TILE);
+                for (int b = kb; b < nbt; b++) bounds.push_back(nn + (b - kb) * TOP_TILE);
+                bounds.push_back(nn + na);
+                for (int c = hp.chdptr[f]; c < hp.chdptr[f + 1]; c++) {
+                    const int ch = hp.chdtgt[c];
+                    const int *r0 = h->rel.data() + hp.sptr[ch], *r1 = r0 + hp.na[ch];
+                    croff[c] = (int64_t)crng.size();
+                    for (int b : bounds) crng.push_back((int)(std::lower_bound(r0, r1, b) - r0));
+                }
                 tiles.clear();
                 for (int I = 0; I < nbt; I++)
                     for (int J = 0; J < nbt; J++) tiles.push_back({I, J});
@@ -671,7 +701,7 @@ static int32_t prepare_workspace(pp_handle *h) {
                     if (a0 != b0) return a0 < b0;
                     return std::max(a.first, a.second) < std::max(b.first, b.second);
                 });
-                for (const auto &t : tiles) tasks.insert(tasks.end(), {f, t.first, t.second, 1});
+                for (const auto &t : tiles) tasks.insert(tasks.end(), {f, t.first, t.second, 0});
                 front_cost(hp, f, acc);
             }
         hp.top_ntasks = (int)(tasks.size() / 4);
@@ -680,9 +710,13 @@ static int32_t prepare_workspace(pp_handle *h) {
         if (tasks.empty()) tasks.assign(4, 0);
         CK(h, upload(h->d_ttasks, tasks, st), "upload");
         CK(h, upload(h->d_tfoff, foff, st), "upload");
+        CK(h, upload(h->d_croff, croff, st), "upload");
+        CK(h, upload(h->d_crng, crng, st), "upload");
         CK(h, h->d_tflags.ensure(sizeof(int) * (size_t)nflags), "upload");
         hp.d_ttasks = reinterpret_cast<const int4 *>(h->d_ttasks.p);
         hp.d_tfoff = h->d_tfoff.as<int64_t>();
+        hp.d_croff = h->d_croff.as<int64_t>();
+        hp.d_crng = h->d_crng.as<int>();
         hp.d_tflags = h->d_tflags.as<int>();
     }
     CK(h, upload(h->d_mptr, hp.mptr, st), "upload");

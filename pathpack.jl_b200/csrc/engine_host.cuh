@@ -2,16 +2,15 @@
 // (semiring, element type) in ops_*.cu.
 //
 // Factorization: one persistent launch for the bottom of the tree (factor_bottom_kernel), then one for the
-// rest (factor_top_kernel, tile tasks).  Solves: per coupling stage, the subtrees that fit shared memory and
-// the other bottom fronts in one persistent launch each per direction, the rest level by level with
-// sweep_tiled_kernel.
+// rest (factor_top_kernel, tile tasks).  Solves: per coupling stage and direction, one persistent launch each
+// for the subtrees that fit shared memory, the other bottom fronts and the top fronts (sweep_top_kernel).
 #pragma once
 
 #include <algorithm>
 
 #include "ops.h"
 #include "persist.cuh"
-#include "sweep_tiled.cuh"
+#include "sweep_top.cuh"
 #include "top.cuh"
 
 namespace pp {
@@ -112,8 +111,8 @@ struct Engine {
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, factor_top_kernel<SR, T>, 256, smem);
             const int grid = std::max(1, std::min(hp.top_ntasks, std::max(per_sm, 1) * hp.sm_count));
             const int pi = hp.prof ? hp.prof->begin(K_FACTOR_TOP, st) : -1;
-            factor_top_kernel<SR, T><<<grid, 256, smem, st>>>(hp.d_ttasks, hp.top_ntasks, hp.dev, hp.d_tfoff, LD, LL,
-                                                              UD, UL, W, hp.d_tflags);
+            factor_top_kernel<SR, T><<<grid, 256, smem, st>>>(hp.d_ttasks, hp.top_ntasks, hp.dev, hp.d_tfoff,
+                                                              hp.d_croff, hp.d_crng, LD, LL, UD, UL, W, hp.d_tflags);
             PP_TRY(cudaGetLastError());
             if (pi >= 0) hp.prof->end(pi, st, hp.top_cost.bytes, hp.top_cost.pairs);
             nl++;
@@ -123,34 +122,41 @@ struct Engine {
         return cudaSuccess;
     }
 
+    // the top fronts of a stage: one persistent launch (sweep_top_kernel), counters reset from a template
     template <bool FWD, bool TRANS>
-    static cudaError_t sweep_levels(const HostPlan &hp, const Stage &sg, bool ascending, const T *Dv, const T *Ov,
-                                    T *X, int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
-        const int ny = (k + ST_CT - 1) / ST_CT;
-        const int nlev = (int)sg.levels.size();
-        constexpr size_t smem = sweep_tiled_smem<T>();
+    static cudaError_t sweep_top(const HostPlan &hp, const std::pair<int64_t, int> &wl, const SLevel &cost,
+                                 const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
+                                 int64_t *nl) {
+        if (wl.second == 0) return cudaSuccess;
+        constexpr size_t smem = sweep_top_smem<T>();
         int dev = 0;
         cudaGetDevice(&dev);
         static bool attr[64] = {};
         if (dev < 64 && !attr[dev]) {
-            PP_TRY(cudaFuncSetAttribute(sweep_tiled_kernel<SR, T, FWD, TRANS>,
+            PP_TRY(cudaFuncSetAttribute(sweep_top_kernel<SR, T, FWD, TRANS>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
             attr[dev] = true;
         }
-        for (int t = 0; t < nlev; t++) {
-            const SLevel &lv = sg.levels[ascending ? t : nlev - 1 - t];
-            if (lv.count == 0) continue;
-            dim3 grid((unsigned)lv.count, (unsigned)ny);
-            const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD : K_SWEEP_BWD, st) : -1;
-            sweep_tiled_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_sfronts + lv.off, hp.dev, Dv, Ov, X,
-                                                                          ldx, k, unit);
-            PP_TRY(cudaGetLastError());
-            if (pi >= 0)
-                hp.prof->end(pi, st, (double)k * (2.0 * lv.res_rows + (FWD ? 2.0 : 1.0) * lv.sep_rows) + lv.blk_elems,
-                             (double)k * lv.pairs_col);
-            (*nl)++;
+        const int ntiles = (k + SW_CT - 1) / SW_CT;
+        if (FWD) {
+            PP_TRY(reset_sync(hp, hp.d_tpending0, ntiles, st));
+        } else {
+            PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int) * (16 + (size_t)ntiles * hp.nf), st));
         }
-        return cudaSuccess;
+        int per_sm = 1;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_top_kernel<SR, T, FWD, TRANS>, 256, smem);
+        const int64_t tasks = (int64_t)wl.second * ntiles;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tasks, std::max(per_sm, 1) * hp.sm_count));
+        const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD : K_SWEEP_BWD, st) : -1;
+        sweep_top_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev, Dv,
+                                                                     Ov, X, ldx, k, unit, hp.d_sync + 16, hp.d_sync,
+                                                                     hp.d_sync + 1);
+        PP_TRY(cudaGetLastError());
+        if (pi >= 0)
+            hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
+                         (double)k * cost.pairs_col);
+        (*nl)++;
+        return check_err(hp.d_sync + 1, st);
     }
 
     template <bool FWD, bool TRANS>
@@ -214,8 +220,8 @@ struct Engine {
                 const Stage &sg = hp.lstages[s];
                 PP_TRY((sweep_subtrees<true, false>(hp, hp.sub_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_bottom<true, false>(hp, hp.sb_fwd[s], hp.sb_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
-                PP_TRY((sweep_levels<true, false>(hp, sg, true, LD, LL, X, ldx, k, 1, st, &nl)));
-                PP_TRY((sweep_levels<false, false>(hp, sg, false, UD, UL, X, ldx, k, 0, st, &nl)));
+                PP_TRY((sweep_top<true, false>(hp, hp.st_fwd[s], hp.st_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
+                PP_TRY((sweep_top<false, false>(hp, hp.st_bwd[s], hp.st_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_bottom<false, false>(hp, hp.sb_bwd[s], hp.sb_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_subtrees<false, false>(hp, hp.sub_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 if (sg.coupled && sg.nverts > 0) {
@@ -240,8 +246,8 @@ struct Engine {
                 }
                 PP_TRY((sweep_subtrees<true, true>(hp, hp.sub_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_bottom<true, true>(hp, hp.sb_fwd_r[s], hp.sb_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
-                PP_TRY((sweep_levels<true, true>(hp, sg, true, UD, UL, X, ldx, k, 0, st, &nl)));
-                PP_TRY((sweep_levels<false, true>(hp, sg, false, LD, LL, X, ldx, k, 1, st, &nl)));
+                PP_TRY((sweep_top<true, true>(hp, hp.st_fwd_r[s], hp.st_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
+                PP_TRY((sweep_top<false, true>(hp, hp.st_bwd_r[s], hp.st_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_bottom<false, true>(hp, hp.sb_bwd_r[s], hp.sb_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_subtrees<false, true>(hp, hp.sub_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
             }

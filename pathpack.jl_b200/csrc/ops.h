@@ -93,8 +93,10 @@ struct HostPlan {
     int64_t ws_elems = 0;
     // top of the tree: the tile tasks of the persistent factorization (top.cuh), fronts by height
     int top_ntasks = 0;
-    const int4 *d_ttasks = nullptr;   // (front, I, J, kind: 0 = assembly of column block J, 1 = tile)
+    const int4 *d_ttasks = nullptr;   // (front, I, J, 0): tile (I, J) of the front
     const int64_t *d_tfoff = nullptr;  // per front: first of its flags in d_tflags
+    const int64_t *d_croff = nullptr;  // per child edge (index into chdtgt): first of its ranges in d_crng
+    const int *d_crng = nullptr;       // per child edge: the parent's tile-block boundaries in the child's rel[]
     int *d_tflags = nullptr;           // [0] task counter, [1] error word, then the fronts' flags
     int64_t tflags_n = 0;
     Cost top_cost;
@@ -121,6 +123,10 @@ struct HostPlan {
     std::vector<SubtreeList> sub_l, sub_r;
     const int *d_sroots = nullptr, *d_fdsc = nullptr, *d_slot = nullptr;
     const int *d_sdone0 = nullptr;     // 1 for fronts outside the bottom, 0 inside (backward flags)
+    // the top fronts of each stage for the persistent top sweep (forward ascending, backward descending heights)
+    std::vector<std::pair<int64_t, int>> st_fwd, st_bwd, st_fwd_r, st_bwd_r;
+    std::vector<SLevel> st_cost_l, st_cost_r;
+    const int *d_tpending0 = nullptr;  // top children per front (forward counters of the top sweep)
     int *d_sync = nullptr;             // scratch: [0] task counter, [1] error word, [16, 16 + nf * tiles) counters
     int64_t sync_cap = 0;              // ints allocated at d_sync
     int sm_count = 148;

@@ -3,7 +3,7 @@
 
 #include <cstddef>
 
-#include "../../include/pathpack_b200.h"
+#include "pathpack_b200.h"
 
 #define PP_INTERNAL __attribute__((visibility("hidden")))
 

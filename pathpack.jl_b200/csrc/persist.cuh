@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(128) factor_bottom_kernel(const int *__restric
 // residual (nn <= SWEEP_NNW) lives in registers, so the triangular solve needs no barrier.  Element reads of
 // the factor blocks are warp-uniform (broadcast).  FWD: wait for the children (counter), solve, (+)-scatter
 // to the separator with atomics, signal the parent.  Backward: wait for the parent's flag, gather from the
-// separator, solve, set the front's flag.  Same per-element dataflow as sweep_tiled_kernel.
+// separator, solve, set the front's flag.  Same per-element dataflow as sweep_top_kernel.
 
 template <int SR, typename T, bool FWD, bool TRANS>
 __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &P, const T *__restrict__ Dv,

@@ -57,7 +57,6 @@ struct SLevel {
 // Solve schedule of one stage: components whose coupling predecessors (rmul) or successors (lmul) are all
 // in earlier stages.
 struct Stage {
-    std::vector<SLevel> levels;  // by height
     int64_t voff = 0;                             // offset into the device vertex list of the stage
     int nverts = 0;
     bool coupled = false;                          // any coupling entries touch the stage

@@ -1,0 +1,247 @@
+// sweep_top.cuh — the triangular solves of the fronts above the bottom of the tree: ONE persistent launch per
+// sweep direction and coupling stage.
+//
+// Tasks are (front, 32 right-hand sides), fronts in height order (children first for the forward sweep,
+// parents first for the backward one), so every task waits only for tasks taken earlier: forward for a counter
+// of its top children (each finished child decrements it), backward for its parent's flag.  A task solves the
+// front's residual rows in blocks of 64 and then, forward, (+)-scatters L21 x to the separator rows with
+// atomics; backward it starts each block with the gather from the separator rows.  The off-diagonal products
+// are register-tiled (2 rows x 4 right-hand sides per thread) over operand chunks staged in shared memory,
+// double-buffered; the 64 x 64 diagonal block is solved warp by warp (a warp holds 4 right-hand sides, a lane
+// 8 rows of one of them) with the pivot values broadcast by shuffles, so the solve needs no CTA barrier.  Per
+// element the operands and their order are those of the reference's strsx2! / sgemx2!
+// (src/CPU/dense/strsx.jl:596-672, src/CPU/chordal/strsx.jl:187-265, 783-830): forward, contributions in
+// increasing pivot order; backward, the separator first, then decreasing pivot order.  The reference sweeps
+// the same fronts level by level, a launch per level (ext/PATHPACKCUDAExt/batched/sweep.jl:9-265).
+#pragma once
+
+#include "persist.cuh"
+
+namespace pp {
+
+constexpr int SW_RB = 64;   // residual rows per block
+constexpr int SW_CT = 32;   // right-hand sides per task
+constexpr int SW_KC = 16;   // operand chunk
+constexpr int SW_AL = SW_KC + 1;  // padded row of the staged matrix chunk
+constexpr int SW_XL = SW_CT + 1;  // padded row of the staged right-hand-side chunk
+constexpr int SW_DL = SW_RB + 1;  // padded row of the diagonal block
+
+template <typename T>
+constexpr size_t sweep_top_smem() {
+    return sizeof(T) * (2 * (size_t)SW_RB * SW_AL + 2 * (size_t)SW_KC * SW_XL + (size_t)SW_RB * SW_DL +
+                        (size_t)SW_RB * SW_XL);
+}
+
+template <int SR, typename T, bool FWD, bool TRANS>
+__global__ void __launch_bounds__(256) sweep_top_kernel(const int *__restrict__ wl, int count, DevPlan P,
+                                                        const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
+                                                        int64_t ldx, int k, int unit, int *flags, int *next,
+                                                        int *err) {
+    using S = Sem<SR, T>;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T *As = reinterpret_cast<T *>(smem_raw);  // 2 x [SW_RB][SW_AL]: matrix chunks
+    T *Xs = As + 2 * SW_RB * SW_AL;            // 2 x [SW_KC][SW_XL]: right-hand-side chunks
+    T *Dd = Xs + 2 * SW_KC * SW_XL;            // [SW_RB][SW_DL]: diagonal block
+    T *Ys = Dd + SW_RB * SW_DL;                // [SW_RB][SW_XL]: the residual block being solved
+    const int tid = threadIdx.x, tc = tid & 7, tr = tid >> 3;
+    const int lane = tid & 31, w = tid >> 5, dc = 4 * w + (lane >> 3), dg = lane & 7;
+    const int ntiles = (k + SW_CT - 1) / SW_CT, nf = P.nf;
+    const int64_t ntask = (int64_t)count * ntiles;
+    const T z = S::zero();
+    const bool scale = !unit && !S::integral;
+
+    while (true) {
+        const int t = cta_take(next);
+        if (t >= ntask) return;
+        const int idx = t / ntiles, tile = t - idx * ntiles;
+        const int f = wl[idx];
+        int *fl = flags + (int64_t)tile * nf;
+        const int p = P.pnt[f];
+        if (FWD) {
+            if (!cta_wait(fl + f, true, err)) return;
+        } else if (p >= 0) {
+            if (!cta_wait(fl + p, false, err)) return;
+        }
+        const int c0 = tile * SW_CT;
+        const int rlo = P.rlo[f], nn = P.nn[f], na = P.na[f];
+        const T *D = Dv + P.dptr[f];
+        const T *O = Ov + P.lptr[f];
+        const int *sep = P.stgt + P.sptr[f];
+        auto Te = [&](int r, int c) -> T { return TRANS ? D[c + (int64_t)r * nn] : D[r + (int64_t)c * nn]; };
+        auto xres = [&](int q) { return rlo + q; };
+        auto xsep = [&](int i) { return sep[i]; };
+
+        T acc[2][4];
+        auto load_acc = [&](int rowbase, int nrows, bool from_x) {
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int r = tr + 32 * i, c = c0 + tc + 8 * j;
+                    acc[i][j] = (from_x && r < nrows && c < k) ? ld_cg(X + (int64_t)(rowbase + r) * ldx + c) : z;
+                }
+        };
+        // acc[i][j] (+)= M(rb + row_i, kidx) (x) X[xrow(kidx)][col_j] for kidx in [kb, ke), ascending or
+        // descending; chunk ch + 1 is loaded into registers while chunk ch is used
+        auto accum = [&](int rb, int nrows, int kb, int ke, bool desc, auto M, auto xrow) {
+            const int kn = ke - kb;
+            if (kn <= 0) return;
+            const int nch = (kn + SW_KC - 1) / SW_KC;
+            T ra[4], rx[2];
+            auto fetch = [&](int ch) {
+                const int kc = min(SW_KC, kn - ch * SW_KC);
+                const int cb = desc ? ke - ch * SW_KC - kc : kb + ch * SW_KC;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    // consecutive threads read consecutive addresses: rows of the stored blocks, or (TRANS) columns
+                    const int e = tid + 256 * q;
+                    const int r = TRANS ? e / SW_KC : e % SW_RB, kk = TRANS ? e % SW_KC : e / SW_RB;
+                    ra[q] = (r < nrows && kk < kc) ? M(rb + r, cb + kk) : z;
+                }
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const int e = tid + 256 * q, kk = e / SW_CT, c = e % SW_CT;
+                    rx[q] = (kk < kc && c0 + c < k) ? ld_cg(X + (int64_t)xrow(cb + kk) * ldx + c0 + c) : z;
+                }
+            };
+            auto store = [&](int buf) {
+                T *a = As + buf * SW_RB * SW_AL;
+                T *x = Xs + buf * SW_KC * SW_XL;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int e = tid + 256 * q;
+                    const int r = TRANS ? e / SW_KC : e % SW_RB, kk = TRANS ? e % SW_KC : e / SW_RB;
+                    a[r * SW_AL + kk] = ra[q];
+                }
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const int e = tid + 256 * q;
+                    x[(e / SW_CT) * SW_XL + e % SW_CT] = rx[q];
+                }
+            };
+            fetch(0);
+            store(0);
+            __syncthreads();
+            for (int ch = 0; ch < nch; ch++) {
+                if (ch + 1 < nch) fetch(ch + 1);
+                const int kc = min(SW_KC, kn - ch * SW_KC);
+                const T *a = As + (ch & 1) * SW_RB * SW_AL;
+                const T *x = Xs + (ch & 1) * SW_KC * SW_XL;
+                for (int u = 0; u < kc; u++) {
+                    const int kk = desc ? kc - 1 - u : u;
+                    const T a0 = a[tr * SW_AL + kk], a1 = a[(tr + 32) * SW_AL + kk];
+                    T b[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) b[j] = x[kk * SW_XL + tc + 8 * j];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        acc[0][j] = S::muladd(a0, b[j], acc[0][j]);
+                        acc[1][j] = S::muladd(a1, b[j], acc[1][j]);
+                    }
+                }
+                if (ch + 1 < nch) store((ch + 1) & 1);
+                __syncthreads();
+            }
+        };
+
+        // the diagonal block of rows r0 .. r0 + nv - 1: acc -> Ys, solved warp by warp, written to X
+        auto diag_solve = [&](int r0, int nv) {
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) Ys[(tr + 32 * i) * SW_XL + tc + 8 * j] = acc[i][j];
+            for (int e = tid; e < SW_RB * SW_RB; e += 256) {
+                const int q = TRANS ? e / SW_RB : e % SW_RB, c = TRANS ? e % SW_RB : e / SW_RB;
+                Dd[q * SW_DL + c] = (q < nv && c < nv) ? Te(r0 + q, r0 + c) : z;
+            }
+            __syncthreads();
+            // lane (dc, dg) holds rows dg + 8 u of right-hand side dc; pivot 8 u + g lives in lane (dc, g), slot u
+            T y[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) y[u] = Ys[(dg + 8 * u) * SW_XL + dc];
+            const int src = lane & ~7;
+            if (FWD) {
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    for (int g = 0; g < 8; g++) {
+                        const int q = 8 * u + g;
+                        if (q >= nv) break;
+                        T yq = __shfl_sync(0xffffffffu, y[u], src | g);
+                        if (scale) yq = S::mul(yq, S::star(Dd[q * SW_DL + q]));
+                        if (dg == g) y[u] = yq;
+#pragma unroll
+                        for (int v = 0; v < 8; v++) {
+                            const int r = dg + 8 * v;
+                            if (r > q && r < nv) y[v] = S::muladd(Dd[r * SW_DL + q], yq, y[v]);
+                        }
+                    }
+            } else {
+#pragma unroll
+                for (int u = 7; u >= 0; u--)
+                    for (int g = 7; g >= 0; g--) {
+                        const int q = 8 * u + g;
+                        if (q >= nv) continue;
+                        T yq = __shfl_sync(0xffffffffu, y[u], src | g);
+                        if (scale) yq = S::mul(S::star(Dd[q * SW_DL + q]), yq);
+                        if (dg == g) y[u] = yq;
+#pragma unroll
+                        for (int v = 0; v < 8; v++) {
+                            const int r = dg + 8 * v;
+                            if (r < q) y[v] = S::muladd(Dd[r * SW_DL + q], yq, y[v]);
+                        }
+                    }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) Ys[(dg + 8 * u) * SW_XL + dc] = y[u];
+            __syncthreads();
+            for (int e = tid; e < SW_RB * SW_CT; e += 256) {
+                const int r = e / SW_CT, c = e % SW_CT;
+                if (r < nv && c0 + c < k) X[(int64_t)(rlo + r0 + r) * ldx + c0 + c] = Ys[r * SW_XL + c];
+            }
+            __syncthreads();
+        };
+
+        if (FWD) {
+            for (int r0 = 0; r0 < nn; r0 += SW_RB) {
+                const int nv = min(SW_RB, nn - r0);
+                load_acc(rlo + r0, nv, true);
+                accum(r0, nv, 0, r0, false, Te, xres);
+                diag_solve(r0, nv);
+            }
+            // separator: X[sep_i] (+)= (L21 x)_i
+            auto Of = [&](int i, int q) -> T { return TRANS ? O[q + (int64_t)i * nn] : O[i + (int64_t)q * na]; };
+            for (int i0 = 0; i0 < na; i0 += SW_RB) {
+                const int nv = min(SW_RB, na - i0);
+                load_acc(0, 0, false);
+                accum(i0, nv, 0, nn, false, Of, xres);
+#pragma unroll
+                for (int i = 0; i < 2; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int r = tr + 32 * i, c = c0 + tc + 8 * j;
+                        if (r < nv && c < k) S::atomic_add(X + (int64_t)sep[i0 + r] * ldx + c, acc[i][j]);
+                    }
+            }
+        } else {
+            auto Ob = [&](int r, int i) -> T { return TRANS ? O[i + (int64_t)r * na] : O[r + (int64_t)i * nn]; };
+            for (int r1 = nn; r1 > 0; r1 -= SW_RB) {
+                const int r0 = max(0, r1 - SW_RB), nv = r1 - r0;
+                load_acc(rlo + r0, nv, true);
+                accum(r0, nv, 0, na, false, Ob, xsep);
+                accum(r0, nv, r1, nn, true, Te, xres);
+                diag_solve(r0, nv);
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            if (FWD) {
+                if (p >= 0) atomicSub(fl + p, 1);
+            } else {
+                atomicExch(fl + f, 1);
+            }
+        }
+    }
+}
+
+}  // namespace pp

@@ -6,9 +6,9 @@
 // whole number of tiles that the parent reads in place.  The partial LU of the front is a left-looking tile
 // algorithm; every task owns one tile:
 //
-//   EA(J)    assemble column block J: zero, extend-add of the children's update matrices (last child first),
-//            then the entries of A (sgetrf_loop!, src/CPU/chordal/sgetrf.jl:101-131; sgetrf_send! :257-290)
-//   T(I, J)  F[I, J] (+)= F[I, k] (x) F[k, J] for the pivot blocks k < min(I, J, kb), in increasing k, then
+//   T(I, J)  assemble the tile in shared memory: zero, extend-add of the children's update matrices (last
+//            child first), then the entries of A (sgetrf_loop!, src/CPU/chordal/sgetrf.jl:101-131; sgetrf_send!
+//            :257-290); F[I, J] (+)= F[I, k] (x) F[k, J] for the pivot blocks k < min(I, J, kb), increasing k;
 //              I == J < kb : partial LU of the diagonal tile                        (sgetrf2!, dense/sgetrf.jl)
 //              J < kb < I or J < I < kb : x <- x U_JJ*   (strsx2! :R :U :N, dense/strsx.jl:596-672)
 //              I < kb, I < J : x <- L_II* x             (strsx2! :L :L :U)
@@ -16,15 +16,16 @@
 //
 // For every element this applies the pivots in increasing order with the same operands as the right-looking
 // scalar LU, so the factor is bit-identical to the reference's.  Tasks come from one list in an order where
-// every dependency is earlier (fronts by height, EA tasks first, tiles by (min(I, J), max(I, J))); CTAs take
-// them from an atomic counter and wait (bounded) on per-tile flags, so the lowest unfinished task can always
-// run and the launch cannot deadlock.  A front's finished separator tiles are counted, and its parent's EA
-// tasks wait for the count.  The reference factors the top of the tree level by level with several launches
+// every dependency is earlier (fronts by height, tiles by (min(I, J), max(I, J))); CTAs take them from an
+// atomic counter and wait (bounded) on per-tile flags, so the lowest unfinished task can always run and the
+// launch cannot deadlock.  A front's finished separator tiles are counted, and its parent's tiles wait for
+// the count.  The children's rows and columns that land in each tile block of the parent are contiguous
+// ranges of the sorted rel[] (crng, computed on the host), so a tile gathers exactly its own entries.  The reference factors the top of the tree level by level with several launches
 // per front (ext/PATHPACKCUDAExt/chordal/sgetrf_top.jl:1-254); here the whole top is one launch and
 // independent tiles of different fronts and levels overlap.
 //
-// Flags of front f start at foff[f]: [J] EA done, [nbt + I * nbt + J] tile final, [nbt + nbt^2] separator
-// tiles done.  flags[0] is the task counter, flags[1] the error word.
+// Flags of front f start at foff[f]: [I * nbt + J] tile final, [nbt^2] separator tiles done.  flags[0] is the
+// task counter, flags[1] the error word.
 #pragma once
 
 #include "persist.cuh"
@@ -33,6 +34,7 @@ namespace pp {
 
 constexpr int TB = TOP_TILE;  // tile edge
 constexpr int TLD = TB + 1;  // padded row of a shared tile
+constexpr int CHILD_CHUNK = 32;  // children whose ranges are staged in shared memory at a time
 
 template <typename T>
 constexpr size_t factor_top_smem() {
@@ -51,15 +53,21 @@ __device__ __forceinline__ void tile_range(int b, int nn, int na, int kb, int &s
     }
 }
 
+// acquire load of a flag another CTA publishes (__threadfence, then an atomic store): the data the producer
+// wrote before the flag is visible to this thread, and to the rest of the CTA after the barrier that follows
+__device__ __forceinline__ int ld_acquire(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // thread 0 polls until *p >= target (bounded; gives up at once when another CTA reported an error)
 __device__ __forceinline__ bool cta_wait_geq(const int *p, int target, int *err) {
     __shared__ int s_ok;
     if (threadIdx.x == 0) {
         long long it = 0;
         int ok = 1;
-        while (true) {
-            const int v = *(volatile const int *)p;
-            if (v >= target) break;
+        while (ld_acquire(p) < target) {
             if (*(volatile const int *)err) {
                 ok = 0;
                 break;
@@ -71,7 +79,6 @@ __device__ __forceinline__ bool cta_wait_geq(const int *p, int target, int *err)
             }
             __nanosleep(64);
         }
-        __threadfence();
         s_ok = ok;
     }
     __syncthreads();
@@ -80,29 +87,173 @@ __device__ __forceinline__ bool cta_wait_geq(const int *p, int target, int *err)
     return ok;
 }
 
-// first index in the ascending a[0 .. n) that is >= v
-__device__ __forceinline__ int lower_bound_dev(const int *a, int n, int v) {
-    int lo = 0, hi = n;
-    while (lo < hi) {
-        const int m = (lo + hi) >> 1;
-        if (a[m] < v)
-            lo = m + 1;
-        else
-            hi = m;
+// the entry of A that combine_entry adds to the assembled value of element (i, j) of the front (z if none)
+template <typename T>
+__device__ __forceinline__ T a_entry(int i, int j, int nn, int na, int64_t Dp, int64_t Lp, const T *LD, const T *LL,
+                                     const T *UD, const T *UL, T z) {
+    if (j < nn) {
+        if (i < nn) {
+            const int64_t o = Dp + i + (int64_t)j * nn;
+            return (nn == 1 || i <= j) ? UD[o] : LD[o];
+        }
+        return LL[Lp + (i - nn) + (int64_t)j * na];
     }
-    return lo;
+    if (i < nn) return UL[Lp + i + (int64_t)(j - nn) * nn];
+    return z;
+}
+
+// combine_entry with the entry of A already loaded (a_entry): the same operations in the same order
+template <int SR, typename T>
+__device__ __forceinline__ T combine_with(T v, T a, int i, int j, int nn) {
+    using S = Sem<SR, T>;
+    if (j < nn) {
+        if (i < nn) return nn == 1 ? S::add(a, v) : S::add(v, a);
+        return S::add(a, v);
+    }
+    if (i < nn) return S::add(a, v);
+    return v;
+}
+
+template <bool B>
+struct Half {
+    static constexpr bool hi = B;  // pivots 32 .. 63 (held in the second register set)
+};
+
+// x <- x U* for the 64 rows of the tile (strsx2! :R :U :N): U is the upper triangle of the b x b diagonal tile D
+template <int SR, typename T>
+__device__ __forceinline__ void tile_solve_right(T *X, const T *D, int b) {
+    using S = Sem<SR, T>;
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    T x0[8], x1[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        x0[q] = X[(8 * w + q) * TLD + l];
+        x1[q] = X[(8 * w + q) * TLD + l + 32];
+    }
+    auto step = [&](int p, auto half) {
+        constexpr bool hi = decltype(half)::hi;
+        const T s = S::integral ? S::one() : S::star(D[p * TLD + p]);
+        const T u0 = D[p * TLD + l], u1 = D[p * TLD + l + 32];
+        const bool g0 = l > p && l < b, g1 = l + 32 > p && l + 32 < b;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            T xp = __shfl_sync(0xffffffffu, hi ? x1[q] : x0[q], p & 31);
+            if (!S::integral) xp = S::mul(xp, s);
+            if (!hi && l == p) x0[q] = xp;
+            if (hi && l + 32 == p) x1[q] = xp;
+            if (g0) x0[q] = S::muladd(xp, u0, x0[q]);
+            if (g1) x1[q] = S::muladd(xp, u1, x1[q]);
+        }
+    };
+    for (int p = 0; p < min(b, 32); p++) step(p, Half<false>());
+    for (int p = 32; p < b; p++) step(p, Half<true>());
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        X[(8 * w + q) * TLD + l] = x0[q];
+        X[(8 * w + q) * TLD + l + 32] = x1[q];
+    }
+}
+
+// x <- L* x for the 64 columns of the tile (strsx2! :L :L :U): L is the strict lower triangle of D
+template <int SR, typename T>
+__device__ __forceinline__ void tile_solve_left(T *X, const T *D, int b) {
+    using S = Sem<SR, T>;
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    T x0[8], x1[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        x0[q] = X[l * TLD + 8 * w + q];
+        x1[q] = X[(l + 32) * TLD + 8 * w + q];
+    }
+    auto step = [&](int p, auto half) {
+        constexpr bool hi = decltype(half)::hi;
+        const T l0 = D[l * TLD + p], l1 = D[(l + 32) * TLD + p];
+        const bool g0 = l > p && l < b, g1 = l + 32 > p && l + 32 < b;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const T xp = __shfl_sync(0xffffffffu, hi ? x1[q] : x0[q], p & 31);
+            if (g0) x0[q] = S::muladd(l0, xp, x0[q]);
+            if (g1) x1[q] = S::muladd(l1, xp, x1[q]);
+        }
+    };
+    for (int p = 0; p < min(b, 32); p++) step(p, Half<false>());
+    for (int p = 32; p < b; p++) step(p, Half<true>());
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        X[l * TLD + 8 * w + q] = x0[q];
+        X[(l + 32) * TLD + 8 * w + q] = x1[q];
+    }
+}
+
+// partial LU of the b x b diagonal tile: warp w holds columns 8w .. 8w+7; the owner of pivot column p scales
+// it and publishes it in a double-buffered slot of sv (one barrier per pivot), every warp then updates its
+// later columns with the pivot row taken from its own registers
+template <int SR, typename T>
+__device__ __forceinline__ void tile_lu(T *X, T *sv, int b) {
+    using S = Sem<SR, T>;
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    T x0[8], x1[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        x0[q] = X[l * TLD + 8 * w + q];
+        x1[q] = X[(l + 32) * TLD + 8 * w + q];
+    }
+    // pivots in groups of eight, the columns of warp cg: the owner's column index is a compile-time constant
+    for (int cg = 0; 8 * cg < b; cg++) {
+#pragma unroll
+        for (int qp = 0; qp < 8; qp++) {
+            const int p = 8 * cg + qp;
+            if (p >= b) break;
+            const bool hi = p >= 32;
+            T *col = sv + (p & 1) * (2 * TB + 2);
+            const bool g0 = l > p && l < b, g1 = l + 32 > p && l + 32 < b;
+            if (w == cg) {
+                const T d = __shfl_sync(0xffffffffu, hi ? x1[qp] : x0[qp], p & 31);
+                if (!S::integral) {
+                    const T s = S::star(d);
+                    if (g0) x0[qp] = S::mul(x0[qp], s);
+                    if (g1) x1[qp] = S::mul(x1[qp], s);
+                }
+                col[l] = x0[qp];
+                col[l + 32] = x1[qp];
+            }
+            __syncthreads();
+            const T c0 = col[l], c1 = col[l + 32];
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const int c = 8 * w + q;
+                if (c > p && c < b) {
+                    const T up = __shfl_sync(0xffffffffu, hi ? x1[q] : x0[q], p & 31);
+                    if (g0) x0[q] = S::muladd(c0, up, x0[q]);
+                    if (g1) x1[q] = S::muladd(c1, up, x1[q]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        X[l * TLD + 8 * w + q] = x0[q];
+        X[(l + 32) * TLD + 8 * w + q] = x1[q];
+    }
 }
 
 template <int SR, typename T>
 __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict__ tasks, int ntasks, DevPlan P,
-                                                         const int64_t *__restrict__ foff, T *LD, T *LL, T *UD,
-                                                         T *UL, T *W, int *flags) {
+                                                         const int64_t *__restrict__ foff,
+                                                         const int64_t *__restrict__ croff,
+                                                         const int *__restrict__ crng, T *LD, T *LL, T *UD, T *UL,
+                                                         T *W, int *flags) {
     using S = Sem<SR, T>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *As = reinterpret_cast<T *>(smem_raw);  // [TB][TLD]: A operand (rows x k), or the diagonal tile
     T *Bs = As + TB * TLD;                     // [TB][TLD]: B operand (k x columns)
     T *sv = Bs + TB * TLD;                     // 2 x [column TB | row TB | 2]: pivot broadcasts, double-buffered
     int *next = flags, *err = flags + 1;
+    __shared__ int4 s_child[CHILD_CHUNK];  // per child: first row, rows, first column, columns in this tile
+    __shared__ int64_t s_cmat[CHILD_CHUNK];
+    __shared__ int2 s_cmeta[CHILD_CHUNK];  // leading dimension of the update matrix, offset of rel
+    __shared__ int s_ctop[CHILD_CHUNK];    // the child if it is a top front, else -1
+    __shared__ int s_bad;
     const int tid = threadIdx.x, tc = tid & 15, tr = tid >> 4;
     const T z = S::zero();
 
@@ -117,63 +268,96 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
         T *F = W + P.fws[f];
         const int64_t Dp = P.dptr[f], Lp = P.lptr[f];
 
-        if (task.w == 0) {
-            // ---- EA(J): assemble column block J of the frontal matrix
-            for (int c = P.chdptr[f]; c < P.chdptr[f + 1]; c++) {
-                const int ch = P.chdtgt[c];
-                if (P.fws[ch] < 0) continue;  // a bottom child: finished by the earlier launch
-                const int sbc = (P.na[ch] + TB - 1) / TB, nbc = (P.nn[ch] + TB - 1) / TB + sbc;
-                if (!cta_wait_geq(flags + foff[ch] + nbc + nbc * nbc, sbc * sbc, err)) return;
-            }
-            int j0, mj;
-            tile_range(J, nn, na, kb, j0, mj);
-            for (int e = tid; e < nj * mj; e += blockDim.x) F[(e % nj) + (int64_t)(j0 + e / nj) * nj] = z;
-            __syncthreads();
-            for (int c = P.chdptr[f + 1] - 1; c >= P.chdptr[f]; c--) {
-                const int ch = P.chdtgt[c];
-                const int nac = P.na[ch];
-                const int *rel = P.rel + P.sptr[ch];
-                const T *M = W + P.mptr[ch];
-                const int mld = P.mld[ch];
-                const int wlo = lower_bound_dev(rel, nac, j0), whi = lower_bound_dev(rel, nac, j0 + mj);
-                const int cnt = (whi - wlo) * nac;
-                for (int e = tid; e < cnt; e += blockDim.x) {
-                    const int v = e % nac, w = wlo + e / nac;
-                    const int64_t o = rel[v] + (int64_t)rel[w] * nj;
-                    F[o] = S::add(F[o], ld_cg(M + v + (int64_t)w * mld));
-                }
-                __syncthreads();
-            }
-            for (int e = tid; e < nj * mj; e += blockDim.x) {
-                const int i = e % nj, j = j0 + e / nj;
-                const int64_t o = i + (int64_t)j * nj;
-                F[o] = combine_entry<SR, T>(F[o], i, j, nn, na, Dp, Lp, LD, LL, UD, UL);
-            }
-            __syncthreads();
-            if (tid == 0) {
-                __threadfence();
-                atomicExch(fl + J, 1);
-            }
-            continue;
-        }
-
-        // ---- T(I, J)
+        // ---- T(I, J): assemble the tile in shared memory once the children's update matrices are final
         int i0, mi, j0, mj;
         tile_range(I, nn, na, kb, i0, mi);
         tile_range(J, nn, na, kb, j0, mj);
-        if (!cta_wait_geq(fl + J, 1, err)) return;
+        // issue the loads that do not depend on the children first: this thread's entries of A (element
+        // e = tid + 256 k of the tile, column-major), and per child its ranges and update-matrix location
+        const int c_lo = P.chdptr[f], c_hi = P.chdptr[f + 1];
+        T aval[TB * TB / 256];
+#pragma unroll
+        for (int k = 0; k < TB * TB / 256; k++) {
+            const int e = tid + 256 * k, r = e % TB, c = e / TB;
+            aval[k] = (r < mi && c < mj) ? a_entry<T>(i0 + r, j0 + c, nn, na, Dp, Lp, LD, LL, UD, UL, z) : z;
+        }
+        for (int e = tid; e < TB * TB; e += blockDim.x) As[(e % TB) * TLD + e / TB] = z;
+        for (int cb = c_hi; cb > c_lo; cb -= CHILD_CHUNK) {
+            // children cb - CHILD_CHUNK .. cb - 1 (clamped), applied last first
+            const int c0 = max(c_lo, cb - CHILD_CHUNK), nch = cb - c0;
+            if (tid < nch) {
+                const int c = c0 + tid, ch = P.chdtgt[c];
+                const int *rng = crng + croff[c];
+                const int vlo = rng[I], wlo = rng[J];
+                s_child[tid] = make_int4(vlo, rng[I + 1] - vlo, wlo, rng[J + 1] - wlo);
+                s_cmat[tid] = P.mptr[ch];
+                s_cmeta[tid] = make_int2(P.mld[ch], (int)P.sptr[ch]);
+                s_ctop[tid] = P.fws[ch] >= 0 ? ch : -1;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                // the top children must have finished their update matrices (bottom ones did, earlier launch)
+                int bad = 0;
+                for (int q = 0; q < nch && !bad; q++) {
+                    const int ch = s_ctop[q];
+                    if (ch < 0) continue;
+                    const int sbc = (P.na[ch] + TB - 1) / TB, nbc = (P.nn[ch] + TB - 1) / TB + sbc;
+                    long long it = 0;
+                    while (ld_acquire(flags + foff[ch] + nbc * nbc) < sbc * sbc) {
+                        if (*(volatile const int *)err || ++it > WAIT_LIMIT) {
+                            atomicExch(err, 1);
+                            bad = 1;
+                            break;
+                        }
+                        __nanosleep(64);
+                    }
+                }
+                s_bad = bad;
+            }
+            __syncthreads();
+            if (s_bad) return;  // uniform: every thread reads the value thread 0 wrote before the barrier
+            for (int q = nch - 1; q >= 0; q--) {
+                const int4 cr = s_child[q];
+                const int dv = cr.y, cnt = cr.y * cr.w;
+                const T *M = W + s_cmat[q];
+                const int mld = s_cmeta[q].x;
+                const int *rel = P.rel + s_cmeta[q].y;
+                for (int base = 0; base < cnt; base += 8 * 256) {
+                    T m[8];
+                    int o[8];
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        const int e = base + tid + 256 * k;
+                        o[k] = -1;
+                        if (e < cnt) {
+                            const int v = cr.x + e % dv, w = cr.z + e / dv;
+                            o[k] = (rel[v] - i0) * TLD + (rel[w] - j0);
+                            m[k] = ld_cg(M + v + (int64_t)w * mld);
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        if (o[k] >= 0) As[o[k]] = S::add(As[o[k]], m[k]);
+                }
+                __syncthreads();
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < TB * TB / 256; k++) {
+            const int e = tid + 256 * k, r = e % TB, c = e / TB;
+            if (r < mi && c < mj) As[r * TLD + c] = combine_with<SR, T>(As[r * TLD + c], aval[k], i0 + r, j0 + c, nn);
+        }
+        __syncthreads();
         T acc[4][4];
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int r = tr + 16 * i, c = tc + 16 * j;
-                acc[i][j] = (r < mi && c < mj) ? ld_cg(F + (i0 + r) + (int64_t)(j0 + c) * nj) : z;
-            }
+            for (int j = 0; j < 4; j++) acc[i][j] = As[(tr + 16 * i) * TLD + tc + 16 * j];
+        __syncthreads();
         const int K = min(min(I, J), kb);
         for (int k = 0; k < K; k++) {
-            if (!cta_wait_geq(fl + nbt + I * nbt + k, 1, err)) return;
-            if (!cta_wait_geq(fl + nbt + k * nbt + J, 1, err)) return;
+            if (!cta_wait_geq(fl + I * nbt + k, 1, err)) return;
+            if (!cta_wait_geq(fl + k * nbt + J, 1, err)) return;
             const int k0 = k * TB, bk = min(TB, nn - k0);
             for (int e = tid; e < TB * TB; e += blockDim.x) {
                 const int r = e % TB, kk = e / TB;
@@ -196,116 +380,47 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
             __syncthreads();
         }
 
+        // the tile to shared memory (As: rows x columns); the triangular work runs on it warp by warp
         const bool pivot_region = I < kb || J < kb;
-        if (pivot_region && I == J) {
-            // partial LU of the diagonal tile (mi == mj == b): one barrier per pivot, broadcasts double-buffered
-            const int b = mi;
-            for (int p = 0; p < b; p++) {
-                T *buf = sv + (p & 1) * (2 * TB + 2);
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-                    if (tr + 16 * i == p) {
-#pragma unroll
-                        for (int j = 0; j < 4; j++) buf[TB + tc + 16 * j] = acc[i][j];
-                    }
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    if (tc + 16 * j == p) {
-#pragma unroll
-                        for (int i = 0; i < 4; i++) buf[tr + 16 * i] = acc[i][j];
-                    }
-                __syncthreads();
-                const T s = S::integral ? S::one() : S::star(buf[TB + p]);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int r = tr + 16 * i;
-                    if (r <= p || r >= b) continue;
-                    const T l = S::integral ? buf[r] : S::mul(buf[r], s);
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const int c = tc + 16 * j;
-                        if (c == p) acc[i][j] = l;
-                        else if (c > p && c < b) acc[i][j] = S::muladd(l, buf[TB + c], acc[i][j]);
-                    }
-                }
-            }
-            __syncthreads();
-        } else if (pivot_region) {
-            // a panel tile: stage the factored diagonal tile of its pivot block
-            const int d = I > J ? J : I;
-            if (!cta_wait_geq(fl + nbt + d * nbt + d, 1, err)) return;
-            const int d0 = d * TB, b = min(TB, nn - d0);
-            for (int e = tid; e < TB * TB; e += blockDim.x) {
-                const int r = e % TB, c = e / TB;
-                As[r * TLD + c] = (r < b && c < b) ? ld_cg(F + (d0 + r) + (int64_t)(d0 + c) * nj) : z;
-            }
-            __syncthreads();
-            if (I > J) {
-                // x <- x U*: row-wise over the pivot columns p; the pivot column is broadcast
-                for (int p = 0; p < b; p++) {
-                    T *buf = sv + (p & 1) * (2 * TB + 2);
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        if (tc + 16 * j == p) {
-#pragma unroll
-                            for (int i = 0; i < 4; i++) buf[tr + 16 * i] = acc[i][j];
-                        }
-                    __syncthreads();
-                    const T s = S::integral ? S::one() : S::star(As[p * TLD + p]);
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int r = tr + 16 * i;
-                        if (r >= mi) continue;
-                        const T x = S::integral ? buf[r] : S::mul(buf[r], s);
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const int c = tc + 16 * j;
-                            if (c == p) acc[i][j] = x;
-                            else if (c > p && c < b) acc[i][j] = S::muladd(x, As[p * TLD + c], acc[i][j]);
-                        }
-                    }
-                }
-            } else {
-                // x <- L* x (unit diagonal): column-wise over the pivot rows p; the pivot row is broadcast
-                for (int p = 0; p < b; p++) {
-                    T *buf = sv + (p & 1) * (2 * TB + 2);
-#pragma unroll
-                    for (int i = 0; i < 4; i++)
-                        if (tr + 16 * i == p) {
-#pragma unroll
-                            for (int j = 0; j < 4; j++) buf[TB + tc + 16 * j] = acc[i][j];
-                        }
-                    __syncthreads();
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int r = tr + 16 * i;
-                        if (r <= p || r >= b) continue;
-                        const T l = As[r * TLD + p];
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            if (tc + 16 * j < mj) acc[i][j] = S::muladd(l, buf[TB + tc + 16 * j], acc[i][j]);
-                    }
-                }
-            }
-            __syncthreads();
-        }
-
-        // store the tile (and its factor entries)
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int r = tr + 16 * i, c = tc + 16 * j;
-                if (r < mi && c < mj) {
-                    F[(i0 + r) + (int64_t)(j0 + c) * nj] = acc[i][j];
-                    if (pivot_region) store_entry<T>(acc[i][j], i0 + r, j0 + c, nn, na, Dp, Lp, LD, LL, UD, UL);
-                }
+            for (int j = 0; j < 4; j++) As[(tr + 16 * i) * TLD + tc + 16 * j] = acc[i][j];
+        if (pivot_region && I != J) {
+            // a panel tile: stage the factored diagonal tile of its pivot block in Bs
+            const int d = I > J ? J : I;
+            if (!cta_wait_geq(fl + d * nbt + d, 1, err)) return;
+            const int d0 = d * TB, b = min(TB, nn - d0);
+            for (int e = tid; e < TB * TB; e += blockDim.x) {
+                const int r = e % TB, c = e / TB;
+                Bs[r * TLD + c] = (r < b && c < b) ? ld_cg(F + (d0 + r) + (int64_t)(d0 + c) * nj) : z;
             }
+        }
+        __syncthreads();
+        if (pivot_region) {
+            if (I == J)
+                tile_lu<SR, T>(As, sv, mi);
+            else if (I > J)
+                tile_solve_right<SR, T>(As, Bs, mj);
+            else
+                tile_solve_left<SR, T>(As, Bs, mi);
+            __syncthreads();
+        }
+
+        // store the tile (and its factor entries) column by column
+        for (int e = tid; e < TB * TB; e += blockDim.x) {
+            const int r = e % TB, c = e / TB;
+            if (r < mi && c < mj) {
+                const T v = As[r * TLD + c];
+                F[(i0 + r) + (int64_t)(j0 + c) * nj] = v;
+                if (pivot_region) store_entry<T>(v, i0 + r, j0 + c, nn, na, Dp, Lp, LD, LL, UD, UL);
+            }
+        }
         __syncthreads();
         if (tid == 0) {
             __threadfence();
-            atomicExch(fl + nbt + I * nbt + J, 1);
-            if (!pivot_region) atomicAdd(fl + nbt + nbt * nbt, 1);
+            atomicExch(fl + I * nbt + J, 1);
+            if (!pivot_region) atomicAdd(fl + nbt * nbt, 1);
         }
     }
 }

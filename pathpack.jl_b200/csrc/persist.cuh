@@ -104,6 +104,12 @@ __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &
     const bool scale = !unit && !S::integral;
     const int64_t drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;  // Te(r, c) = D[r * drs + c * dcs]
     for (int p = 0; p < nn; p++) xg[32 * p] = ok ? ld_cg(Xc + (int64_t)(rlo + p) * ldx) : z;
+    if (FWD && zero_absorbs<SR>) {
+        // the 32 right-hand sides are zero on the whole residual: the step changes nothing
+        bool nz = false;
+        for (int p = 0; p < nn; p++) nz |= !(xg[32 * p] == z);
+        if (!__any_sync(0xffffffffu, nz)) return;
+    }
     if (FWD) {
         const int64_t ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
         for (int p = 0; p < nn; p++) {
@@ -239,7 +245,14 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     const int nres = P.rlo[r] + P.nn[r] - rlo0;
     const int nsep = P.na[r];
     const int *sepr = P.stgt + P.sptr[r];
-    for (int s = 0; s < nres; s++) xs[32 * s] = ok ? Xc[(int64_t)(rlo0 + s) * ldx] : z;
+    bool nz = false;
+    for (int s = 0; s < nres; s++) {
+        xs[32 * s] = ok ? Xc[(int64_t)(rlo0 + s) * ldx] : z;
+        nz |= !(xs[32 * s] == z);
+    }
+    // forward: the 32 right-hand sides are zero on the subtree's rows, so no step changes anything (the
+    // sources of these columns lie outside the subtree)
+    if (FWD && zero_absorbs<SR> && !__any_sync(0xffffffffu, nz)) return;
     for (int i = 0; i < nsep; i++) xs[32 * (nres + i)] = (FWD || !ok) ? z : Xc[(int64_t)sepr[i] * ldx];
     for (int gg = 0; gg <= r - f0; gg++) {
         const int g = FWD ? f0 + gg : r - gg;

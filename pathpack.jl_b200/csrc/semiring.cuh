@@ -78,6 +78,12 @@ __device__ __forceinline__ void atomic_max_f64(double *p, double v) {
         atomicMin(reinterpret_cast<unsigned long long *>(p), (unsigned long long)__double_as_longlong(v));
 }
 
+// Whether the semiring's zero absorbs in the solves: muladd(zero, b, c) = c and mul(zero, b) = zero for every
+// b a factor can hold (a NaN product is zero; the x86 select keeps c).  Then a forward-sweep step whose
+// right-hand-side rows are all zero changes nothing and may be skipped.  Not PlusProd: 0 * Inf is NaN there.
+template <int SR>
+constexpr bool zero_absorbs = SR != PLUSPROD;
+
 template <int SR, typename T>
 struct Sem;
 

@@ -201,7 +201,17 @@ __global__ void __launch_bounds__(256) sweep_top_kernel(const int *__restrict__ 
             __syncthreads();
         };
 
-        if (FWD) {
+        bool live = true;
+        if (FWD && zero_absorbs<SR>) {
+            // the 32 right-hand sides are zero on the whole residual: the task changes nothing
+            bool nz = false;
+            for (int e = tid; e < nn * SW_CT; e += 256) {
+                const int c = c0 + e % SW_CT;
+                if (c < k) nz |= !(ld_cg(X + (int64_t)(rlo + e / SW_CT) * ldx + c) == z);
+            }
+            live = __syncthreads_or(nz) != 0;
+        }
+        if (FWD && live) {
             for (int r0 = 0; r0 < nn; r0 += SW_RB) {
                 const int nv = min(SW_RB, nn - r0);
                 load_acc(rlo + r0, nv, true);
@@ -222,7 +232,7 @@ __global__ void __launch_bounds__(256) sweep_top_kernel(const int *__restrict__ 
                         if (r < nv && c < k) S::atomic_add(X + (int64_t)sep[i0 + r] * ldx + c, acc[i][j]);
                     }
             }
-        } else {
+        } else if (!FWD) {
             auto Ob = [&](int r, int i) -> T { return TRANS ? O[i + (int64_t)r * na] : O[r + (int64_t)i * nn]; };
             for (int r1 = nn; r1 > 0; r1 -= SW_RB) {
                 const int r0 = max(0, r1 - SW_RB), nv = r1 - r0;

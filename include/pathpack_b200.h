@@ -14,7 +14,11 @@
  *   - Device memory is owned by the handle and released by pp_destroy, also after an error.
  *   - A handle is bound to one device and one stream; calls on one handle must be serialised by the caller.
  *     Different handles may be used from different threads.  Calls with host outputs return after the data
- *     is in host memory; calls with device outputs are ordered on the handle's stream (pp_sync waits).
+ *     is in host memory.  Calls whose outputs stay on the device (pp_factor, pp_lmul / pp_rmul / pp_star with
+ *     PP_DEVICE, pp_update_values from device memory) only enqueue their work on the handle's stream
+ *     (pp_stream) and return; a device error of such a call (PP_ETIMEOUT: a bounded wait of a persistent
+ *     kernel expired) is returned by the next call that waits for the stream: pp_sync, a call with host
+ *     inputs or outputs, pp_get_factor, pp_get_stats, pp_get_profile, pp_lmul_static.
  *   - Matrices are column-major (Julia's layout), with a leading dimension.
  *   - Index arrays are int64 and may be 1-based (as Julia and CliqueTrees hold them, `base` = 1) or 0-based.
  */
@@ -106,8 +110,8 @@ int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t where);
 int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, const void *LD, const void *LL, const void *UD,
                       const void *UL, const void *Nval);
 
-/* Factorize the star, A* = U* L*, in place on the device.  Replaces lu!(F) -> sgetrf!(F),
-   src/CPU/abstract_slu.jl:119-121 and src/CPU/chordal/sgetrf.jl:3-290. */
+/* Factorize the star, A* = U* L*, in place on the device (enqueued; see the conventions above).  Replaces
+   lu!(F) -> sgetrf!(F), src/CPU/abstract_slu.jl:119-121 and src/CPU/chordal/sgetrf.jl:3-290. */
 int32_t pp_factor(pp_handle *h);
 
 /* Download the factor arrays to the host (any pointer may be NULL). */
@@ -125,7 +129,7 @@ int32_t pp_rmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where);
    several GPUs share one star. */
 int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where);
 
-/* Wait for the handle's stream. */
+/* Wait for the handle's stream; reports a device error of the calls enqueued since the last wait. */
 int32_t pp_sync(pp_handle *h);
 
 /* ---- lmul! allocating nothing (no counterpart in the reference) ----

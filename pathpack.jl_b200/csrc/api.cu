@@ -82,7 +82,9 @@ struct DevBuf {
 struct pp_handle {
     int device = 0;
     cudaStream_t stream = nullptr;
-    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;    // around the last solve
+    cudaEvent_t fev0 = nullptr, fev1 = nullptr;  // around the last factorization
+    bool factor_pending = false, solve_pending = false;  // enqueued, times not yet read
     std::string err;
     bool have_structure = false, have_values = false, factored = false;
     int sr = -1, dt = -1;
@@ -94,7 +96,7 @@ struct pp_handle {
     DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
         d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_sfronts, d_sverts, d_pnt, d_fbottom,
         d_fpending0, d_spending0, d_sdone0, d_tpending0, d_sync, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags, d_croff,
-        d_crng;
+        d_crng, d_err;
     std::vector<int> pnt, height, rel;
     int maxh = 0;
     // values and work
@@ -168,6 +170,8 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev1);
+    if (e == cudaSuccess) e = cudaEventCreate(&h->fev0);
+    if (e == cudaSuccess) e = cudaEventCreate(&h->fev1);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) {
         pp_destroy(h);
@@ -184,6 +188,8 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
+    if (h->fev0) cudaEventDestroy(h->fev0);
+    if (h->fev1) cudaEventDestroy(h->fev1);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;  // DevBuf destructors free the device memory
     return PP_OK;
@@ -367,6 +373,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 sroot_of[f] = (int)f;
             }
             covered[f] = 1;
+            hp.sub_fmax = std::max(hp.sub_fmax, hp.nn[f] * hp.nn[f] + hp.nn[f] * hp.na[f]);
         }
         std::vector<int> slot(std::max<int64_t>(nS, 1), 0);
         for (int64_t f = 0; f < nf; f++) {
@@ -392,6 +399,10 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
             const bool mid = sbot[f] && !covered[f];
             if (mid) sdone0[f] = 0;
             if (mid && pnt[f] >= 0) spending0[pnt[f]]++;
+            if (mid) {
+                hp.bot_fmax = std::max(hp.bot_fmax, hp.nn[f] * hp.nn[f] + hp.nn[f] * hp.na[f]);
+                hp.bot_namax = std::max(hp.bot_namax, hp.na[f]);
+            }
             if (!sbot[f] && pnt[f] >= 0) tpending0[pnt[f]]++;  // top children (the top sweep's counters)
         }
         auto build_stages = [&](const std::vector<int> &stage_of, std::vector<Stage> &out, std::vector<int> &sfronts,
@@ -515,6 +526,8 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         CK(h, upload(h->d_sdone0, sdone0, st), "upload");
         CK(h, upload(h->d_tpending0, tpending0, st), "upload");
         CK(h, h->d_sync.ensure(sizeof(int) * (32 * nf + 16)), "upload");
+        CK(h, h->d_err.ensure(sizeof(int) * 4), "upload");
+        CK(h, cudaMemsetAsync(h->d_err.p, 0, sizeof(int) * 4, st), "upload");
         CK(h, cudaStreamSynchronize(st), "upload");
         DevPlan &d = hp.dev;
         d.n = (int)n;
@@ -551,6 +564,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         hp.d_sdone0 = h->d_sdone0.as<int>();
         hp.d_tpending0 = h->d_tpending0.as<int>();
         hp.d_sync = h->d_sync.as<int>();
+        hp.d_err = h->d_err.as<int>();
         hp.sync_cap = 32 * nf + 16;
         hp.sm_count = h->sm_count;
         h->invp = invp;
@@ -853,8 +867,7 @@ extern "C" int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t whe
     CK(h, h->ops->assemble(h->hp, h->csc_ptr.as<int>(), h->csc_row.as<int>(), h->csc_val.p, values_of(h), st),
        "pp_update_values");
     h->prof.end(pi, st, 2.0 * (h->nD + h->nL) + h->hp.nN + (double)nnz * (1.0 + 8.0 / es), 0);
-    CK(h, cudaStreamSynchronize(st), "pp_update_values");
-    h->prof.collect();
+    if (where == PP_HOST) CK(h, cudaStreamSynchronize(st), "pp_update_values");  // the caller's array is free
     h->have_values = true;
     h->factored = false;
     ok(h);
@@ -884,6 +897,33 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
     return PP_OK;
 }
 
+// Wait for the handle's stream, then take the times of the calls enqueued since the last wait and the error
+// word of the persistent kernels (set when a bounded wait expired; cleared once reported).
+static int32_t settle(pp_handle *h, const char *who) {
+    CK(h, cudaStreamSynchronize(h->stream), who);
+    if (h->factor_pending) {
+        float ms = 0;
+        if (cudaEventElapsedTime(&ms, h->fev0, h->fev1) == cudaSuccess) h->st.ms_factor = ms;
+        h->factor_pending = false;
+    }
+    if (h->solve_pending) {
+        float ms = 0;
+        if (cudaEventElapsedTime(&ms, h->ev0, h->ev1) == cudaSuccess) h->st.ms_solve = ms;
+        h->solve_pending = false;
+    }
+    h->prof.collect();
+    if (h->hp.d_err) {
+        int err = 0;
+        CK(h, cudaMemcpy(&err, h->hp.d_err, sizeof(int), cudaMemcpyDeviceToHost), who);
+        if (err) {
+            CK(h, cudaMemset(h->hp.d_err, 0, sizeof(int)), who);
+            return fail(h, PP_ETIMEOUT, "%s: a bounded device wait expired (a dependency of the persistent kernels "
+                        "never completed)", who);
+        }
+    }
+    return PP_OK;
+}
+
 extern "C" int32_t pp_factor(pp_handle *h) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_factor: null handle");
     if (!h->have_values) return fail(h, PP_ESTATE, "pp_factor: no values (call pp_assemble or pp_set_values)");
@@ -896,14 +936,10 @@ extern "C" int32_t pp_factor(pp_handle *h) {
     }
     cudaStream_t st = h->stream;
     int64_t nl = 0;
-    CK(h, cudaEventRecord(h->ev0, st), "pp_factor");
+    CK(h, cudaEventRecord(h->fev0, st), "pp_factor");
     CK(h, h->ops->factor(h->hp, values_of(h), st, &nl), "pp_factor");
-    CK(h, cudaEventRecord(h->ev1, st), "pp_factor");
-    CK(h, cudaEventSynchronize(h->ev1), "pp_factor");
-    h->prof.collect();
-    float ms = 0;
-    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
-    h->st.ms_factor = ms;
+    CK(h, cudaEventRecord(h->fev1, st), "pp_factor");
+    h->factor_pending = true;
     h->st.kernel_launches = nl;
     h->factored = true;
     ok(h);
@@ -920,7 +956,8 @@ extern "C" int32_t pp_get_factor(pp_handle *h, void *LD, void *LL, void *UD, voi
     if (UD && h->nD) CK(h, cudaMemcpyAsync(UD, h->UD.p, es * h->nD, cudaMemcpyDeviceToHost, st), "pp_get_factor");
     if (LL && h->nL) CK(h, cudaMemcpyAsync(LL, h->LL.p, es * h->nL, cudaMemcpyDeviceToHost, st), "pp_get_factor");
     if (UL && h->nL) CK(h, cudaMemcpyAsync(UL, h->UL.p, es * h->nL, cudaMemcpyDeviceToHost, st), "pp_get_factor");
-    CK(h, cudaStreamSynchronize(st), "pp_get_factor");
+    const int32_t r = settle(h, "pp_get_factor");
+    if (r != PP_OK) return r;
     ok(h);
     return PP_OK;
 }
@@ -999,19 +1036,17 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
         CK(h, h->ops->cols_out(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
     h->prof.end(pi, st, 2.0 * n * k, 0);
     CK(h, cudaEventRecord(h->ev1, st), who);
+    h->solve_pending = true;
+    h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)k;
+    h->st.kernel_launches = nl + 2;
     if (where == PP_HOST) {
         if (left)
             CK(h, cudaMemcpy2DAsync(B, es * ldb, Bd, es * n, es * n, k, cudaMemcpyDeviceToHost, st), who);
         else
             CK(h, cudaMemcpy2DAsync(B, es * ldb, Bd, es * k, es * k, n, cudaMemcpyDeviceToHost, st), who);
+        const int32_t r = settle(h, who);  // the result is in host memory when the call returns
+        if (r != PP_OK) return r;
     }
-    CK(h, cudaStreamSynchronize(st), who);
-    h->prof.collect();
-    float ms = 0;
-    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
-    h->st.ms_solve = ms;
-    h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)k;
-    h->st.kernel_launches = nl + 2;
     ok(h);
     return PP_OK;
 }
@@ -1066,16 +1101,15 @@ int32_t pp_internal_lmul_scratch(pp_handle *h, void *B, int64_t ldb, int64_t k, 
     if (e == cudaSuccess) e = h->ops->solve(h->hp, values_of(h), 1, X, ldx, (int)k, st, &nl);
     if (e == cudaSuccess) e = h->ops->rows_out(B, ldb, X, ldx, h->hp.dev.invp, n, (int)k, st);
     if (e == cudaSuccess) e = cudaEventRecord(h->ev1, st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     h->hp.d_sync = save_sync;
     h->hp.sync_cap = save_cap;
     h->hp.prof = save_prof;
     if (e != cudaSuccess) return cuda_fail(h, e, who);
-    float ms = 0;
-    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
-    h->st.ms_solve = ms;
+    h->solve_pending = true;
     h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)k;
     h->st.kernel_launches = nl + 2;
+    const int32_t r = settle(h, who);  // the scratch is free again when the call returns
+    if (r != PP_OK) return r;
     ok(h);
     return PP_OK;
 }
@@ -1130,10 +1164,9 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
     if (ensure_sync(h, pw) != PP_OK) return PP_ENOMEM;
     cudaStream_t st = h->stream;
     int64_t nl = 0;
-    float total = 0;
+    CK(h, cudaEventRecord(h->ev0, st), who);
     for (int64_t c0 = 0; c0 < ncols; c0 += pw) {
         const int w = (int)std::min<int64_t>(pw, ncols - c0);
-        CK(h, cudaEventRecord(h->ev0, st), who);
         CK(h, h->ops->fill_zero(h->X.p, (int64_t)n * ldx, st), who);
         CK(h, h->ops->unit_sources(h->X.p, ldx, h->hp.dev.invp, col0 + c0, w, st), who);
         CK(h, h->ops->solve(h->hp, values_of(h), 1, h->X.p, ldx, w, st, &nl), who);
@@ -1142,21 +1175,22 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
         const int pi = h->prof.begin(K_PERMUTE, st);
         CK(h, h->ops->rows_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
         h->prof.end(pi, st, 2.0 * n * w, 0);
-        CK(h, cudaEventRecord(h->ev1, st), who);
         nl += 3;
-        if (where == PP_HOST)
+        if (where == PP_HOST) {
             CK(h, cudaMemcpy2DAsync(static_cast<char *>(C) + es * (size_t)c0 * ldc, es * ldc, h->stage_out.p, es * n,
                                     es * n, w, cudaMemcpyDeviceToHost, st),
                who);
-        CK(h, cudaStreamSynchronize(st), who);
-        h->prof.collect();
-        float ms = 0;
-        cudaEventElapsedTime(&ms, h->ev0, h->ev1);
-        total += ms;
+            CK(h, cudaStreamSynchronize(st), who);  // the staging buffer is reused by the next panel
+        }
     }
-    h->st.ms_solve = total;
+    CK(h, cudaEventRecord(h->ev1, st), who);
+    h->solve_pending = true;
     h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)ncols;
     h->st.kernel_launches = nl;
+    if (where == PP_HOST) {
+        const int32_t r = settle(h, who);
+        if (r != PP_OK) return r;
+    }
     ok(h);
     return PP_OK;
 }
@@ -1164,13 +1198,17 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
 extern "C" int32_t pp_sync(pp_handle *h) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_sync: null handle");
     cudaSetDevice(h->device);
-    CK(h, cudaStreamSynchronize(h->stream), "pp_sync");
+    const int32_t r = settle(h, "pp_sync");
+    if (r != PP_OK) return r;
     ok(h);
     return PP_OK;
 }
 
 extern "C" int32_t pp_get_stats(pp_handle *h, pp_stats *s) {
     if (!h || !s) return fail(h, PP_EINVAL, "pp_get_stats: null argument");
+    cudaSetDevice(h->device);
+    const int32_t r = settle(h, "pp_get_stats");
+    if (r != PP_OK) return r;
     int64_t bytes = 0;
     for (DevBuf *b : {&h->d_rlo, &h->d_nn, &h->d_na, &h->d_sptr, &h->d_stgt, &h->d_rel, &h->d_dptr, &h->d_lptr,
                       &h->d_chdptr, &h->d_chdtgt, &h->d_mptr, &h->d_mld, &h->d_fws, &h->d_nptr, &h->d_ntgt,
@@ -1187,7 +1225,8 @@ extern "C" int32_t pp_get_stats(pp_handle *h, pp_stats *s) {
 extern "C" int32_t pp_set_profile(pp_handle *h, int32_t on) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_set_profile: null handle");
     cudaSetDevice(h->device);
-    cudaStreamSynchronize(h->stream);
+    const int32_t r = settle(h, "pp_set_profile");
+    if (r != PP_OK) return r;
     h->prof.reset();
     h->prof.on = on != 0;
     ok(h);
@@ -1197,8 +1236,8 @@ extern "C" int32_t pp_set_profile(pp_handle *h, int32_t on) {
 extern "C" int32_t pp_get_profile(pp_handle *h, pp_kernel_class *out, int32_t max, int32_t *count) {
     if (!h || (!out && max > 0)) return fail(h, PP_EINVAL, "pp_get_profile: null argument");
     cudaSetDevice(h->device);
-    cudaStreamSynchronize(h->stream);
-    h->prof.collect();
+    const int32_t r = settle(h, "pp_get_profile");
+    if (r != PP_OK) return r;
     int c = 0;
     for (int k = 0; k < K_NCLASS && c < max; k++) {
         if (h->prof.launches[k] == 0) continue;

@@ -69,17 +69,10 @@ struct Engine {
         return cudaSuccess;
     }
 
-    // the error word of a persistent launch: a bounded wait expired
-    static cudaError_t check_err(const int *word, cudaStream_t st) {
-        int err = 0;
-        PP_TRY(cudaMemcpyAsync(&err, word, sizeof(int), cudaMemcpyDeviceToHost, st));
-        PP_TRY(cudaStreamSynchronize(st));
-        return err ? cudaErrorLaunchTimeout : cudaSuccess;
-    }
-
-    // scratch layout: d_sync[0] task counter, d_sync[1] error word, d_sync + 16 the per-(tile, front) counters
+    // scratch layout: d_sync[0] task counter of the current launch, d_sync + 16 the per-(tile, front) counters.
+    // A bounded wait that expires sets hp.d_err; the C ABI reads it at the next synchronisation.
     static cudaError_t reset_sync(const HostPlan &hp, const int *init, int ntiles, cudaStream_t st) {
-        PP_TRY(cudaMemsetAsync(hp.d_sync, 0, 2 * sizeof(int), st));
+        PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int), st));
         if (ntiles == 1) return cudaMemcpyAsync(hp.d_sync + 16, init, sizeof(int) * hp.nf, cudaMemcpyDeviceToDevice, st);
         init_flags_kernel<<<grid_for((int64_t)hp.nf * ntiles, 256), 256, 0, st>>>(hp.d_sync + 16, init, hp.nf, ntiles);
         return cudaGetLastError();
@@ -98,11 +91,10 @@ struct Engine {
             const int grid = std::max(1, std::min(hp.fb_count, std::max(per_sm, 1) * hp.sm_count));
             const int pi = hp.prof ? hp.prof->begin(K_FRONT_BOTTOM, st) : -1;
             factor_bottom_kernel<SR, T><<<grid, 128, smem, st>>>(hp.d_fbottom, hp.fb_count, hp.dev, LD, LL, UD, UL, W,
-                                                                 hp.d_sync + 16, hp.d_sync, hp.d_sync + 1);
+                                                                 hp.d_sync + 16, hp.d_sync, hp.d_err);
             PP_TRY(cudaGetLastError());
             if (pi >= 0) hp.prof->end(pi, st, hp.fb_bytes, hp.fb_pairs);
             nl++;
-            PP_TRY(check_err(hp.d_sync + 1, st));
         }
         if (hp.top_ntasks > 0) {
             constexpr size_t smem = factor_top_smem<T>();
@@ -112,11 +104,11 @@ struct Engine {
             const int grid = std::max(1, std::min(hp.top_ntasks, std::max(per_sm, 1) * hp.sm_count));
             const int pi = hp.prof ? hp.prof->begin(K_FACTOR_TOP, st) : -1;
             factor_top_kernel<SR, T><<<grid, 256, smem, st>>>(hp.d_ttasks, hp.top_ntasks, hp.dev, hp.d_tfoff,
-                                                              hp.d_croff, hp.d_crng, LD, LL, UD, UL, W, hp.d_tflags);
+                                                              hp.d_croff, hp.d_crng, LD, LL, UD, UL, W, hp.d_tflags,
+                                                              hp.d_err);
             PP_TRY(cudaGetLastError());
             if (pi >= 0) hp.prof->end(pi, st, hp.top_cost.bytes, hp.top_cost.pairs);
             nl++;
-            PP_TRY(check_err(hp.d_tflags + 1, st));
         }
         if (launches) *launches += nl;
         return cudaSuccess;
@@ -141,7 +133,8 @@ struct Engine {
         if (FWD) {
             PP_TRY(reset_sync(hp, hp.d_tpending0, ntiles, st));
         } else {
-            PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int) * (16 + (size_t)ntiles * hp.nf), st));
+            PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int), st));
+            PP_TRY(cudaMemsetAsync(hp.d_sync + 16, 0, sizeof(int) * (size_t)ntiles * hp.nf, st));
         }
         int per_sm = 1;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_top_kernel<SR, T, FWD, TRANS>, 256, smem);
@@ -150,13 +143,13 @@ struct Engine {
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD : K_SWEEP_BWD, st) : -1;
         sweep_top_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev, Dv,
                                                                      Ov, X, ldx, k, unit, hp.d_sync + 16, hp.d_sync,
-                                                                     hp.d_sync + 1);
+                                                                     hp.d_err);
         PP_TRY(cudaGetLastError());
         if (pi >= 0)
             hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
                          (double)k * cost.pairs_col);
         (*nl)++;
-        return check_err(hp.d_sync + 1, st);
+        return cudaSuccess;
     }
 
     template <bool FWD, bool TRANS>
@@ -166,39 +159,50 @@ struct Engine {
         if (wl.second == 0) return cudaSuccess;
         const int ntiles = (k + 31) / 32;
         PP_TRY(reset_sync(hp, FWD ? hp.d_spending0 : hp.d_sdone0, ntiles, st));
+        const int fmax = std::max(hp.bot_fmax, 1), namax = std::max(hp.bot_namax, 1);
+        const size_t smem = 8 * bottom_warp_bytes<T>(fmax, namax);
+        int dev = 0;
+        cudaGetDevice(&dev);
+        static size_t attr[64] = {};
+        if (dev < 64 && attr[dev] < smem) {
+            PP_TRY(cudaFuncSetAttribute(sweep_bottom_kernel<SR, T, FWD, TRANS>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attr[dev] = smem;
+        }
         int per_sm = 1;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_bottom_kernel<SR, T, FWD, TRANS>, 256, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_bottom_kernel<SR, T, FWD, TRANS>, 256, smem);
         const int64_t tasks = (int64_t)wl.second * ntiles;
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((tasks + 7) / 8, std::max(per_sm, 1) * hp.sm_count));
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_BOTTOM : K_SWEEP_BWD_BOTTOM, st) : -1;
-        sweep_bottom_kernel<SR, T, FWD, TRANS><<<grid, 256, 0, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev, Dv,
-                                                                     Ov, X, ldx, k, unit, hp.d_sync + 16,
-                                                                     hp.d_sync, hp.d_sync + 1);
+        sweep_bottom_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev,
+                                                                        Dv, Ov, X, ldx, k, unit, hp.d_sync + 16,
+                                                                        hp.d_sync, hp.d_err, fmax, namax);
         PP_TRY(cudaGetLastError());
         if (pi >= 0)
             hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
                          (double)k * cost.pairs_col);
         (*nl)++;
-        return check_err(hp.d_sync + 1, st);
+        return cudaSuccess;
     }
 
     template <bool FWD, bool TRANS>
     static cudaError_t sweep_subtrees(const HostPlan &hp, const SubtreeList &sl, const T *Dv, const T *Ov, T *X,
                                       int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
         if (sl.count == 0) return cudaSuccess;
-        constexpr size_t smem = sizeof(T) * 4 * SUBTREE_ROWS * 32;
+        const int fmax = std::max(hp.sub_fmax, 1);
+        const size_t smem = 4 * subtree_warp_bytes<T>(fmax);
         int dev = 0;
         cudaGetDevice(&dev);
-        static bool attr[64] = {};
-        if (dev < 64 && !attr[dev]) {
+        static size_t attr[64] = {};
+        if (dev < 64 && attr[dev] < smem) {
             PP_TRY(cudaFuncSetAttribute(sweep_subtree_kernel<SR, T, FWD, TRANS>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            attr[dev] = true;
+            attr[dev] = smem;
         }
         const int64_t tasks = (int64_t)sl.count * ((k + 31) / 32);
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_SUBTREE : K_SWEEP_BWD_SUBTREE, st) : -1;
         sweep_subtree_kernel<SR, T, FWD, TRANS><<<(unsigned)((tasks + 3) / 4), 128, smem, st>>>(
-            hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit);
+            hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit, fmax);
         PP_TRY(cudaGetLastError());
         if (pi >= 0) hp.prof->end(pi, st, 0, 0);
         (*nl)++;

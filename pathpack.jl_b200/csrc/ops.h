@@ -122,12 +122,15 @@ struct HostPlan {
     // subtrees solved in shared memory (per stage), their roots, first descendants and separator slots
     std::vector<SubtreeList> sub_l, sub_r;
     const int *d_sroots = nullptr, *d_fdsc = nullptr, *d_slot = nullptr;
+    int sub_fmax = 0;                  // largest nn * nn + nn * na of a front inside those subtrees
+    int bot_fmax = 0, bot_namax = 0;   // largest nn * nn + nn * na and na of the other bottom fronts
     const int *d_sdone0 = nullptr;     // 1 for fronts outside the bottom, 0 inside (backward flags)
     // the top fronts of each stage for the persistent top sweep (forward ascending, backward descending heights)
     std::vector<std::pair<int64_t, int>> st_fwd, st_bwd, st_fwd_r, st_bwd_r;
     std::vector<SLevel> st_cost_l, st_cost_r;
     const int *d_tpending0 = nullptr;  // top children per front (forward counters of the top sweep)
-    int *d_sync = nullptr;             // scratch: [0] task counter, [1] error word, [16, 16 + nf * tiles) counters
+    int *d_sync = nullptr;             // scratch: [0] task counter, [16, 16 + nf * tiles) counters
+    int *d_err = nullptr;              // set by a persistent kernel whose bounded wait expired
     int64_t sync_cap = 0;              // ints allocated at d_sync
     int sm_count = 148;
 };

@@ -87,10 +87,33 @@ __global__ void __launch_bounds__(128) factor_bottom_kernel(const int *__restric
 // to the separator with atomics, signal the parent.  Backward: wait for the parent's flag, gather from the
 // separator, solve, set the front's flag.  Same per-element dataflow as sweep_top_kernel.
 
-template <int SR, typename T, bool FWD, bool TRANS>
+// one element (4 or 8 bytes) copied into shared memory asynchronously (cp.async); cp_async_wait_all waits for
+// this thread's copies
+template <typename T>
+__device__ __forceinline__ void cp_async_elem(T *dst, const T *src) {
+    static_assert(sizeof(T) == 4 || sizeof(T) == 8, "element copies of 4 or 8 bytes");
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    if constexpr (sizeof(T) == 8)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(src) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// shared memory of one warp of sweep_bottom_kernel: a front's factor blocks (D, then the off-diagonal block)
+// and its separator positions
+template <typename T>
+__host__ __device__ constexpr size_t bottom_warp_bytes(int fmax, int namax) {
+    return (sizeof(T) * (size_t)fmax + sizeof(int) * (size_t)namax + 15) & ~(size_t)15;
+}
+
+// One (front, 32-column tile) task of the bottom sweeps: the residual values (nn <= NMAX) in registers, the
+// factor blocks and separator positions copied into the warp's shared memory (cp.async, all in flight at
+// once), the separator values of the backward sweep loaded eight at a time ahead of their use.
+template <int SR, typename T, bool FWD, bool TRANS, int NMAX>
 __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &P, const T *__restrict__ Dv,
                                                 const T *__restrict__ Ov, T *X, int64_t ldx, int k, int unit,
-                                                T *xg /* this lane's column of a SWEEP_NNW x 32 scratch */) {
+                                                T *fb, int *sb) {
     using S = Sem<SR, T>;
     const int lane = threadIdx.x & 31;
     const int col = tile * 32 + lane;
@@ -102,48 +125,69 @@ __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &
     T *Xc = X + (ok ? col : 0);
     const T z = S::zero();
     const bool scale = !unit && !S::integral;
-    const int64_t drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;  // Te(r, c) = D[r * drs + c * dcs]
-    for (int p = 0; p < nn; p++) xg[32 * p] = ok ? ld_cg(Xc + (int64_t)(rlo + p) * ldx) : z;
+    const int drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;  // Te(r, c) = D[r * drs + c * dcs]
+    T x[NMAX];
+#pragma unroll
+    for (int p = 0; p < NMAX; p++) x[p] = (p < nn && ok) ? ld_cg(Xc + (int64_t)(rlo + p) * ldx) : z;
     if (FWD && zero_absorbs<SR>) {
         // the 32 right-hand sides are zero on the whole residual: the step changes nothing
         bool nz = false;
-        for (int p = 0; p < nn; p++) nz |= !(xg[32 * p] == z);
+#pragma unroll
+        for (int p = 0; p < NMAX; p++) nz |= !(x[p] == z);
         if (!__any_sync(0xffffffffu, nz)) return;
     }
+    for (int e = lane; e < nn * nn; e += 32) cp_async_elem(fb + e, D + e);
+    for (int e = lane; e < nn * na; e += 32) cp_async_elem(fb + nn * nn + e, O + e);
+    for (int e = lane; e < na; e += 32) cp_async_elem(sb + e, sep + e);
+    cp_async_wait_all();
+    __syncwarp();
+    const T *Ds = fb, *Os = fb + nn * nn;
     if (FWD) {
-        const int64_t ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
-        for (int p = 0; p < nn; p++) {
-            T xp = xg[32 * p];
-            if (scale) {
-                xp = S::mul(xp, S::star(__ldg(D + p * (drs + dcs))));
-                xg[32 * p] = xp;
-            }
-            for (int q = p + 1; q < nn; q++) xg[32 * q] = S::muladd(__ldg(D + q * drs + p * dcs), xp, xg[32 * q]);
+        const int ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
+#pragma unroll
+        for (int p = 0; p < NMAX; p++) {
+            if (p >= nn) break;
+            if (scale) x[p] = S::mul(x[p], S::star(Ds[p * (drs + dcs)]));
+#pragma unroll
+            for (int q = p + 1; q < NMAX; q++)
+                if (q < nn) x[q] = S::muladd(Ds[q * drs + p * dcs], x[p], x[q]);
         }
-        for (int p = 0; p < nn; p++)
-            if (ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, xg[32 * p]);
+#pragma unroll
+        for (int p = 0; p < NMAX; p++)
+            if (p < nn && ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, x[p]);
         for (int i = 0; i < na; i++) {
             T a = z;
-            for (int p = 0; p < nn; p++) a = S::muladd(__ldg(O + i * ors + p * ocs), xg[32 * p], a);
-            if (ok) S::atomic_add(Xc + (int64_t)sep[i] * ldx, a);
+#pragma unroll
+            for (int p = 0; p < NMAX; p++)
+                if (p < nn) a = S::muladd(Os[i * ors + p * ocs], x[p], a);
+            if (ok) S::atomic_add(Xc + (int64_t)sb[i] * ldx, a);
         }
     } else {
-        const int64_t ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
-        for (int i = 0; i < na; i++) {
-            const T xi = ok ? ld_cg(Xc + (int64_t)sep[i] * ldx) : z;
-            for (int p = 0; p < nn; p++) xg[32 * p] = S::muladd(__ldg(O + p * ors + i * ocs), xi, xg[32 * p]);
-        }
-        for (int p = nn - 1; p >= 0; p--) {
-            T xp = xg[32 * p];
-            if (scale) {
-                xp = S::mul(S::star(__ldg(D + p * (drs + dcs))), xp);
-                xg[32 * p] = xp;
+        const int ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
+        for (int i0 = 0; i0 < na; i0 += 8) {
+            T xv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) xv[u] = (i0 + u < na && ok) ? ld_cg(Xc + (int64_t)sb[i0 + u] * ldx) : z;
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                if (i0 + u >= na) break;
+#pragma unroll
+                for (int p = 0; p < NMAX; p++)
+                    if (p < nn) x[p] = S::muladd(Os[p * ors + (i0 + u) * ocs], xv[u], x[p]);
             }
-            for (int q = 0; q < p; q++) xg[32 * q] = S::muladd(__ldg(D + q * drs + p * dcs), xp, xg[32 * q]);
         }
-        for (int p = 0; p < nn; p++)
-            if (ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, xg[32 * p]);
+#pragma unroll
+        for (int p = NMAX - 1; p >= 0; p--) {
+            if (p >= nn) continue;
+            if (scale) x[p] = S::mul(S::star(Ds[p * (drs + dcs)]), x[p]);
+#pragma unroll
+            for (int q = 0; q < p; q++) x[q] = S::muladd(Ds[q * drs + p * dcs], x[p], x[q]);
+        }
+#pragma unroll
+        for (int p = 0; p < NMAX; p++)
+            if (p < nn && ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, x[p]);
     }
+    __syncwarp();  // the buffers are reused by the warp's next task
 }
 
 // lane 0 of the warp polls *p until it satisfies the predicate (or the limit expires); broadcast result
@@ -175,14 +219,16 @@ __device__ __forceinline__ bool warp_wait(const int *p, bool for_zero, int *err)
 // Independent warp tasks (front, 32-column tile), in work-list order with the tiles innermost.  flags holds one
 // counter (forward: children not yet done) or flag (backward: done) per (tile, front): flags[tile * nf + f].
 template <int SR, typename T, bool FWD, bool TRANS>
-__global__ void __launch_bounds__(256, 2) sweep_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P,
-                                                              const T *__restrict__ Dv, const T *__restrict__ Ov,
-                                                              T *X, int64_t ldx, int k, int unit, int *flags,
-                                                              int *next, int *err) {
-    __shared__ T scratch[8][SWEEP_NNW * 32];
+__global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P,
+                                                           const T *__restrict__ Dv, const T *__restrict__ Ov,
+                                                           T *X, int64_t ldx, int k, int unit, int *flags,
+                                                           int *next, int *err, int fmax, int namax) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char *mine = smem_raw + (size_t)(threadIdx.x >> 5) * bottom_warp_bytes<T>(fmax, namax);
+    T *fb = reinterpret_cast<T *>(mine);
+    int *sb = reinterpret_cast<int *>(fb + fmax);
     const int ntiles = (k + 31) / 32;
     const int lane = threadIdx.x & 31;
-    T *xg = &scratch[threadIdx.x >> 5][lane];
     const int nf = P.nf;
     const int64_t ntask = (int64_t)count * ntiles;
     while (true) {
@@ -199,7 +245,13 @@ __global__ void __launch_bounds__(256, 2) sweep_bottom_kernel(const int *__restr
         } else if (p >= 0) {
             if (!warp_wait(fl + p, false, err)) return;
         }
-        warp_front_tile<SR, T, FWD, TRANS>(f, tile, P, Dv, Ov, X, ldx, k, unit, xg);
+        const int nn = P.nn[f];
+        if (nn <= 4)
+            warp_front_tile<SR, T, FWD, TRANS, 4>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+        else if (nn <= 8)
+            warp_front_tile<SR, T, FWD, TRANS, 8>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+        else
+            warp_front_tile<SR, T, FWD, TRANS, SWEEP_NNW>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
         __syncwarp();
         if (lane == 0) {
             __threadfence();
@@ -222,15 +274,81 @@ __global__ void __launch_bounds__(256, 2) sweep_bottom_kernel(const int *__restr
 // slot[Sptr[g] + i] is the shared-memory row of the i-th separator vertex of front g.  Each lane touches only
 // its own column, so a task needs no barrier.
 
+
+// One front of a subtree for this lane's right-hand side: its nn <= NMAX residual values in registers (the
+// loops are unrolled to NMAX and guarded by nn), the factor blocks D (nn x nn) and O (the off-diagonal block)
+// and the separator slots sl in shared memory, the subtree's rows in xs.  Same operations in the same order
+// as warp_front_tile.
+template <int SR, typename T, bool FWD, bool TRANS, int NMAX>
+__device__ __forceinline__ void subtree_front(int nn, int na, T *xg, T *xs, const T *D, const int *sl, bool scale) {
+    using S = Sem<SR, T>;
+    const T z = S::zero();
+    const T *O = D + nn * nn;
+    const int drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;  // Te(r, c) = D[r * drs + c * dcs]
+    T x[NMAX];
+#pragma unroll
+    for (int p = 0; p < NMAX; p++) x[p] = p < nn ? xg[32 * p] : z;
+    if (FWD) {
+        const int ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
+#pragma unroll
+        for (int p = 0; p < NMAX; p++) {
+            if (p >= nn) break;
+            if (scale) x[p] = S::mul(x[p], S::star(D[p * (drs + dcs)]));
+#pragma unroll
+            for (int q = p + 1; q < NMAX; q++)
+                if (q < nn) x[q] = S::muladd(D[q * drs + p * dcs], x[p], x[q]);
+        }
+        for (int i = 0; i < na; i++) {
+            T a = z;
+#pragma unroll
+            for (int p = 0; p < NMAX; p++)
+                if (p < nn) a = S::muladd(O[i * ors + p * ocs], x[p], a);
+            T &c = xs[32 * sl[i]];
+            c = S::add(c, a);
+        }
+    } else {
+        const int ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
+        for (int i = 0; i < na; i++) {
+            const T xi = xs[32 * sl[i]];
+#pragma unroll
+            for (int p = 0; p < NMAX; p++)
+                if (p < nn) x[p] = S::muladd(O[p * ors + i * ocs], xi, x[p]);
+        }
+#pragma unroll
+        for (int p = NMAX - 1; p >= 0; p--) {
+            if (p >= nn) continue;
+            if (scale) x[p] = S::mul(S::star(D[p * (drs + dcs)]), x[p]);
+#pragma unroll
+            for (int q = 0; q < p; q++) x[q] = S::muladd(D[q * drs + p * dcs], x[p], x[q]);
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < NMAX; p++)
+        if (p < nn) xg[32 * p] = x[p];
+}
+
+// shared memory of one warp of sweep_subtree_kernel: the rows, two factor-block buffers of fmax elements and
+// two slot buffers
+template <typename T>
+__host__ __device__ constexpr size_t subtree_warp_bytes(int fmax) {
+    return sizeof(T) * ((size_t)SUBTREE_ROWS * 32 + 2 * (size_t)fmax) + sizeof(int) * 2 * SUBTREE_ROWS;
+}
+
+// The fronts of the subtree are r's descendants fdsc[r] .. r, contiguous in postorder.  The factor blocks of the
+// next front (D, the off-diagonal block, the separator slots) are copied into shared memory with cp.async while
+// the current one is solved, so every factor operand is read from shared memory.
 template <int SR, typename T, bool FWD, bool TRANS>
 __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restrict__ roots, int nroots, DevPlan P,
                                                             const int *__restrict__ fdsc, const int *__restrict__ slot,
                                                             const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
-                                                            int64_t ldx, int k, int unit) {
+                                                            int64_t ldx, int k, int unit, int fmax) {
     using S = Sem<SR, T>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    T *xs = reinterpret_cast<T *>(smem_raw) + (size_t)w * SUBTREE_ROWS * 32 + lane;  // row s at xs[32 * s]
+    unsigned char *mine = smem_raw + (size_t)w * subtree_warp_bytes<T>(fmax);
+    T *xs = reinterpret_cast<T *>(mine) + lane;  // row s at xs[32 * s]
+    T *fb = reinterpret_cast<T *>(mine) + SUBTREE_ROWS * 32;
+    int *sb = reinterpret_cast<int *>(fb + 2 * fmax);
     const int ntiles = (k + 31) / 32;
     const int64_t t = (int64_t)blockIdx.x * 4 + w;
     if (t >= (int64_t)nroots * ntiles) return;
@@ -245,6 +363,24 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     const int nres = P.rlo[r] + P.nn[r] - rlo0;
     const int nsep = P.na[r];
     const int *sepr = P.stgt + P.sptr[r];
+    const int ng = r - f0 + 1;
+    // stage front number gi of the traversal into buffer buf; its sizes and first row come back in registers
+    auto issue = [&](int gi, int buf, int &nn, int &na, int &rlo) {
+        const int g = FWD ? f0 + gi : r - gi;
+        nn = P.nn[g];
+        na = P.na[g];
+        rlo = P.rlo[g];
+        const T *D = Dv + P.dptr[g];
+        const T *O = Ov + P.lptr[g];
+        const int *sl = slot + P.sptr[g];
+        T *b = fb + buf * fmax;
+        for (int e = lane; e < nn * nn; e += 32) cp_async_elem(b + e, D + e);
+        for (int e = lane; e < nn * na; e += 32) cp_async_elem(b + nn * nn + e, O + e);
+        int *s = sb + buf * SUBTREE_ROWS;
+        for (int e = lane; e < na; e += 32) cp_async_elem(s + e, sl + e);
+    };
+    int nn1, na1, rlo1;
+    issue(0, 0, nn1, na1, rlo1);
     bool nz = false;
     for (int s = 0; s < nres; s++) {
         xs[32 * s] = ok ? Xc[(int64_t)(rlo0 + s) * ldx] : z;
@@ -252,48 +388,26 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     }
     // forward: the 32 right-hand sides are zero on the subtree's rows, so no step changes anything (the
     // sources of these columns lie outside the subtree)
-    if (FWD && zero_absorbs<SR> && !__any_sync(0xffffffffu, nz)) return;
+    if (FWD && zero_absorbs<SR> && !__any_sync(0xffffffffu, nz)) {
+        cp_async_wait_all();
+        return;
+    }
     for (int i = 0; i < nsep; i++) xs[32 * (nres + i)] = (FWD || !ok) ? z : Xc[(int64_t)sepr[i] * ldx];
-    for (int gg = 0; gg <= r - f0; gg++) {
-        const int g = FWD ? f0 + gg : r - gg;
-        const int nn = P.nn[g], na = P.na[g];
-        T *xg = xs + 32 * (P.rlo[g] - rlo0);  // the front's residual rows: xg[32 * p]
-        const T *D = Dv + P.dptr[g];
-        const T *O = Ov + P.lptr[g];
-        const int *sl = slot + P.sptr[g];
-        // (r, c) of the triangle and (sep i, residual p) of the off-diagonal block as read by this sweep
-        const int64_t drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;
-        if (FWD) {
-            const int64_t ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
-            for (int p = 0; p < nn; p++) {
-                T xp = xg[32 * p];
-                if (scale) {
-                    xp = S::mul(xp, S::star(__ldg(D + p * (drs + dcs))));
-                    xg[32 * p] = xp;
-                }
-                for (int q = p + 1; q < nn; q++) xg[32 * q] = S::muladd(__ldg(D + q * drs + p * dcs), xp, xg[32 * q]);
-            }
-            for (int i = 0; i < na; i++) {
-                T a = z;
-                for (int p = 0; p < nn; p++) a = S::muladd(__ldg(O + i * ors + p * ocs), xg[32 * p], a);
-                T &c = xs[32 * sl[i]];
-                c = S::add(c, a);
-            }
-        } else {
-            const int64_t ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
-            for (int i = 0; i < na; i++) {
-                const T xi = xs[32 * sl[i]];
-                for (int p = 0; p < nn; p++) xg[32 * p] = S::muladd(__ldg(O + p * ors + i * ocs), xi, xg[32 * p]);
-            }
-            for (int p = nn - 1; p >= 0; p--) {
-                T xp = xg[32 * p];
-                if (scale) {
-                    xp = S::mul(S::star(__ldg(D + p * (drs + dcs))), xp);
-                    xg[32 * p] = xp;
-                }
-                for (int q = 0; q < p; q++) xg[32 * q] = S::muladd(__ldg(D + q * drs + p * dcs), xp, xg[32 * q]);
-            }
-        }
+    for (int gi = 0; gi < ng; gi++) {
+        const int nn = nn1, na = na1, rlo = rlo1;
+        cp_async_wait_all();
+        __syncwarp();
+        if (gi + 1 < ng) issue(gi + 1, (gi + 1) & 1, nn1, na1, rlo1);
+        T *xg = xs + 32 * (rlo - rlo0);  // the front's residual rows: xg[32 * p]
+        const T *D = fb + (gi & 1) * fmax;
+        const int *sl = sb + (gi & 1) * SUBTREE_ROWS;
+        if (nn <= 4)
+            subtree_front<SR, T, FWD, TRANS, 4>(nn, na, xg, xs, D, sl, scale);
+        else if (nn <= 8)
+            subtree_front<SR, T, FWD, TRANS, 8>(nn, na, xg, xs, D, sl, scale);
+        else
+            subtree_front<SR, T, FWD, TRANS, SWEEP_NNW>(nn, na, xg, xs, D, sl, scale);
+        __syncwarp();  // the buffer is refilled two fronts later
     }
     if (!ok) return;
     for (int s = 0; s < nres; s++) Xc[(int64_t)(rlo0 + s) * ldx] = xs[32 * s];

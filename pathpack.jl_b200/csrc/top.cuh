@@ -25,7 +25,7 @@
 // independent tiles of different fronts and levels overlap.
 //
 // Flags of front f start at foff[f]: [I * nbt + J] tile final, [nbt^2] separator tiles done.  flags[0] is the
-// task counter, flags[1] the error word.
+// task counter; err is the error word of the factorization.
 #pragma once
 
 #include "persist.cuh"
@@ -242,13 +242,13 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
                                                          const int64_t *__restrict__ foff,
                                                          const int64_t *__restrict__ croff,
                                                          const int *__restrict__ crng, T *LD, T *LL, T *UD, T *UL,
-                                                         T *W, int *flags) {
+                                                         T *W, int *flags, int *err) {
     using S = Sem<SR, T>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *As = reinterpret_cast<T *>(smem_raw);  // [TB][TLD]: A operand (rows x k), or the diagonal tile
     T *Bs = As + TB * TLD;                     // [TB][TLD]: B operand (k x columns)
     T *sv = Bs + TB * TLD;                     // 2 x [column TB | row TB | 2]: pivot broadcasts, double-buffered
-    int *next = flags, *err = flags + 1;
+    int *next = flags;
     __shared__ int4 s_child[CHILD_CHUNK];  // per child: first row, rows, first column, columns in this tile
     __shared__ int64_t s_cmat[CHILD_CHUNK];
     __shared__ int2 s_cmeta[CHILD_CHUNK];  // leading dimension of the update matrix, offset of rel

@@ -103,9 +103,13 @@ class B200SLU:
               self._h)
         return self
 
-    def factor(self):
-        """lu!(F): the multifrontal factorization of the star on the GPU."""
+    def factor(self, sync=True):
+        """lu!(F): the multifrontal factorization of the star on the GPU.  The C call only enqueues the work on
+        the handle's stream; with sync=False this returns at once too, and a device error is reported by the next
+        call that waits (sync(), a solve into host memory, factors(), stats())."""
         check(lib().pp_factor(self._h), self._h)
+        if sync:
+            self.sync()
         return self
 
     def factors(self):
@@ -158,7 +162,7 @@ class B200SLU:
         check(lib().pp_lmul_static(self._h, vptr(B), ld, k), self._h)
         return B
 
-    def _solve(self, B, left):
+    def _solve(self, B, left, sync=True):
         n = self.S.n
         fn = lib().pp_lmul if left else lib().pp_rmul
         if hasattr(B, "data_ptr"):  # a CUDA torch tensor, used in place
@@ -171,6 +175,8 @@ class B200SLU:
                     raise ValueError("B must be column-major (stride(0) == 1)")
                 k, ld = (B.shape[1], B.stride(1)) if left else (B.shape[0], B.stride(1))
             check(fn(self._h, vptr(B), ld, k, PP_DEVICE), self._h)
+            if sync:  # device results are ordered on the handle's stream; make them visible to every stream
+                self.sync()
             return B
         X = np.asarray(B)
         vec = X.ndim == 1
@@ -196,6 +202,7 @@ class B200SLU:
             out = np.empty((n, ncols), dtype=self.dtype, order="F")
         if hasattr(out, "data_ptr"):
             check(lib().pp_star(self._h, vptr(out), out.stride(1), col0, ncols, PP_DEVICE), self._h)
+            self.sync()
         else:
             if not out.flags.f_contiguous:
                 raise ValueError("out must be column-major")

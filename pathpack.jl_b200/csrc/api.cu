@@ -84,6 +84,8 @@ struct pp_handle {
     cudaStream_t stream = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;    // around the last solve
     cudaEvent_t fev0 = nullptr, fev1 = nullptr;  // around the last factorization
+    cudaStream_t copy_stream = nullptr;           // host-to-device copies that may overlap the handle's work
+    cudaEvent_t copy_ev = nullptr;
     bool factor_pending = false, solve_pending = false;  // enqueued, times not yet read
     std::string err;
     bool have_structure = false, have_values = false, factored = false;
@@ -172,6 +174,8 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev1);
     if (e == cudaSuccess) e = cudaEventCreate(&h->fev0);
     if (e == cudaSuccess) e = cudaEventCreate(&h->fev1);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->copy_ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) {
         pp_destroy(h);
@@ -190,6 +194,11 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
     if (h->ev1) cudaEventDestroy(h->ev1);
     if (h->fev0) cudaEventDestroy(h->fev0);
     if (h->fev1) cudaEventDestroy(h->fev1);
+    if (h->copy_ev) cudaEventDestroy(h->copy_ev);
+    if (h->copy_stream) {
+        cudaStreamSynchronize(h->copy_stream);
+        cudaStreamDestroy(h->copy_stream);
+    }
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;  // DevBuf destructors free the device memory
     return PP_OK;
@@ -1010,15 +1019,19 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
     void *Bd = B;
     int64_t ldbd = ldb;
     if (where == PP_HOST) {
+        // the copy runs on the copy stream, so it overlaps work still queued on the handle's stream (a
+        // factorization enqueued just before); the stream waits for it before the solve reads B
         CK(h, h->stage_in.ensure(bbytes), who);
         Bd = h->stage_in.p;
         if (left) {
             ldbd = n;
-            CK(h, cudaMemcpy2DAsync(Bd, es * n, B, es * ldb, es * n, k, cudaMemcpyHostToDevice, st), who);
+            CK(h, cudaMemcpy2DAsync(Bd, es * n, B, es * ldb, es * n, k, cudaMemcpyHostToDevice, h->copy_stream), who);
         } else {
             ldbd = k;
-            CK(h, cudaMemcpy2DAsync(Bd, es * k, B, es * ldb, es * k, n, cudaMemcpyHostToDevice, st), who);
+            CK(h, cudaMemcpy2DAsync(Bd, es * k, B, es * ldb, es * k, n, cudaMemcpyHostToDevice, h->copy_stream), who);
         }
+        CK(h, cudaEventRecord(h->copy_ev, h->copy_stream), who);
+        CK(h, cudaStreamWaitEvent(st, h->copy_ev, 0), who);
     }
     int64_t nl = 0;
     CK(h, cudaEventRecord(h->ev0, st), who);

@@ -48,6 +48,18 @@ def peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+def profiled_traffic(kernel):
+    """DRAM bytes per launch of the kernel (dram__bytes_read.sum + dram__bytes_write.sum) from the committed ncu
+    summary profiles/<kernel>_config2.md, or None."""
+    path = os.path.join(REPO, "profiles", "%s_config2.md" % kernel.split("(")[0])
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":")[1])
+    return None
+
+
 # ----------------------------------------------------------------------------------------------- workloads
 
 def config2(rank):
@@ -267,7 +279,7 @@ def run_ours(args, rank, world, local):
     per_launch_s = d["ms"] / 1e3 / d["launches"]
     achieved = d["bytes"] / d["launches"] / per_launch_s / 1e9
     roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": float(pk["hbm_gbs"]), "unit": "GB/s",
-            "frac": achieved / float(pk["hbm_gbs"]), "traffic": None, "peak_source": src,
+            "frac": achieved / float(pk["hbm_gbs"]), "traffic": profiled_traffic(name), "peak_source": src,
             "launches_per_step": d["launches"] / args.steps, "ms_per_step": d["ms"] / args.steps,
             "pairs_per_s": d["pairs"] / (d["ms"] / 1e3) if d["ms"] > 0 else 0.0}
     kernels = {k_: {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps,

@@ -382,7 +382,6 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 sroot_of[f] = (int)f;
             }
             covered[f] = 1;
-            hp.sub_fmax = std::max(hp.sub_fmax, hp.nn[f] * hp.nn[f] + hp.nn[f] * hp.na[f]);
         }
         std::vector<int> slot(std::max<int64_t>(nS, 1), 0);
         for (int64_t f = 0; f < nf; f++) {

@@ -189,8 +189,7 @@ struct Engine {
     static cudaError_t sweep_subtrees(const HostPlan &hp, const SubtreeList &sl, const T *Dv, const T *Ov, T *X,
                                       int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
         if (sl.count == 0) return cudaSuccess;
-        const int fmax = std::max(hp.sub_fmax, 1);
-        const size_t smem = 4 * subtree_warp_bytes<T>(fmax);
+        const size_t smem = 4 * subtree_warp_bytes<T>();
         int dev = 0;
         cudaGetDevice(&dev);
         static size_t attr[64] = {};
@@ -202,7 +201,7 @@ struct Engine {
         const int64_t tasks = (int64_t)sl.count * ((k + 31) / 32);
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_SUBTREE : K_SWEEP_BWD_SUBTREE, st) : -1;
         sweep_subtree_kernel<SR, T, FWD, TRANS><<<(unsigned)((tasks + 3) / 4), 128, smem, st>>>(
-            hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit, fmax);
+            hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit);
         PP_TRY(cudaGetLastError());
         if (pi >= 0) hp.prof->end(pi, st, 0, 0);
         (*nl)++;

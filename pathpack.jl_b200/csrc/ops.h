@@ -122,7 +122,6 @@ struct HostPlan {
     // subtrees solved in shared memory (per stage), their roots, first descendants and separator slots
     std::vector<SubtreeList> sub_l, sub_r;
     const int *d_sroots = nullptr, *d_fdsc = nullptr, *d_slot = nullptr;
-    int sub_fmax = 0;                  // largest nn * nn + nn * na of a front inside those subtrees
     int bot_fmax = 0, bot_namax = 0;   // largest nn * nn + nn * na and na of the other bottom fronts
     const int *d_sdone0 = nullptr;     // 1 for fronts outside the bottom, 0 inside (backward flags)
     // the top fronts of each stage for the persistent top sweep (forward ascending, backward descending heights)

@@ -277,13 +277,13 @@ __global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict
 
 // One front of a subtree for this lane's right-hand side: its nn <= NMAX residual values in registers (the
 // loops are unrolled to NMAX and guarded by nn), the factor blocks D (nn x nn) and O (the off-diagonal block)
-// and the separator slots sl in shared memory, the subtree's rows in xs.  Same operations in the same order
+// and the separator slots sl, the subtree's rows in xs.  Same operations in the same order
 // as warp_front_tile.
 template <int SR, typename T, bool FWD, bool TRANS, int NMAX>
-__device__ __forceinline__ void subtree_front(int nn, int na, T *xg, T *xs, const T *D, const int *sl, bool scale) {
+__device__ __forceinline__ void subtree_front(int nn, int na, T *xg, T *xs, const T *__restrict__ D,
+                                              const T *__restrict__ O, const int *__restrict__ sl, bool scale) {
     using S = Sem<SR, T>;
     const T z = S::zero();
-    const T *O = D + nn * nn;
     const int drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;  // Te(r, c) = D[r * drs + c * dcs]
     T x[NMAX];
 #pragma unroll
@@ -327,28 +327,24 @@ __device__ __forceinline__ void subtree_front(int nn, int na, T *xg, T *xs, cons
         if (p < nn) xg[32 * p] = x[p];
 }
 
-// shared memory of one warp of sweep_subtree_kernel: the rows, two factor-block buffers of fmax elements and
-// two slot buffers
+// shared memory of one warp of sweep_subtree_kernel: the subtree's rows for its 32 right-hand sides
 template <typename T>
-__host__ __device__ constexpr size_t subtree_warp_bytes(int fmax) {
-    return sizeof(T) * ((size_t)SUBTREE_ROWS * 32 + 2 * (size_t)fmax) + sizeof(int) * 2 * SUBTREE_ROWS;
+__host__ __device__ constexpr size_t subtree_warp_bytes() {
+    return sizeof(T) * (size_t)SUBTREE_ROWS * 32;
 }
 
-// The fronts of the subtree are r's descendants fdsc[r] .. r, contiguous in postorder.  The factor blocks of the
-// next front (D, the off-diagonal block, the separator slots) are copied into shared memory with cp.async while
-// the current one is solved, so every factor operand is read from shared memory.
+// The fronts of the subtree are r's descendants fdsc[r] .. r, contiguous in postorder.  Each front's residual
+// values of this lane are held in registers while it is solved (subtree_front); the factor operands are read
+// through the read-only cache.
 template <int SR, typename T, bool FWD, bool TRANS>
 __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restrict__ roots, int nroots, DevPlan P,
                                                             const int *__restrict__ fdsc, const int *__restrict__ slot,
                                                             const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
-                                                            int64_t ldx, int k, int unit, int fmax) {
+                                                            int64_t ldx, int k, int unit) {
     using S = Sem<SR, T>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    unsigned char *mine = smem_raw + (size_t)w * subtree_warp_bytes<T>(fmax);
-    T *xs = reinterpret_cast<T *>(mine) + lane;  // row s at xs[32 * s]
-    T *fb = reinterpret_cast<T *>(mine) + SUBTREE_ROWS * 32;
-    int *sb = reinterpret_cast<int *>(fb + 2 * fmax);
+    T *xs = reinterpret_cast<T *>(smem_raw + (size_t)w * subtree_warp_bytes<T>()) + lane;  // row s at xs[32 * s]
     const int ntiles = (k + 31) / 32;
     const int64_t t = (int64_t)blockIdx.x * 4 + w;
     if (t >= (int64_t)nroots * ntiles) return;
@@ -364,20 +360,12 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     const int nsep = P.na[r];
     const int *sepr = P.stgt + P.sptr[r];
     const int ng = r - f0 + 1;
-    // stage front number gi of the traversal into buffer buf; its sizes and first row come back in registers
-    auto issue = [&](int gi, int buf, int &nn, int &na, int &rlo) {
+    // the sizes and first row of front number gi of the traversal, loaded one front ahead
+    auto issue = [&](int gi, int, int &nn, int &na, int &rlo) {
         const int g = FWD ? f0 + gi : r - gi;
         nn = P.nn[g];
         na = P.na[g];
         rlo = P.rlo[g];
-        const T *D = Dv + P.dptr[g];
-        const T *O = Ov + P.lptr[g];
-        const int *sl = slot + P.sptr[g];
-        T *b = fb + buf * fmax;
-        for (int e = lane; e < nn * nn; e += 32) cp_async_elem(b + e, D + e);
-        for (int e = lane; e < nn * na; e += 32) cp_async_elem(b + nn * nn + e, O + e);
-        int *s = sb + buf * SUBTREE_ROWS;
-        for (int e = lane; e < na; e += 32) cp_async_elem(s + e, sl + e);
     };
     int nn1, na1, rlo1;
     issue(0, 0, nn1, na1, rlo1);
@@ -388,26 +376,24 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     }
     // forward: the 32 right-hand sides are zero on the subtree's rows, so no step changes anything (the
     // sources of these columns lie outside the subtree)
-    if (FWD && zero_absorbs<SR> && !__any_sync(0xffffffffu, nz)) {
-        cp_async_wait_all();
-        return;
-    }
+    if (FWD && zero_absorbs<SR> && !__any_sync(0xffffffffu, nz)) return;
     for (int i = 0; i < nsep; i++) xs[32 * (nres + i)] = (FWD || !ok) ? z : Xc[(int64_t)sepr[i] * ldx];
     for (int gi = 0; gi < ng; gi++) {
         const int nn = nn1, na = na1, rlo = rlo1;
-        cp_async_wait_all();
         __syncwarp();
         if (gi + 1 < ng) issue(gi + 1, (gi + 1) & 1, nn1, na1, rlo1);
         T *xg = xs + 32 * (rlo - rlo0);  // the front's residual rows: xg[32 * p]
-        const T *D = fb + (gi & 1) * fmax;
-        const int *sl = sb + (gi & 1) * SUBTREE_ROWS;
+        const int g = FWD ? f0 + gi : r - gi;
+        const T *D = Dv + P.dptr[g];
+        const T *O = Ov + P.lptr[g];
+        const int *sl = slot + P.sptr[g];
         if (nn <= 4)
-            subtree_front<SR, T, FWD, TRANS, 4>(nn, na, xg, xs, D, sl, scale);
+            subtree_front<SR, T, FWD, TRANS, 4>(nn, na, xg, xs, D, O, sl, scale);
         else if (nn <= 8)
-            subtree_front<SR, T, FWD, TRANS, 8>(nn, na, xg, xs, D, sl, scale);
+            subtree_front<SR, T, FWD, TRANS, 8>(nn, na, xg, xs, D, O, sl, scale);
         else
-            subtree_front<SR, T, FWD, TRANS, SWEEP_NNW>(nn, na, xg, xs, D, sl, scale);
-        __syncwarp();  // the buffer is refilled two fronts later
+            subtree_front<SR, T, FWD, TRANS, SWEEP_NNW>(nn, na, xg, xs, D, O, sl, scale);
+        __syncwarp();
     }
     if (!ok) return;
     for (int s = 0; s < nres; s++) Xc[(int64_t)(rlo0 + s) * ldx] = xs[32 * s];

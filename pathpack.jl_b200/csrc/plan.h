@@ -11,7 +11,7 @@ namespace pp {
 // largest residual of a front in the register-resident warp sweep of the bottom of the tree
 constexpr int SWEEP_NNW = 16;
 // rows (residual range + root separator) of a subtree solved in shared memory by one warp
-constexpr int SUBTREE_ROWS = 96;
+constexpr int SUBTREE_ROWS = 64;
 // tile edge of the persistent factorization of the top of the tree
 constexpr int TOP_TILE = 64;
 

@@ -84,8 +84,9 @@ struct pp_handle {
     cudaStream_t stream = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;    // around the last solve
     cudaEvent_t fev0 = nullptr, fev1 = nullptr;  // around the last factorization
-    cudaStream_t copy_stream = nullptr;           // host-to-device copies that may overlap the handle's work
+    cudaStream_t copy_stream = nullptr;           // copies that may overlap the handle's work
     cudaEvent_t copy_ev = nullptr;
+    cudaEvent_t panel_ready[2] = {}, panel_copied[2] = {};  // double-buffered star panels to host memory
     bool factor_pending = false, solve_pending = false;  // enqueued, times not yet read
     std::string err;
     bool have_structure = false, have_values = false, factored = false;
@@ -176,6 +177,10 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
     if (e == cudaSuccess) e = cudaEventCreate(&h->fev1);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->copy_ev, cudaEventDisableTiming);
+    for (int i = 0; i < 2 && e == cudaSuccess; i++) {
+        e = cudaEventCreateWithFlags(&h->panel_ready[i], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->panel_copied[i], cudaEventDisableTiming);
+    }
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) {
         pp_destroy(h);
@@ -195,6 +200,10 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
     if (h->fev0) cudaEventDestroy(h->fev0);
     if (h->fev1) cudaEventDestroy(h->fev1);
     if (h->copy_ev) cudaEventDestroy(h->copy_ev);
+    for (int i = 0; i < 2; i++) {
+        if (h->panel_ready[i]) cudaEventDestroy(h->panel_ready[i]);
+        if (h->panel_copied[i]) cudaEventDestroy(h->panel_copied[i]);
+    }
     if (h->copy_stream) {
         cudaStreamSynchronize(h->copy_stream);
         cudaStreamDestroy(h->copy_stream);
@@ -1168,7 +1177,7 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
     pw = std::min<int64_t>(pw, (ncols + 31) & ~(int64_t)31);
     const int64_t ldx = pw;
     const size_t xbytes = es * (size_t)n * ldx;
-    const size_t sbytes = where == PP_HOST ? es * (size_t)n * pw : 0;
+    const size_t sbytes = where == PP_HOST ? 2 * es * (size_t)n * pw : 0;  // two staging panels
     if (need_memory(h, (xbytes > h->X.bytes ? xbytes : 0) + (sbytes > h->stage_out.bytes ? sbytes : 0), who) != PP_OK)
         return PP_ENOMEM;
     CK(h, h->X.ensure(xbytes), who);
@@ -1177,23 +1186,35 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
     cudaStream_t st = h->stream;
     int64_t nl = 0;
     CK(h, cudaEventRecord(h->ev0, st), who);
-    for (int64_t c0 = 0; c0 < ncols; c0 += pw) {
+    // host output: panel i is written to staging buffer i % 2 and copied to C on the copy stream while panel
+    // i + 1 is computed; panel i + 2 waits for that copy before it reuses the buffer
+    int64_t panel = 0;
+    for (int64_t c0 = 0; c0 < ncols; c0 += pw, panel++) {
         const int w = (int)std::min<int64_t>(pw, ncols - c0);
+        const int buf = (int)(panel & 1);
         CK(h, h->ops->fill_zero(h->X.p, (int64_t)n * ldx, st), who);
         CK(h, h->ops->unit_sources(h->X.p, ldx, h->hp.dev.invp, col0 + c0, w, st), who);
         CK(h, h->ops->solve(h->hp, values_of(h), 1, h->X.p, ldx, w, st, &nl), who);
-        void *dst = where == PP_HOST ? h->stage_out.p : (void *)(static_cast<char *>(C) + es * (size_t)c0 * ldc);
+        void *stage = static_cast<char *>(h->stage_out.p) + (size_t)buf * es * (size_t)n * pw;
+        void *dst = where == PP_HOST ? stage : (void *)(static_cast<char *>(C) + es * (size_t)c0 * ldc);
         const int64_t lddst = where == PP_HOST ? n : ldc;
+        if (where == PP_HOST && panel >= 2) CK(h, cudaStreamWaitEvent(st, h->panel_copied[buf], 0), who);
         const int pi = h->prof.begin(K_PERMUTE, st);
         CK(h, h->ops->rows_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
         h->prof.end(pi, st, 2.0 * n * w, 0);
         nl += 3;
         if (where == PP_HOST) {
-            CK(h, cudaMemcpy2DAsync(static_cast<char *>(C) + es * (size_t)c0 * ldc, es * ldc, h->stage_out.p, es * n,
-                                    es * n, w, cudaMemcpyDeviceToHost, st),
+            CK(h, cudaEventRecord(h->panel_ready[buf], st), who);
+            CK(h, cudaStreamWaitEvent(h->copy_stream, h->panel_ready[buf], 0), who);
+            CK(h, cudaMemcpy2DAsync(static_cast<char *>(C) + es * (size_t)c0 * ldc, es * ldc, stage, es * n, es * n, w,
+                                    cudaMemcpyDeviceToHost, h->copy_stream),
                who);
-            CK(h, cudaStreamSynchronize(st), who);  // the staging buffer is reused by the next panel
+            CK(h, cudaEventRecord(h->panel_copied[buf], h->copy_stream), who);
         }
+    }
+    if (where == PP_HOST) {
+        CK(h, cudaEventRecord(h->copy_ev, h->copy_stream), who);
+        CK(h, cudaStreamWaitEvent(st, h->copy_ev, 0), who);  // the last copies are part of the call
     }
     CK(h, cudaEventRecord(h->ev1, st), who);
     h->solve_pending = true;

@@ -38,7 +38,7 @@ constexpr int CHILD_CHUNK = 32;  // children whose ranges are staged in shared m
 
 template <typename T>
 constexpr size_t factor_top_smem() {
-    return sizeof(T) * (2 * (size_t)TB * TLD + 2 * (2 * (size_t)TB + 2));
+    return sizeof(T) * 2 * (size_t)TB * TLD;
 }
 
 // first row/column and size of tile block b of a front (pivot blocks from 0, separator blocks from nn)
@@ -185,11 +185,15 @@ __device__ __forceinline__ void tile_solve_left(T *X, const T *D, int b) {
     }
 }
 
-// partial LU of the b x b diagonal tile: warp w holds columns 8w .. 8w+7; the owner of pivot column p scales
-// it and publishes it in a double-buffered slot of sv (one barrier per pivot), every warp then updates its
-// later columns with the pivot row taken from its own registers
+// Partial LU of the b x b diagonal tile, warp-pipelined: warp w holds columns 8w .. 8w+7 (lanes: rows l and
+// l + 32).  Column p, once it has all the updates of pivots < p, is scaled by its owner and published in X
+// with a per-column flag in shared memory; a warp waits only for the columns it needs, so there is no CTA
+// barrier per pivot.  The owner of column p + 1 applies pivot p to that column first and publishes it at once
+// (a lookahead of one), then updates its other columns.  Per element the operands and their order are those
+// of lu_smem.  A wait that does not end within its bound sets *err (the tile is then garbage, the launch
+// reports the error).
 template <int SR, typename T>
-__device__ __forceinline__ void tile_lu(T *X, T *sv, int b) {
+__device__ __forceinline__ void tile_lu(T *X, int *colflag, int b, int *err) {
     using S = Sem<SR, T>;
     const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
     T x0[8], x1[8];
@@ -198,31 +202,60 @@ __device__ __forceinline__ void tile_lu(T *X, T *sv, int b) {
         x0[q] = X[l * TLD + 8 * w + q];
         x1[q] = X[(l + 32) * TLD + 8 * w + q];
     }
-    // pivots in groups of eight, the columns of warp cg: the owner's column index is a compile-time constant
+    // scale column p (slot q of this warp) by the star of its diagonal and publish it
+    auto publish = [&](int p, T &y0, T &y1) {
+        const T d = __shfl_sync(0xffffffffu, p >= 32 ? y1 : y0, p & 31);
+        if (!S::integral) {
+            const T s = S::star(d);
+            if (l > p && l < b) y0 = S::mul(y0, s);
+            if (l + 32 > p && l + 32 < b) y1 = S::mul(y1, s);
+        }
+        X[l * TLD + p] = y0;
+        X[(l + 32) * TLD + p] = y1;
+        __syncwarp();
+        __threadfence_block();
+        if (l == 0) *(volatile int *)(colflag + p) = 1;
+    };
+    if (w == 0) publish(0, x0[0], x1[0]);
     for (int cg = 0; 8 * cg < b; cg++) {
+        if (w < cg) break;  // every column of this warp is before the rest of the pivots
 #pragma unroll
         for (int qp = 0; qp < 8; qp++) {
             const int p = 8 * cg + qp;
             if (p >= b) break;
             const bool hi = p >= 32;
-            T *col = sv + (p & 1) * (2 * TB + 2);
-            const bool g0 = l > p && l < b, g1 = l + 32 > p && l + 32 < b;
-            if (w == cg) {
-                const T d = __shfl_sync(0xffffffffu, hi ? x1[qp] : x0[qp], p & 31);
-                if (!S::integral) {
-                    const T s = S::star(d);
-                    if (g0) x0[qp] = S::mul(x0[qp], s);
-                    if (g1) x1[qp] = S::mul(x1[qp], s);
+            if (w != cg) {
+                if (l == 0) {
+                    long long it = 0;
+                    while (*(volatile int *)(colflag + p) == 0)
+                        if (++it > WAIT_LIMIT) {
+                            atomicExch(err, 1);
+                            break;
+                        }
                 }
-                col[l] = x0[qp];
-                col[l + 32] = x1[qp];
+                __syncwarp();
+                __threadfence_block();
             }
-            __syncthreads();
-            const T c0 = col[l], c1 = col[l + 32];
+            const T c0 = X[l * TLD + p], c1 = X[(l + 32) * TLD + p];
+            const bool g0 = l > p && l < b, g1 = l + 32 > p && l + 32 < b;
+            // lookahead: column p + 1 first
+            if (qp < 7) {
+                if (w == cg && p + 1 < b) {
+                    const T up = __shfl_sync(0xffffffffu, hi ? x1[qp + 1] : x0[qp + 1], p & 31);
+                    if (g0) x0[qp + 1] = S::muladd(c0, up, x0[qp + 1]);
+                    if (g1) x1[qp + 1] = S::muladd(c1, up, x1[qp + 1]);
+                    publish(p + 1, x0[qp + 1], x1[qp + 1]);
+                }
+            } else if (w == cg + 1 && p + 1 < b) {
+                const T up = __shfl_sync(0xffffffffu, hi ? x1[0] : x0[0], p & 31);
+                if (g0) x0[0] = S::muladd(c0, up, x0[0]);
+                if (g1) x1[0] = S::muladd(c1, up, x1[0]);
+                publish(p + 1, x0[0], x1[0]);
+            }
 #pragma unroll
             for (int q = 0; q < 8; q++) {
                 const int c = 8 * w + q;
-                if (c > p && c < b) {
+                if (c > p + 1 && c < b) {
                     const T up = __shfl_sync(0xffffffffu, hi ? x1[q] : x0[q], p & 31);
                     if (g0) x0[q] = S::muladd(c0, up, x0[q]);
                     if (g1) x1[q] = S::muladd(c1, up, x1[q]);
@@ -247,13 +280,13 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *As = reinterpret_cast<T *>(smem_raw);  // [TB][TLD]: A operand (rows x k), or the diagonal tile
     T *Bs = As + TB * TLD;                     // [TB][TLD]: B operand (k x columns)
-    T *sv = Bs + TB * TLD;                     // 2 x [column TB | row TB | 2]: pivot broadcasts, double-buffered
     int *next = flags;
     __shared__ int4 s_child[CHILD_CHUNK];  // per child: first row, rows, first column, columns in this tile
     __shared__ int64_t s_cmat[CHILD_CHUNK];
     __shared__ int2 s_cmeta[CHILD_CHUNK];  // leading dimension of the update matrix, offset of rel
     __shared__ int s_ctop[CHILD_CHUNK];    // the child if it is a top front, else -1
     __shared__ int s_bad;
+    __shared__ int s_colflag[TB];  // published pivot columns of the diagonal tile's LU
     const int tid = threadIdx.x, tc = tid & 15, tr = tid >> 4;
     const T z = S::zero();
 
@@ -396,10 +429,11 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
                 Bs[r * TLD + c] = (r < b && c < b) ? ld_cg(F + (d0 + r) + (int64_t)(d0 + c) * nj) : z;
             }
         }
+        if (pivot_region && I == J && tid < TB) s_colflag[tid] = 0;
         __syncthreads();
         if (pivot_region) {
             if (I == J)
-                tile_lu<SR, T>(As, sv, mi);
+                tile_lu<SR, T>(As, s_colflag, mi, err);
             else if (I > J)
                 tile_solve_right<SR, T>(As, Bs, mj);
             else

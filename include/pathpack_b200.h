@@ -110,8 +110,11 @@ int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t where);
 int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, const void *LD, const void *LL, const void *UD,
                       const void *UL, const void *Nval);
 
-/* Factorize the star, A* = U* L*, in place on the device (enqueued; see the conventions above).  Replaces
-   lu!(F) -> sgetrf!(F), src/CPU/abstract_slu.jl:119-121 and src/CPU/chordal/sgetrf.jl:3-290. */
+/* Factorize the star, A* = U* L*, in place on the device (enqueued; see the conventions above).  The top of
+   the elimination tree is factored on a second, higher-priority stream of the handle, so that a solve enqueued
+   next sweeps the bottom of the tree meanwhile; every call of the handle orders itself after it, and pp_sync
+   waits for it.  Replaces lu!(F) -> sgetrf!(F), src/CPU/abstract_slu.jl:119-121 and
+   src/CPU/chordal/sgetrf.jl:3-290. */
 int32_t pp_factor(pp_handle *h);
 
 /* Download the factor arrays to the host (any pointer may be NULL). */
@@ -164,7 +167,9 @@ typedef struct pp_kernel_class {
 int32_t pp_set_profile(pp_handle *h, int32_t on);
 int32_t pp_get_profile(pp_handle *h, pp_kernel_class *out, int32_t max, int32_t *count);
 
-/* The handle's CUDA stream (a cudaStream_t), for callers that order their own work after the handle's. */
+/* The handle's CUDA stream (a cudaStream_t), for callers that order their own work after the handle's: work
+   ordered after it follows every call enqueued before (the solves included); only the top of a factorization
+   that no solve has followed yet may still be running (pp_sync waits for it). */
 void *pp_stream(pp_handle *h);
 
 /* ---- dense kernels on caller device memory (ordered on `stream`, a cudaStream_t or NULL) ---- */

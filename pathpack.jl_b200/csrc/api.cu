@@ -85,6 +85,11 @@ struct pp_handle {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;    // around the last solve
     cudaEvent_t fev0 = nullptr, fev1 = nullptr;  // around the last factorization
     cudaStream_t copy_stream = nullptr;           // copies that may overlap the handle's work
+    // the top of the tree is factored on its own stream: a solve enqueued next on the handle's stream runs its
+    // bottom sweeps meanwhile and waits for ev_factored before its top sweeps; every other call that reads or
+    // writes the factor makes the handle's stream wait for ev_factored first (after_factor)
+    cudaStream_t factor_stream = nullptr;
+    cudaEvent_t ev_bottom = nullptr, ev_factored = nullptr;
     cudaEvent_t copy_ev = nullptr;
     cudaEvent_t panel_ready[2] = {}, panel_copied[2] = {};  // double-buffered star panels to host memory
     bool factor_pending = false, solve_pending = false;  // enqueued, times not yet read
@@ -101,6 +106,7 @@ struct pp_handle {
         d_fpending0, d_spending0, d_sdone0, d_tpending0, d_sync, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags, d_croff,
         d_crng, d_err;
     std::vector<int> pnt, height, rel;
+    std::vector<int> sfronts, sroots;  // host copies of the solve work lists (reordered by prepare_workspace)
     int maxh = 0;
     // values and work
     DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val;
@@ -170,7 +176,12 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
     if (!h) return fail(nullptr, PP_ENOMEM, "pp_create: out of host memory");
     h->device = device;
     e = cudaSetDevice(device);
-    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
+    int prio_low = 0, prio_high = 0;
+    if (e == cudaSuccess) e = cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high);
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&h->stream, cudaStreamNonBlocking, prio_low);
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&h->factor_stream, cudaStreamNonBlocking, prio_high);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->ev_bottom, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->ev_factored, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev1);
     if (e == cudaSuccess) e = cudaEventCreate(&h->fev0);
@@ -200,6 +211,12 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
     if (h->fev0) cudaEventDestroy(h->fev0);
     if (h->fev1) cudaEventDestroy(h->fev1);
     if (h->copy_ev) cudaEventDestroy(h->copy_ev);
+    if (h->factor_stream) {
+        cudaStreamSynchronize(h->factor_stream);
+        cudaStreamDestroy(h->factor_stream);
+    }
+    for (cudaEvent_t ev : {h->ev_bottom, h->ev_factored})
+        if (ev) cudaEventDestroy(ev);
     for (int i = 0; i < 2; i++) {
         if (h->panel_ready[i]) cudaEventDestroy(h->panel_ready[i]);
         if (h->panel_copied[i]) cudaEventDestroy(h->panel_copied[i]);
@@ -228,6 +245,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         return fail(h, PP_EINVAL, "pp_set_structure: null array");
     if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_set_structure: base must be 0 or 1");
     cudaSetDevice(h->device);
+    if (h->factor_stream) cudaStreamSynchronize(h->factor_stream);  // nothing in flight reads the old plan
     h->have_structure = h->have_values = h->factored = false;
     h->nnz_assembled = -1;
     HostPlan hp;
@@ -584,8 +602,13 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         hp.d_err = h->d_err.as<int>();
         hp.sync_cap = 32 * nf + 16;
         hp.sm_count = h->sm_count;
+        hp.ev_bottom = h->ev_bottom;
+        hp.ev_factored = h->ev_factored;
+        hp.top_stream = h->factor_stream;
         h->invp = invp;
         h->pnt = pnt;
+        h->sfronts = sfronts;
+        h->sroots = sroots;
         h->height = height;  // factorization heights and rel, kept for prepare_workspace
         h->rel = rel;
         h->maxh = maxh;
@@ -674,6 +697,29 @@ static int32_t prepare_workspace(pp_handle *h) {
     hp.ws_elems = off;
     const int maxh = h->maxh;
     cudaStream_t st = h->stream;
+    CK(h, cudaStreamSynchronize(h->factor_stream), "prepare_workspace");
+    CK(h, cudaStreamSynchronize(st), "prepare_workspace");
+    // stage 0 of each solve direction lists the subtrees and forward bottom fronts that the bottom kernel
+    // factors first: a solve sweeps them while the top of the tree is factored.  fbot holds every child of a
+    // front it holds, so the stable partition keeps each child before its parent.
+    for (int d = 0; d < 2; d++) {
+        const std::vector<SubtreeList> &subs = d ? hp.sub_r : hp.sub_l;
+        const std::vector<std::pair<int64_t, int>> &fw = d ? hp.sb_fwd_r : hp.sb_fwd;
+        hp.early_sub[d] = hp.early_bot[d] = 0;
+        auto in_bottom = [&](int f) { return fbot[f] != 0; };
+        if (!subs.empty() && subs[0].count > 0) {
+            int *r = h->sroots.data() + subs[0].off;
+            hp.early_sub[d] = (int)(std::stable_partition(r, r + subs[0].count, in_bottom) - r);
+        }
+        if (!fw.empty() && fw[0].second > 0) {
+            int *b = h->sfronts.data() + fw[0].first;
+            hp.early_bot[d] = (int)(std::stable_partition(b, b + fw[0].second, in_bottom) - b);
+        }
+    }
+    CK(h, upload(h->d_sroots, h->sroots, st), "upload");
+    CK(h, upload(h->d_sfronts, h->sfronts, st), "upload");
+    hp.d_sroots = h->d_sroots.as<int>();
+    hp.d_sfronts = h->d_sfronts.as<int>();
     {
         std::vector<std::vector<int>> byh(maxh + 1);
         std::vector<int> pending0(nf, 0);
@@ -803,12 +849,17 @@ static Values values_of(pp_handle *h) {
     return v;
 }
 
+// The handle's stream waits for the top of the last factorization (a no-op if there was none): every call that
+// writes the factor's values or workspace orders itself after it this way.
+static cudaError_t after_factor(pp_handle *h) { return cudaStreamWaitEvent(h->stream, h->ev_factored, 0); }
+
 extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, const int64_t *colptr,
                                const int64_t *rowval, const void *nzval, int32_t base) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_assemble: null handle");
     if (!h->have_structure) return fail(h, PP_ESTATE, "pp_assemble: no structure (call pp_set_structure first)");
     if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_assemble: base must be 0 or 1");
     cudaSetDevice(h->device);
+    CK(h, cudaStreamSynchronize(h->factor_stream), "pp_assemble");  // buffers may be reallocated below
     int32_t r = set_semiring(h, semiring, dtype, "pp_assemble");
     if (r != PP_OK) return r;
     const int n = h->hp.n;
@@ -877,6 +928,7 @@ extern "C" int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t whe
             if (a[p] < 0) return fail(h, PP_EUNSUPPORTED, "pp_update_values: Int32 MinPlus takes weights in [0, INT32_MAX]");
     }
     cudaStream_t st = h->stream;
+    CK(h, after_factor(h), "pp_update_values");
     if (nnz > 0)
         CK(h, cudaMemcpyAsync(h->csc_val.p, nzval, es * nnz, where == PP_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
                               st), "pp_update_values");
@@ -896,6 +948,7 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
     if (!h) return fail(nullptr, PP_EINVAL, "pp_set_values: null handle");
     if (!h->have_structure) return fail(h, PP_ESTATE, "pp_set_values: no structure");
     cudaSetDevice(h->device);
+    CK(h, cudaStreamSynchronize(h->factor_stream), "pp_set_values");
     int32_t r = set_semiring(h, semiring, dtype, "pp_set_values");
     if (r != PP_OK) return r;
     const size_t es = h->ops->esize;
@@ -917,6 +970,7 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
 // Wait for the handle's stream, then take the times of the calls enqueued since the last wait and the error
 // word of the persistent kernels (set when a bounded wait expired; cleared once reported).
 static int32_t settle(pp_handle *h, const char *who) {
+    CK(h, cudaStreamSynchronize(h->factor_stream), who);
     CK(h, cudaStreamSynchronize(h->stream), who);
     if (h->factor_pending) {
         float ms = 0;
@@ -947,15 +1001,18 @@ extern "C" int32_t pp_factor(pp_handle *h) {
     cudaSetDevice(h->device);
     const size_t wbytes = h->ops->esize * std::max<int64_t>(h->hp.ws_elems, 1);
     if (wbytes > h->W.bytes) {
+        CK(h, cudaStreamSynchronize(h->factor_stream), "pp_factor");
+        CK(h, cudaStreamSynchronize(h->stream), "pp_factor");
         h->W.release();
         if (need_memory(h, wbytes, "pp_factor") != PP_OK) return PP_ENOMEM;
         CK(h, h->W.ensure(wbytes), "pp_factor");
     }
     cudaStream_t st = h->stream;
     int64_t nl = 0;
+    CK(h, after_factor(h), "pp_factor");  // the previous top factorization reads the bottom's update matrices
     CK(h, cudaEventRecord(h->fev0, st), "pp_factor");
     CK(h, h->ops->factor(h->hp, values_of(h), st, &nl), "pp_factor");
-    CK(h, cudaEventRecord(h->fev1, st), "pp_factor");
+    CK(h, cudaEventRecord(h->fev1, h->factor_stream), "pp_factor");  // the top of the tree ends there
     h->factor_pending = true;
     h->st.kernel_launches = nl;
     h->factored = true;

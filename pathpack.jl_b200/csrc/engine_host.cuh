@@ -2,8 +2,10 @@
 // (semiring, element type) in ops_*.cu.
 //
 // Factorization: one persistent launch for the bottom of the tree (factor_bottom_kernel), then one for the
-// rest (factor_top_kernel, tile tasks).  Solves: per coupling stage and direction, one persistent launch each
-// for the subtrees that fit shared memory, the other bottom fronts and the top fronts (sweep_top_kernel).
+// rest (factor_top_kernel, tile tasks) on a second stream, so that a solve enqueued behind it runs its bottom
+// sweeps while the top of the tree is being factored.  Solves: per coupling stage and direction, one persistent
+// launch each for the subtrees that fit shared memory, the other bottom fronts and the top fronts
+// (sweep_top_kernel).
 #pragma once
 
 #include <algorithm>
@@ -96,20 +98,27 @@ struct Engine {
             if (pi >= 0) hp.prof->end(pi, st, hp.fb_bytes, hp.fb_pairs);
             nl++;
         }
+        cudaStream_t ts = st;
+        if (hp.top_stream && hp.ev_bottom && hp.ev_factored) {
+            ts = hp.top_stream;
+            PP_TRY(cudaEventRecord(hp.ev_bottom, st));
+            PP_TRY(cudaStreamWaitEvent(ts, hp.ev_bottom, 0));
+        }
         if (hp.top_ntasks > 0) {
             constexpr size_t smem = factor_top_smem<T>();
-            PP_TRY(cudaMemsetAsync(hp.d_tflags, 0, sizeof(int) * (size_t)hp.tflags_n, st));
+            PP_TRY(cudaMemsetAsync(hp.d_tflags, 0, sizeof(int) * (size_t)hp.tflags_n, ts));
             int per_sm = 1;
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, factor_top_kernel<SR, T>, 256, smem);
             const int grid = std::max(1, std::min(hp.top_ntasks, std::max(per_sm, 1) * hp.sm_count));
-            const int pi = hp.prof ? hp.prof->begin(K_FACTOR_TOP, st) : -1;
-            factor_top_kernel<SR, T><<<grid, 256, smem, st>>>(hp.d_ttasks, hp.top_ntasks, hp.dev, hp.d_tfoff,
+            const int pi = hp.prof ? hp.prof->begin(K_FACTOR_TOP, ts) : -1;
+            factor_top_kernel<SR, T><<<grid, 256, smem, ts>>>(hp.d_ttasks, hp.top_ntasks, hp.dev, hp.d_tfoff,
                                                               hp.d_croff, hp.d_crng, LD, LL, UD, UL, W, hp.d_tflags,
                                                               hp.d_err);
             PP_TRY(cudaGetLastError());
-            if (pi >= 0) hp.prof->end(pi, st, hp.top_cost.bytes, hp.top_cost.pairs);
+            if (pi >= 0) hp.prof->end(pi, ts, hp.top_cost.bytes, hp.top_cost.pairs);
             nl++;
         }
+        if (ts != st) PP_TRY(cudaEventRecord(hp.ev_factored, ts));
         if (launches) *launches += nl;
         return cudaSuccess;
     }
@@ -152,13 +161,18 @@ struct Engine {
         return cudaSuccess;
     }
 
+    // reset = false continues the counters of the previous launch over the same list (its second part)
     template <bool FWD, bool TRANS>
     static cudaError_t sweep_bottom(const HostPlan &hp, const std::pair<int64_t, int> &wl, const SLevel &cost,
                                     const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
-                                    int64_t *nl) {
+                                    int64_t *nl, bool reset = true) {
         if (wl.second == 0) return cudaSuccess;
         const int ntiles = (k + 31) / 32;
-        PP_TRY(reset_sync(hp, FWD ? hp.d_spending0 : hp.d_sdone0, ntiles, st));
+        if (reset) {
+            PP_TRY(reset_sync(hp, FWD ? hp.d_spending0 : hp.d_sdone0, ntiles, st));
+        } else {
+            PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int), st));
+        }
         const int fmax = std::max(hp.bot_fmax, 1), namax = std::max(hp.bot_namax, 1);
         const size_t smem = 8 * bottom_warp_bytes<T>(fmax, namax);
         int dev = 0;
@@ -208,6 +222,36 @@ struct Engine {
         return cudaSuccess;
     }
 
+    // The forward sweep of the bottom of stage s (subtrees, then the other bottom fronts).  In stage 0 the
+    // fronts factored by the bottom kernel come first; the stream then waits for the end of the factorization
+    // (a no-op once it has ended) and sweeps the rest.
+    template <bool TRANS>
+    static cudaError_t forward_bottom(const HostPlan &hp, int d, size_t s, const T *Dv, const T *Ov, T *X,
+                                      int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
+        const SubtreeList &sub = (d ? hp.sub_r : hp.sub_l)[s];
+        const std::pair<int64_t, int> &bot = (d ? hp.sb_fwd_r : hp.sb_fwd)[s];
+        const SLevel &cost = (d ? hp.sb_cost_r : hp.sb_cost_l)[s];
+        if (s > 0 || !hp.ev_factored) {
+            PP_TRY((sweep_subtrees<true, TRANS>(hp, sub, Dv, Ov, X, ldx, k, unit, st, nl)));
+            return sweep_bottom<true, TRANS>(hp, bot, cost, Dv, Ov, X, ldx, k, unit, st, nl);
+        }
+        SubtreeList sa = sub, sb = sub;
+        sa.count = std::min(hp.early_sub[d], sub.count);
+        sb.off = sub.off + sa.count;
+        sb.count = sub.count - sa.count;
+        std::pair<int64_t, int> ba = bot, bb = bot;
+        ba.second = std::min(hp.early_bot[d], bot.second);
+        bb.first = bot.first + ba.second;
+        bb.second = bot.second - ba.second;
+        const SLevel none{};  // the profile counts the list's bytes and pairs once, with its first launch
+        PP_TRY((sweep_subtrees<true, TRANS>(hp, sa, Dv, Ov, X, ldx, k, unit, st, nl)));
+        PP_TRY((sweep_bottom<true, TRANS>(hp, ba, cost, Dv, Ov, X, ldx, k, unit, st, nl)));
+        PP_TRY(cudaStreamWaitEvent(st, hp.ev_factored, 0));
+        PP_TRY((sweep_subtrees<true, TRANS>(hp, sb, Dv, Ov, X, ldx, k, unit, st, nl)));
+        return sweep_bottom<true, TRANS>(hp, bb, ba.second ? none : cost, Dv, Ov, X, ldx, k, unit, st, nl,
+                                         ba.second == 0);
+    }
+
     // left: lmul! (X <- A* X: per stage L* forward, U* backward, then the coupling scatter);
     // otherwise rmul! on the transposed layout (per stage the coupling gather, then U* forward, L* backward).
     // src/CPU/blocked/sgetrs.jl:203-255 and src/CPU/chordal/sgetrs.jl:29-51.
@@ -221,8 +265,7 @@ struct Engine {
         if (left) {
             for (size_t s = 0; s < hp.lstages.size(); s++) {
                 const Stage &sg = hp.lstages[s];
-                PP_TRY((sweep_subtrees<true, false>(hp, hp.sub_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
-                PP_TRY((sweep_bottom<true, false>(hp, hp.sb_fwd[s], hp.sb_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
+                PP_TRY((forward_bottom<false>(hp, 0, s, LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_top<true, false>(hp, hp.st_fwd[s], hp.st_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_top<false, false>(hp, hp.st_bwd[s], hp.st_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_bottom<false, false>(hp, hp.sb_bwd[s], hp.sb_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
@@ -247,8 +290,7 @@ struct Engine {
                     if (pi >= 0) hp.prof->end(pi, st, 0, 0);
                     nl++;
                 }
-                PP_TRY((sweep_subtrees<true, true>(hp, hp.sub_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
-                PP_TRY((sweep_bottom<true, true>(hp, hp.sb_fwd_r[s], hp.sb_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
+                PP_TRY((forward_bottom<true>(hp, 1, s, UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_top<true, true>(hp, hp.st_fwd_r[s], hp.st_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_top<false, true>(hp, hp.st_bwd_r[s], hp.st_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_bottom<false, true>(hp, hp.sb_bwd_r[s], hp.sb_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));

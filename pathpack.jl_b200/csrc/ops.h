@@ -130,6 +130,13 @@ struct HostPlan {
     const int *d_tpending0 = nullptr;  // top children per front (forward counters of the top sweep)
     int *d_sync = nullptr;             // scratch: [0] task counter, [16, 16 + nf * tiles) counters
     int *d_err = nullptr;              // set by a persistent kernel whose bounded wait expired
+    // The top of the tree is factored on top_stream, after ev_bottom (recorded on the calling stream behind the
+    // bottom kernel); ev_factored marks its end.  A solve enqueued behind the factorization runs the first
+    // early_sub[d] subtrees and early_bot[d] forward bottom fronts of its stage 0 (d = 0 lmul!, 1 rmul!; all of
+    // them factored by the bottom kernel, listed first) before it waits for ev_factored.
+    cudaStream_t top_stream = nullptr;
+    cudaEvent_t ev_bottom = nullptr, ev_factored = nullptr;
+    int early_sub[2] = {0, 0}, early_bot[2] = {0, 0};
     int64_t sync_cap = 0;              // ints allocated at d_sync
     int sm_count = 148;
 };

@@ -14,10 +14,11 @@
 //   PlusProd (+, *)     zero 0     one 1     star a < 1 ? 1/(1-a) : +Inf real.jl:17-66, smuladd = fma
 //   OrAnd    (|, &)     zero 0     one INT32_MAX  integral               boolean.jl:31-79
 //
-// A floating product that is NaN (Inf + -Inf, Inf * 0) is szero (tropical.jl:164-182); min/max here are
-// fminf/fmaxf, which also drop a NaN sum, as the reference's GPU kernels do (llvm.minnum,
-// ext/PATHPACKCUDAExt.jl:46-49).  They differ from the CPU's select (x < y ? x : y) only on +0/-0 ties
-// and NaN accumulators, neither of which the solver produces from NaN-free inputs without -0.0 weights.
+// A floating product that is NaN (Inf + -Inf, Inf * 0) is szero (tropical.jl:164-182).  Float64 min/max are
+// the CPU's select (x < y ? x : y, vmin_d / vmax_d below); Float32 min/max are fminf/fmaxf, which also drop a
+// NaN sum, as the reference's GPU kernels do (llvm.minnum, ext/PATHPACKCUDAExt.jl:46-49).  Those differ from
+// the select only on +0/-0 ties and NaN accumulators, neither of which the solver produces from NaN-free
+// inputs without -0.0 weights.
 //
 // Int32 MinPlus is defined on [0, INT32_MAX] with a saturating product: operands are non-negative, so the
 // 32-bit unsigned sum cannot wrap and min(a + b, c) over unsigned values with c <= INT32_MAX is the
@@ -335,5 +336,20 @@ struct Sem<ORAND, int32_t> {
     static __device__ __forceinline__ T star(T) { return one(); }
     static __device__ __forceinline__ void atomic_add(T *p, T v) { atomicOr(p, v); }
 };
+
+// pred ? muladd(a, b, c) : c.  For Float64 (min, +) and (max, +) the predicate folds into the select of the
+// (+): x = pred && a * b < c ? a * b : c is vmin_d(a * b, c) with the same operands.
+template <int SR, typename T>
+__device__ __forceinline__ T muladd_if(bool pred, T a, T b, T c) {
+    if constexpr ((SR == MINPLUS || SR == MAXPLUS) && sizeof(T) == 8 && !Sem<SR, T>::integral) {
+        const T t = a + b;
+        if constexpr (SR == MINPLUS)
+            return (pred && t < c) ? t : c;
+        else
+            return (pred && t > c) ? t : c;
+    } else {
+        return pred ? Sem<SR, T>::muladd(a, b, c) : c;
+    }
+}
 
 }  // namespace pp

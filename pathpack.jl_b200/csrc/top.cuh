@@ -133,16 +133,16 @@ __device__ __forceinline__ void tile_solve_right(T *X, const T *D, int b) {
     auto step = [&](int p, auto half) {
         constexpr bool hi = decltype(half)::hi;
         const T s = S::integral ? S::one() : S::star(D[p * TLD + p]);
-        const T u0 = D[p * TLD + l], u1 = D[p * TLD + l + 32];
-        const bool g0 = l > p && l < b, g1 = l + 32 > p && l + 32 < b;
+        const T u0 = hi ? S::zero() : D[p * TLD + l], u1 = D[p * TLD + l + 32];
+        const bool g0 = !hi && l > p && l < b, g1 = l + 32 > p && l + 32 < b;  // rows < 32 are done when hi
 #pragma unroll
         for (int q = 0; q < 8; q++) {
             T xp = __shfl_sync(0xffffffffu, hi ? x1[q] : x0[q], p & 31);
             if (!S::integral) xp = S::mul(xp, s);
             if (!hi && l == p) x0[q] = xp;
             if (hi && l + 32 == p) x1[q] = xp;
-            if (g0) x0[q] = S::muladd(xp, u0, x0[q]);
-            if (g1) x1[q] = S::muladd(xp, u1, x1[q]);
+            if (!hi) x0[q] = muladd_if<SR, T>(g0, xp, u0, x0[q]);
+            x1[q] = muladd_if<SR, T>(g1, xp, u1, x1[q]);
         }
     };
     for (int p = 0; p < min(b, 32); p++) step(p, Half<false>());
@@ -167,13 +167,13 @@ __device__ __forceinline__ void tile_solve_left(T *X, const T *D, int b) {
     }
     auto step = [&](int p, auto half) {
         constexpr bool hi = decltype(half)::hi;
-        const T l0 = D[l * TLD + p], l1 = D[(l + 32) * TLD + p];
-        const bool g0 = l > p && l < b, g1 = l + 32 > p && l + 32 < b;
+        const T l0 = hi ? S::zero() : D[l * TLD + p], l1 = D[(l + 32) * TLD + p];
+        const bool g0 = !hi && l > p && l < b, g1 = l + 32 > p && l + 32 < b;  // rows < 32 are done when hi
 #pragma unroll
         for (int q = 0; q < 8; q++) {
             const T xp = __shfl_sync(0xffffffffu, hi ? x1[q] : x0[q], p & 31);
-            if (g0) x0[q] = S::muladd(l0, xp, x0[q]);
-            if (g1) x1[q] = S::muladd(l1, xp, x1[q]);
+            if (!hi) x0[q] = muladd_if<SR, T>(g0, l0, xp, x0[q]);
+            x1[q] = muladd_if<SR, T>(g1, l1, xp, x1[q]);
         }
     };
     for (int p = 0; p < min(b, 32); p++) step(p, Half<false>());
@@ -185,13 +185,15 @@ __device__ __forceinline__ void tile_solve_left(T *X, const T *D, int b) {
     }
 }
 
-// Partial LU of the b x b diagonal tile, warp-pipelined: warp w holds columns 8w .. 8w+7 (lanes: rows l and
-// l + 32).  Column p, once it has all the updates of pivots < p, is scaled by its owner and published in X
-// with a per-column flag in shared memory; a warp waits only for the columns it needs, so there is no CTA
-// barrier per pivot.  The owner of column p + 1 applies pivot p to that column first and publishes it at once
-// (a lookahead of one), then updates its other columns.  Per element the operands and their order are those
-// of lu_smem.  A wait that does not end within its bound sets *err (the tile is then garbage, the launch
-// reports the error).
+// Partial LU of the b x b diagonal tile, warp-pipelined.  Columns are dealt round-robin: warp w holds columns
+// w, w + 8, ... (lanes: rows l and l + 32), slot 0 being its column of the current group of eight pivots (the
+// slots move down after each group).  Column p + 1 belongs to warp (p + 1) & 7: once it has pivot p, that warp
+// scales it by the star of its diagonal and publishes it in X with a per-column flag in shared memory, before
+// its other columns take pivot p, so consecutive pivots are published by different warps and the next
+// lookahead never waits behind a warp's own updates.  Pivots p >= 32 touch rows l + 32 only and at most four
+// slots.  Every column is final when published, so X holds the factored tile at the end.  Per element the
+// operands and their order are those of lu_smem.  A wait that does not end within its bound sets *err (the
+// tile is then garbage, the launch reports the error).
 template <int SR, typename T>
 __device__ __forceinline__ void tile_lu(T *X, int *colflag, int b, int *err) {
     using S = Sem<SR, T>;
@@ -199,10 +201,9 @@ __device__ __forceinline__ void tile_lu(T *X, int *colflag, int b, int *err) {
     T x0[8], x1[8];
 #pragma unroll
     for (int q = 0; q < 8; q++) {
-        x0[q] = X[l * TLD + 8 * w + q];
-        x1[q] = X[(l + 32) * TLD + 8 * w + q];
+        x0[q] = X[l * TLD + 8 * q + w];
+        x1[q] = X[(l + 32) * TLD + 8 * q + w];
     }
-    // scale column p (slot q of this warp) by the star of its diagonal and publish it
     auto publish = [&](int p, T &y0, T &y1) {
         const T d = __shfl_sync(0xffffffffu, p >= 32 ? y1 : y0, p & 31);
         if (!S::integral) {
@@ -216,58 +217,56 @@ __device__ __forceinline__ void tile_lu(T *X, int *colflag, int b, int *err) {
         __threadfence_block();
         if (l == 0) *(volatile int *)(colflag + p) = 1;
     };
-    if (w == 0) publish(0, x0[0], x1[0]);
-    for (int cg = 0; 8 * cg < b; cg++) {
-        if (w < cg) break;  // every column of this warp is before the rest of the pivots
+    auto group = [&](int pg, auto half) {
+        constexpr bool HI = decltype(half)::hi;
+        constexpr int NS = HI ? 4 : 8;  // live slots
 #pragma unroll
         for (int qp = 0; qp < 8; qp++) {
-            const int p = 8 * cg + qp;
-            if (p >= b) break;
-            const bool hi = p >= 32;
-            if (w != cg) {
-                if (l == 0) {
-                    long long it = 0;
-                    while (*(volatile int *)(colflag + p) == 0)
-                        if (++it > WAIT_LIMIT) {
-                            atomicExch(err, 1);
-                            break;
-                        }
+            const int p = 8 * pg + qp;
+            if (p < b) {
+                if (w != qp) {  // column p is warp qp's
+                    if (l == 0) {
+                        long long it = 0;
+                        while (*(volatile int *)(colflag + p) == 0)
+                            if (++it > WAIT_LIMIT) {
+                                atomicExch(err, 1);
+                                break;
+                            }
+                    }
+                    __syncwarp();
+                    __threadfence_block();
                 }
-                __syncwarp();
-                __threadfence_block();
-            }
-            const T c0 = X[l * TLD + p], c1 = X[(l + 32) * TLD + p];
-            const bool g0 = l > p && l < b, g1 = l + 32 > p && l + 32 < b;
-            // lookahead: column p + 1 first
-            if (qp < 7) {
-                if (w == cg && p + 1 < b) {
-                    const T up = __shfl_sync(0xffffffffu, hi ? x1[qp + 1] : x0[qp + 1], p & 31);
-                    if (g0) x0[qp + 1] = S::muladd(c0, up, x0[qp + 1]);
-                    if (g1) x1[qp + 1] = S::muladd(c1, up, x1[qp + 1]);
-                    publish(p + 1, x0[qp + 1], x1[qp + 1]);
+                const T c0 = HI ? S::zero() : X[l * TLD + p], c1 = X[(l + 32) * TLD + p];
+                const bool g0 = !HI && l > p && l < b, g1 = l + 32 > p && l + 32 < b;
+                // lookahead: column p + 1 is slot 0 of warp qp + 1, or slot 1 of warp 0 after the group
+                const int la_w = (qp + 1) & 7, la_s = qp < 7 ? 0 : 1;
+                if (w == la_w && p + 1 < b) {
+                    const T up = __shfl_sync(0xffffffffu, HI ? x1[la_s] : x0[la_s], p & 31);
+                    if (!HI) x0[la_s] = muladd_if<SR, T>(g0, c0, up, x0[la_s]);
+                    x1[la_s] = muladd_if<SR, T>(g1, c1, up, x1[la_s]);
+                    publish(p + 1, x0[la_s], x1[la_s]);
                 }
-            } else if (w == cg + 1 && p + 1 < b) {
-                const T up = __shfl_sync(0xffffffffu, hi ? x1[0] : x0[0], p & 31);
-                if (g0) x0[0] = S::muladd(c0, up, x0[0]);
-                if (g1) x1[0] = S::muladd(c1, up, x1[0]);
-                publish(p + 1, x0[0], x1[0]);
-            }
+                T up[NS];
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                const int c = 8 * w + q;
-                if (c > p + 1 && c < b) {
-                    const T up = __shfl_sync(0xffffffffu, hi ? x1[q] : x0[q], p & 31);
-                    if (g0) x0[q] = S::muladd(c0, up, x0[q]);
-                    if (g1) x1[q] = S::muladd(c1, up, x1[q]);
+                for (int sl = 0; sl < NS; sl++) up[sl] = __shfl_sync(0xffffffffu, HI ? x1[sl] : x0[sl], p & 31);
+#pragma unroll
+                for (int sl = 0; sl < NS; sl++) {
+                    const int c = w + 8 * (pg + sl);
+                    const bool on = c > p + 1 && c < b;
+                    if (!HI) x0[sl] = muladd_if<SR, T>(on && g0, c0, up[sl], x0[sl]);
+                    x1[sl] = muladd_if<SR, T>(on && g1, c1, up[sl], x1[sl]);
                 }
             }
         }
-    }
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-        X[l * TLD + 8 * w + q] = x0[q];
-        X[(l + 32) * TLD + 8 * w + q] = x1[q];
-    }
+        for (int sl = 0; sl < 7; sl++) {
+            x0[sl] = x0[sl + 1];
+            x1[sl] = x1[sl + 1];
+        }
+    };
+    if (w == 0) publish(0, x0[0], x1[0]);
+    for (int pg = 0; pg < 4 && 8 * pg < b; pg++) group(pg, Half<false>());
+    for (int pg = 4; 8 * pg < b; pg++) group(pg, Half<true>());
 }
 
 template <int SR, typename T>

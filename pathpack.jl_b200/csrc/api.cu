@@ -12,6 +12,7 @@
 #include <cstring>
 #include <memory>
 #include <new>
+#include <queue>
 #include <string>
 #include <vector>
 
@@ -233,6 +234,71 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
 extern "C" void *pp_stream(pp_handle *h) { return h ? (void *)h->stream : nullptr; }
 
 // ---------------------------------------------------------------- structure
+
+// Order of the fronts of one persistent bottom-sweep launch.  The launch hands its (front, 32-column tile)
+// tasks to warps in list order and a warp whose task is not ready waits, so the list follows a schedule
+// simulated on the host: `slots` fronts at a time (the launch's warps over the tiles of a front), a front
+// costing about 4 + nn * na / 36 (microseconds, fitted to measured task times), ready once its dependencies
+// are done (the backward sweep: its parent; the forward sweep: its children in the list), the ready front with
+// the longest path of remaining work first.  Every front comes after the fronts it depends on.
+static std::vector<int> sweep_order(const std::vector<int> &fronts, const std::vector<int> &nn,
+                                    const std::vector<int> &na, const std::vector<int> &pnt, bool fwd, int slots) {
+    const int m = (int)fronts.size();
+    std::vector<int> pos(pnt.size(), -1);
+    for (int i = 0; i < m; i++) pos[fronts[i]] = i;
+    std::vector<double> cost(m), path(m, 0.0);
+    std::vector<int> deps(m, 0), par(m, -1);
+    for (int i = 0; i < m; i++) {
+        const int f = fronts[i];
+        cost[i] = 4.0 + nn[f] * (double)na[f] / 36.0;
+        par[i] = pnt[f] >= 0 ? pos[pnt[f]] : -1;
+    }
+    // the fronts arrive in height order (ascending for the forward list, descending for the backward one), so
+    // a parent's position is after (forward) or before (backward) its children's
+    std::vector<std::vector<int>> kids(m);
+    for (int i = 0; i < m; i++)
+        if (par[i] >= 0) kids[par[i]].push_back(i);
+    if (fwd) {
+        for (int i = m - 1; i >= 0; i--) path[i] = cost[i] + (par[i] >= 0 ? path[par[i]] : 0.0);
+        for (int i = 0; i < m; i++) deps[i] = (int)kids[i].size();
+    } else {
+        for (int i = m - 1; i >= 0; i--) {
+            double mx = 0;
+            for (int c : kids[i]) mx = std::max(mx, path[c]);
+            path[i] = cost[i] + mx;
+        }
+        for (int i = 0; i < m; i++) deps[i] = par[i] >= 0 ? 1 : 0;
+    }
+    using Ready = std::pair<double, int>;  // (remaining path, front)
+    std::priority_queue<Ready> ready;
+    using Run = std::pair<double, int>;  // (finish time, front), earliest first
+    std::priority_queue<Run, std::vector<Run>, std::greater<Run>> running;
+    for (int i = 0; i < m; i++)
+        if (deps[i] == 0) ready.push({path[i], i});
+    std::vector<int> order;
+    order.reserve(m);
+    double now = 0;
+    while ((int)order.size() < m) {
+        while (!ready.empty() && (int)running.size() < std::max(slots, 1)) {
+            const int i = ready.top().second;
+            ready.pop();
+            order.push_back(fronts[i]);
+            running.push({now + cost[i], i});
+        }
+        if (running.empty()) break;  // unreachable: the dependencies form a forest
+        const Run r = running.top();
+        running.pop();
+        now = r.first;
+        const int i = r.second;
+        if (fwd) {
+            if (par[i] >= 0 && --deps[par[i]] == 0) ready.push({path[par[i]], par[i]});
+        } else {
+            for (int c : kids[i])
+                if (--deps[c] == 0) ready.push({path[c], c});
+        }
+    }
+    return order;
+}
 
 extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, const int64_t *Rptr,
                                     const int64_t *Sptr, const int64_t *Stgt, const int64_t *Bptr, const int64_t *Fptr,
@@ -475,21 +541,24 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 sl.count = (int)(sroots.size() - sl.off);
                 subs.push_back(sl);
                 SLevel bc;
+                std::vector<int> up;  // the stage's other bottom fronts, children first
+                for (int hh = 0; hh <= maxh; hh++) up.insert(up.end(), bot[hh].begin(), bot[hh].end());
+                std::vector<int> down(up.rbegin(), up.rend());
+                // fronts in flight: the launch's warps (8 per SM) over the tiles of a front (8 for 256 columns)
+                const int fslots = h->sm_count;
                 std::pair<int64_t, int> fw{(int64_t)sfronts.size(), 0};
-                for (int hh = 0; hh <= maxh; hh++)
-                    for (int f : bot[hh]) {
-                        sfronts.push_back(f);
-                        const double nn = hp.nn[f], na = hp.na[f];
-                        bc.count++;
-                        bc.res_rows += nn;
-                        bc.sep_rows += na;
-                        bc.blk_elems += nn * nn + nn * na;
-                        bc.pairs_col += nn * (nn - 1) / 2 + nn * na;
-                    }
+                for (int f : sweep_order(up, hp.nn, hp.na, pnt, true, fslots)) {
+                    sfronts.push_back(f);
+                    const double nn = hp.nn[f], na = hp.na[f];
+                    bc.count++;
+                    bc.res_rows += nn;
+                    bc.sep_rows += na;
+                    bc.blk_elems += nn * nn + nn * na;
+                    bc.pairs_col += nn * (nn - 1) / 2 + nn * na;
+                }
                 fw.second = (int)(sfronts.size() - fw.first);
                 std::pair<int64_t, int> bw{(int64_t)sfronts.size(), 0};
-                for (int hh = maxh; hh >= 0; hh--)
-                    for (int f : bot[hh]) sfronts.push_back(f);
+                for (int f : sweep_order(down, hp.nn, hp.na, pnt, false, fslots)) sfronts.push_back(f);
                 bw.second = (int)(sfronts.size() - bw.first);
                 bfwd.push_back(fw);
                 bbwd.push_back(bw);

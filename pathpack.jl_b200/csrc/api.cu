@@ -235,14 +235,14 @@ extern "C" void *pp_stream(pp_handle *h) { return h ? (void *)h->stream : nullpt
 
 // ---------------------------------------------------------------- structure
 
-// Order of the fronts of one persistent bottom-sweep launch.  The launch hands its (front, 32-column tile)
-// tasks to warps in list order and a warp whose task is not ready waits, so the list follows a schedule
-// simulated on the host: `slots` fronts at a time (the launch's warps over the tiles of a front), a front
-// costing about 4 + nn * na / 36 (microseconds, fitted to measured task times), ready once its dependencies
-// are done (the backward sweep: its parent; the forward sweep: its children in the list), the ready front with
-// the longest path of remaining work first.  Every front comes after the fronts it depends on.
-static std::vector<int> sweep_order(const std::vector<int> &fronts, const std::vector<int> &nn,
-                                    const std::vector<int> &na, const std::vector<int> &pnt, bool fwd, int slots) {
+// Order of the fronts of one persistent launch (a bottom sweep, or the factorization of the bottom).  The
+// launch hands its tasks to warps or CTAs in list order and one whose task is not ready waits, so the list
+// follows a schedule simulated on the host: `slots` fronts at a time, front f costing fcost[f] (estimated
+// microseconds), ready once its dependencies are done (up: its children in the list, as in a forward sweep or
+// the factorization; down: its parent, as in a backward sweep), the ready front with the longest path of
+// remaining work first.  Every front comes after the fronts it depends on.
+static std::vector<int> schedule_order(const std::vector<int> &fronts, const std::vector<double> &fcost,
+                                       const std::vector<int> &pnt, bool up, int slots) {
     const int m = (int)fronts.size();
     std::vector<int> pos(pnt.size(), -1);
     for (int i = 0; i < m; i++) pos[fronts[i]] = i;
@@ -250,7 +250,7 @@ static std::vector<int> sweep_order(const std::vector<int> &fronts, const std::v
     std::vector<int> deps(m, 0), par(m, -1);
     for (int i = 0; i < m; i++) {
         const int f = fronts[i];
-        cost[i] = 4.0 + nn[f] * (double)na[f] / 36.0;
+        cost[i] = fcost[f];
         par[i] = pnt[f] >= 0 ? pos[pnt[f]] : -1;
     }
     // the fronts arrive in height order (ascending for the forward list, descending for the backward one), so
@@ -258,7 +258,7 @@ static std::vector<int> sweep_order(const std::vector<int> &fronts, const std::v
     std::vector<std::vector<int>> kids(m);
     for (int i = 0; i < m; i++)
         if (par[i] >= 0) kids[par[i]].push_back(i);
-    if (fwd) {
+    if (up) {
         for (int i = m - 1; i >= 0; i--) path[i] = cost[i] + (par[i] >= 0 ? path[par[i]] : 0.0);
         for (int i = 0; i < m; i++) deps[i] = (int)kids[i].size();
     } else {
@@ -290,7 +290,7 @@ static std::vector<int> sweep_order(const std::vector<int> &fronts, const std::v
         running.pop();
         now = r.first;
         const int i = r.second;
-        if (fwd) {
+        if (up) {
             if (par[i] >= 0 && --deps[par[i]] == 0) ready.push({path[par[i]], par[i]});
         } else {
             for (int c : kids[i])
@@ -506,6 +506,12 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
             }
             if (!sbot[f] && pnt[f] >= 0) tpending0[pnt[f]]++;  // top children (the top sweep's counters)
         }
+        // estimated time of a (front, 32-column tile) task of the bottom sweeps, fitted to measured task times
+        std::vector<double> scost(nf);
+        for (int64_t f = 0; f < nf; f++) scost[f] = 4.0 + hp.nn[f] * (double)hp.na[f] / 36.0;
+        std::vector<double> subtree_cost(nf, 0.0);  // of a subtree root: its fronts' estimated task times
+        for (int64_t f = 0; f < nf; f++)
+            if (covered[f]) subtree_cost[sroot_of[f]] += scost[f];
         auto build_stages = [&](const std::vector<int> &stage_of, std::vector<Stage> &out, std::vector<int> &sfronts,
                                 std::vector<int> &sverts, std::vector<std::pair<int64_t, int>> &bfwd,
                                 std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost,
@@ -539,6 +545,9 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                         (sbot[f] ? bot : byh)[height[f]].push_back((int)f);
                     }
                 sl.count = (int)(sroots.size() - sl.off);
+                // the launch runs its subtrees in list order: the longest first
+                std::stable_sort(sroots.begin() + sl.off, sroots.end(),
+                                 [&](int a, int b) { return subtree_cost[a] > subtree_cost[b]; });
                 subs.push_back(sl);
                 SLevel bc;
                 std::vector<int> up;  // the stage's other bottom fronts, children first
@@ -547,7 +556,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 // fronts in flight: the launch's warps (8 per SM) over the tiles of a front (8 for 256 columns)
                 const int fslots = h->sm_count;
                 std::pair<int64_t, int> fw{(int64_t)sfronts.size(), 0};
-                for (int f : sweep_order(up, hp.nn, hp.na, pnt, true, fslots)) {
+                for (int f : schedule_order(up, scost, pnt, true, fslots)) {
                     sfronts.push_back(f);
                     const double nn = hp.nn[f], na = hp.na[f];
                     bc.count++;
@@ -558,7 +567,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 }
                 fw.second = (int)(sfronts.size() - fw.first);
                 std::pair<int64_t, int> bw{(int64_t)sfronts.size(), 0};
-                for (int f : sweep_order(down, hp.nn, hp.na, pnt, false, fslots)) sfronts.push_back(f);
+                for (int f : schedule_order(down, scost, pnt, false, fslots)) sfronts.push_back(f);
                 bw.second = (int)(sfronts.size() - bw.first);
                 bfwd.push_back(fw);
                 bbwd.push_back(bw);
@@ -801,8 +810,15 @@ static int32_t prepare_workspace(pp_handle *h) {
                 hp.fb_maxnj = std::max(hp.fb_maxnj, hp.nn[f] + hp.na[f]);
                 front_cost(hp, f, acc);
             }
-        std::vector<int> wl;
-        for (int hh = 0; hh <= maxh; hh++) wl.insert(wl.end(), byh[hh].begin(), byh[hh].end());
+        std::vector<int> hl;
+        for (int hh = 0; hh <= maxh; hh++) hl.insert(hl.end(), byh[hh].begin(), byh[hh].end());
+        // estimated time of a bottom front (a CTA): a fixed part, the assembly and the partial LU
+        std::vector<double> fcost(nf, 0.0);
+        for (int f : hl) {
+            const double nj = hp.nn[f] + hp.na[f];
+            fcost[f] = 6.0 + nj * nj / 64.0 + hp.nn[f] * nj * nj / 512.0;
+        }
+        const std::vector<int> wl = schedule_order(hl, fcost, h->pnt, true, h->sm_count * 6);
         hp.fb_count = (int)wl.size();
         hp.fb_bytes = acc.bytes;
         hp.fb_pairs = acc.pairs;

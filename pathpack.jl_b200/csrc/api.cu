@@ -509,6 +509,9 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         // estimated time of a (front, 32-column tile) task of the bottom sweeps, fitted to measured task times
         std::vector<double> scost(nf);
         for (int64_t f = 0; f < nf; f++) scost[f] = 4.0 + hp.nn[f] * (double)hp.na[f] / 36.0;
+        // and of a (front, 32-column tile) task of the top sweeps: the diagonal solve, the off-diagonal block
+        std::vector<double> tscost(nf);
+        for (int64_t f = 0; f < nf; f++) tscost[f] = 5.0 + hp.nn[f] / 8.0 + hp.nn[f] * (double)hp.na[f] / 1024.0;
         std::vector<double> subtree_cost(nf, 0.0);  // of a subtree root: its fronts' estimated task times
         for (int64_t f = 0; f < nf; f++)
             if (covered[f]) subtree_cost[sroot_of[f]] += scost[f];
@@ -572,23 +575,26 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 bfwd.push_back(fw);
                 bbwd.push_back(bw);
                 bcost.push_back(bc);
-                // the top fronts: one work list per direction (height ascending / descending)
+                // the top fronts: one work list per direction, schedule-ordered like the bottom ones (a CTA per
+                // (front, tile) task, about two CTAs per SM over the eight tiles of a front)
                 SLevel tc;
+                std::vector<int> tup;
+                for (int hh = 0; hh <= maxh; hh++) tup.insert(tup.end(), byh[hh].begin(), byh[hh].end());
+                std::vector<int> tdown(tup.rbegin(), tup.rend());
+                const int tslots = std::max(1, h->sm_count / 4);
                 std::pair<int64_t, int> tf{(int64_t)sfronts.size(), 0};
-                for (int hh = 0; hh <= maxh; hh++)
-                    for (int f : byh[hh]) {
-                        sfronts.push_back(f);
-                        const double nn = hp.nn[f], na = hp.na[f];
-                        tc.count++;
-                        tc.res_rows += nn;
-                        tc.sep_rows += na;
-                        tc.blk_elems += nn * nn + nn * na;
-                        tc.pairs_col += nn * (nn - 1) / 2 + nn * na;
-                    }
+                for (int f : schedule_order(tup, tscost, pnt, true, tslots)) {
+                    sfronts.push_back(f);
+                    const double nn = hp.nn[f], na = hp.na[f];
+                    tc.count++;
+                    tc.res_rows += nn;
+                    tc.sep_rows += na;
+                    tc.blk_elems += nn * nn + nn * na;
+                    tc.pairs_col += nn * (nn - 1) / 2 + nn * na;
+                }
                 tf.second = (int)(sfronts.size() - tf.first);
                 std::pair<int64_t, int> tb{(int64_t)sfronts.size(), 0};
-                for (int hh = maxh; hh >= 0; hh--)
-                    for (int f : byh[hh]) sfronts.push_back(f);
+                for (int f : schedule_order(tdown, tscost, pnt, false, tslots)) sfronts.push_back(f);
                 tb.second = (int)(sfronts.size() - tb.first);
                 tfwd.push_back(tf);
                 tbwd.push_back(tb);
@@ -828,44 +834,52 @@ static int32_t prepare_workspace(pp_handle *h) {
         hp.d_fpending0 = h->d_fpending0.as<int>();
     }
     {
-        std::vector<std::vector<int>> byh(maxh + 1);
-        for (int f = 0; f < nf; f++)
-            if (!fbot[f]) byh[h->height[f]].push_back(f);
+        std::vector<int> tl;  // the top fronts, children first
+        {
+            std::vector<std::vector<int>> byh(maxh + 1);
+            for (int f = 0; f < nf; f++)
+                if (!fbot[f]) byh[h->height[f]].push_back(f);
+            for (int hh = 0; hh <= maxh; hh++) tl.insert(tl.end(), byh[hh].begin(), byh[hh].end());
+        }
+        // schedule order of the fronts (their tile tasks stay together): a front's critical path is about 50 us
+        // per 64-column pivot block; some sixteen tile tasks of a front are in flight on two CTAs per SM
+        std::vector<double> tcost(nf, 0.0);
+        for (int f : tl) tcost[f] = 20.0 + 50.0 * ((hp.nn[f] + TOP_TILE - 1) / TOP_TILE);
+        tl = schedule_order(tl, tcost, h->pnt, true, std::max(1, h->sm_count * 2 / 16));
         std::vector<int> tasks, crng;
         std::vector<int64_t> foff(nf, 0), croff(std::max<size_t>(hp.chdtgt.size(), 1), 0);
         int64_t nflags = 16;
         Cost acc;
         std::vector<std::pair<int, int>> tiles;
         std::vector<int> bounds;
-        for (int hh = 0; hh <= maxh; hh++)
-            for (int f : byh[hh]) {
-                const int nn = hp.nn[f], na = hp.na[f];
-                const int kb = (nn + TOP_TILE - 1) / TOP_TILE, nbt = kb + (na + TOP_TILE - 1) / TOP_TILE;
-                foff[f] = nflags;
-                nflags += (int64_t)nbt * nbt + 1;
-                // tile block boundaries of the front, and where each child's separator crosses them
-                bounds.clear();
-                for (int b = 0; b < kb; b++) bounds.push_back(b * TOP_TILE);
-                for (int b = kb; b < nbt; b++) bounds.push_back(nn + (b - kb) * TOP_TILE);
-                bounds.push_back(nn + na);
-                for (int c = hp.chdptr[f]; c < hp.chdptr[f + 1]; c++) {
-                    const int ch = hp.chdtgt[c];
-                    const int *r0 = h->rel.data() + hp.sptr[ch], *r1 = r0 + hp.na[ch];
-                    croff[c] = (int64_t)crng.size();
-                    for (int b : bounds) crng.push_back((int)(std::lower_bound(r0, r1, b) - r0));
-                }
-                tiles.clear();
-                for (int I = 0; I < nbt; I++)
-                    for (int J = 0; J < nbt; J++) tiles.push_back({I, J});
-                std::stable_sort(tiles.begin(), tiles.end(), [](const std::pair<int, int> &a,
-                                                                 const std::pair<int, int> &b) {
-                    const int a0 = std::min(a.first, a.second), b0 = std::min(b.first, b.second);
-                    if (a0 != b0) return a0 < b0;
-                    return std::max(a.first, a.second) < std::max(b.first, b.second);
-                });
-                for (const auto &t : tiles) tasks.insert(tasks.end(), {f, t.first, t.second, 0});
-                front_cost(hp, f, acc);
+        for (int f : tl) {
+            const int nn = hp.nn[f], na = hp.na[f];
+            const int kb = (nn + TOP_TILE - 1) / TOP_TILE, nbt = kb + (na + TOP_TILE - 1) / TOP_TILE;
+            foff[f] = nflags;
+            nflags += (int64_t)nbt * nbt + 1;
+            // tile block boundaries of the front, and where each child's separator crosses them
+            bounds.clear();
+            for (int b = 0; b < kb; b++) bounds.push_back(b * TOP_TILE);
+            for (int b = kb; b < nbt; b++) bounds.push_back(nn + (b - kb) * TOP_TILE);
+            bounds.push_back(nn + na);
+            for (int c = hp.chdptr[f]; c < hp.chdptr[f + 1]; c++) {
+                const int ch = hp.chdtgt[c];
+                const int *r0 = h->rel.data() + hp.sptr[ch], *r1 = r0 + hp.na[ch];
+                croff[c] = (int64_t)crng.size();
+                for (int b : bounds) crng.push_back((int)(std::lower_bound(r0, r1, b) - r0));
             }
+            tiles.clear();
+            for (int I = 0; I < nbt; I++)
+                for (int J = 0; J < nbt; J++) tiles.push_back({I, J});
+            std::stable_sort(tiles.begin(), tiles.end(), [](const std::pair<int, int> &a,
+                                                             const std::pair<int, int> &b) {
+                const int a0 = std::min(a.first, a.second), b0 = std::min(b.first, b.second);
+                if (a0 != b0) return a0 < b0;
+                return std::max(a.first, a.second) < std::max(b.first, b.second);
+            });
+            for (const auto &t : tiles) tasks.insert(tasks.end(), {f, t.first, t.second, 0});
+            front_cost(hp, f, acc);
+        }
         hp.top_ntasks = (int)(tasks.size() / 4);
         hp.top_cost = acc;
         hp.tflags_n = nflags;

@@ -58,24 +58,82 @@ __device__ __forceinline__ int cta_take(int *next) {
 
 // ---------------------------------------------------------------- factorization of the bottom fronts
 
+// thread 0 polls the front's counter of unfinished children until it is 0, then claims the front (0 -> -1);
+// -1 means another CTA claimed it.  Returns 1 (claimed here), 0 (claimed elsewhere) or -1 (a bounded wait
+// expired, or another CTA reported an error).
+__device__ __forceinline__ int cta_claim(int *p, int *err) {
+    __shared__ int s_r;
+    if (threadIdx.x == 0) {
+        long long it = 0;
+        int r;
+        while (true) {
+            const int v = *(volatile const int *)p;
+            if (v == -1) {
+                r = 0;
+                break;
+            }
+            if (v == 0) {
+                r = atomicCAS(p, 0, -1) == 0 ? 1 : 0;
+                break;
+            }
+            if (*(volatile const int *)err) {
+                r = -1;
+                break;
+            }
+            if (++it > WAIT_LIMIT) {
+                atomicExch(err, 1);
+                r = -1;
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
+        s_r = r;
+    }
+    __syncthreads();
+    const int r = s_r;
+    __syncthreads();  // s_r is reused by the next claim
+    return r;
+}
+
+// The bottom fronts in work-list order, a CTA each.  The CTA that finishes the last child of a bottom front
+// claims that parent and factors it at once (no queue, no wait); a CTA that takes a front from the list waits
+// for its children and factors it unless such a CTA claimed it first.  Every front is claimed exactly once
+// (the counter goes 0 -> -1 by compare-and-swap).
 template <int SR, typename T>
 __global__ void __launch_bounds__(128) factor_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P, T *LD,
                                                             T *LL, T *UD, T *UL, T *W, int *pending, int *next,
                                                             int *err) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *F = reinterpret_cast<T *>(smem_raw);
+    __shared__ int s_next;
+    int f = -1;
     while (true) {
-        const int t = cta_take(next);
-        if (t >= count) return;
-        const int f = wl[t];
-        if (!cta_wait(pending + f, true, err)) return;
+        if (f < 0) {
+            const int t = cta_take(next);
+            if (t >= count) return;
+            const int g = wl[t];
+            const int r = cta_claim(pending + g, err);
+            if (r < 0) return;
+            if (r == 0) continue;
+            f = g;
+        }
         front_body<SR, T, true>(f, P, F, LD, LL, UD, UL, W);
         __syncthreads();
         if (threadIdx.x == 0) {
             __threadfence();
             const int p = P.pnt[f];
-            if (p >= 0) atomicSub(pending + p, 1);
+            int nx = -1;
+            // a bottom parent (fws < 0) whose last child this was: claim it
+            if (p >= 0 && atomicSub(pending + p, 1) == 1 && P.fws[p] < 0 && atomicCAS(pending + p, 0, -1) == 0) {
+                __threadfence();
+                nx = p;
+            }
+            s_next = nx;
         }
+        __syncthreads();
+        f = s_next;
+        __syncthreads();  // s_next is rewritten after the next front
     }
 }
 

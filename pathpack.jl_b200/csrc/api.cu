@@ -451,10 +451,11 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                     const int a = comp_of_vertex[ntgt[p]];
                     lstage[a] = std::max(lstage[a], lstage[c] + 1);
                 }
-        // bottom of the tree for the persistent sweeps: nn <= SWEEP_NNW in the whole subtree
+        // bottom of the tree for the persistent sweeps: nn <= SWEEP_NNW and nn + na <= SWEEP_NJW in the whole
+        // subtree
         std::vector<char> sbot(nf, 0), allbot(nf, 1);
         for (int64_t f = 0; f < nf; f++) {
-            sbot[f] = (hp.nn[f] <= SWEEP_NNW) && allbot[f];
+            sbot[f] = (hp.nn[f] <= SWEEP_NNW) && (hp.nn[f] + hp.na[f] <= SWEEP_NJW) && allbot[f];
             if (!sbot[f] && pnt[f] >= 0) allbot[pnt[f]] = 0;
         }
         // subtrees solved in shared memory: the whole subtree is in the bottom and its residual range plus the

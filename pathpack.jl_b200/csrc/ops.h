@@ -109,7 +109,7 @@ struct HostPlan {
     DevPlan dev{};
     Profiler *prof = nullptr;
     // bottom of the tree for the persistent kernels: factorization (fronts with nn + na <= the bottom limit
-    // whose whole subtree is such) and solves (nn <= SWEEP_NNW, whole subtree)
+    // whose whole subtree is such) and solves (nn <= SWEEP_NNW, nn + na <= SWEEP_NJW, whole subtree)
     int fb_count = 0, fb_maxnj = 0;
     double fb_bytes = 0, fb_pairs = 0;
     const int *d_fbottom = nullptr;    // work list, height ascending

@@ -10,6 +10,10 @@ namespace pp {
 
 // largest residual of a front in the register-resident warp sweep of the bottom of the tree
 constexpr int SWEEP_NNW = 16;
+// and its largest nn + na: the fronts of the bottom of the tree's factorization for every element type (whose
+// frontal matrix fits 32 KB of shared memory: 64 x 64 Float64), so that a solve sweeps all of the bottom of
+// the tree while the top is still being factored
+constexpr int SWEEP_NJW = 64;
 // rows (residual range + root separator) of a subtree solved in shared memory by one warp
 constexpr int SUBTREE_ROWS = 64;
 // tile edge of the persistent factorization of the top of the tree

@@ -104,7 +104,7 @@ struct pp_handle {
     // device structure
     DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
         d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_sfronts, d_sverts, d_pnt, d_fbottom,
-        d_fpending0, d_spending0, d_sdone0, d_tpending0, d_sync, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags, d_croff,
+        d_fpending0, d_spending0, d_sdone0, d_tpending0, d_sync, d_tentries, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags, d_croff,
         d_crng, d_err;
     std::vector<int> pnt, height, rel;
     std::vector<int> sfronts, sroots;  // host copies of the solve work lists (reordered by prepare_workspace)
@@ -521,7 +521,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                                 std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost,
                                 std::vector<SubtreeList> &subs, std::vector<int> &sroots,
                                 std::vector<std::pair<int64_t, int>> &tfwd, std::vector<std::pair<int64_t, int>> &tbwd,
-                                std::vector<SLevel> &tcost) {
+                                std::vector<SLevel> &tcost, std::vector<int> &tentries) {
             int ns = 0;
             for (int64_t c = 0; c < nB; c++) ns = std::max(ns, stage_of[c] + 1);
             if (nB == 0) ns = 0;
@@ -577,15 +577,18 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 bbwd.push_back(bw);
                 bcost.push_back(bc);
                 // the top fronts: one work list per direction, schedule-ordered like the bottom ones (a CTA per
-                // (front, tile) task, about two CTAs per SM over the eight tiles of a front)
+                // (front, tile) task, about two CTAs per SM over the eight tiles of a front); entries (front,
+                // block of 64 rows): forward the residual blocks ascending, then the separator blocks, backward the
+                // residual blocks descending
                 SLevel tc;
                 std::vector<int> tup;
                 for (int hh = 0; hh <= maxh; hh++) tup.insert(tup.end(), byh[hh].begin(), byh[hh].end());
                 std::vector<int> tdown(tup.rbegin(), tup.rend());
                 const int tslots = std::max(1, h->sm_count / 4);
-                std::pair<int64_t, int> tf{(int64_t)sfronts.size(), 0};
+                auto blocks = [](int m) { return (m + TOP_SWEEP_ROWS - 1) / TOP_SWEEP_ROWS; };
+                std::pair<int64_t, int> tf{(int64_t)tentries.size() / 2, 0};
                 for (int f : schedule_order(tup, tscost, pnt, true, tslots)) {
-                    sfronts.push_back(f);
+                    for (int b = 0; b < blocks(hp.nn[f]) + blocks(hp.na[f]); b++) tentries.insert(tentries.end(), {f, b});
                     const double nn = hp.nn[f], na = hp.na[f];
                     tc.count++;
                     tc.res_rows += nn;
@@ -593,10 +596,11 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                     tc.blk_elems += nn * nn + nn * na;
                     tc.pairs_col += nn * (nn - 1) / 2 + nn * na;
                 }
-                tf.second = (int)(sfronts.size() - tf.first);
-                std::pair<int64_t, int> tb{(int64_t)sfronts.size(), 0};
-                for (int f : schedule_order(tdown, tscost, pnt, false, tslots)) sfronts.push_back(f);
-                tb.second = (int)(sfronts.size() - tb.first);
+                tf.second = (int)(tentries.size() / 2 - tf.first);
+                std::pair<int64_t, int> tb{(int64_t)tentries.size() / 2, 0};
+                for (int f : schedule_order(tdown, tscost, pnt, false, tslots))
+                    for (int b = blocks(hp.nn[f]) - 1; b >= 0; b--) tentries.insert(tentries.end(), {f, b});
+                tb.second = (int)(tentries.size() / 2 - tb.first);
                 tfwd.push_back(tf);
                 tbwd.push_back(tb);
                 tcost.push_back(tc);
@@ -609,12 +613,12 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 out.push_back(std::move(sg));
             }
         };
-        std::vector<int> sfronts, sverts, sroots;
+        std::vector<int> sfronts, sverts, sroots, tentries;
         build_stages(lstage, hp.lstages, sfronts, sverts, hp.sb_fwd, hp.sb_bwd, hp.sb_cost_l, hp.sub_l, sroots,
-                     hp.st_fwd, hp.st_bwd, hp.st_cost_l);
+                     hp.st_fwd, hp.st_bwd, hp.st_cost_l, tentries);
         // rmul stages: the gather concerns the stage's own columns j (rows of earlier components feed them)
         build_stages(rstage, hp.rstages, sfronts, sverts, hp.sb_fwd_r, hp.sb_bwd_r, hp.sb_cost_r, hp.sub_r, sroots,
-                     hp.st_fwd_r, hp.st_bwd_r, hp.st_cost_r);
+                     hp.st_fwd_r, hp.st_bwd_r, hp.st_cost_r, tentries);
         (void)ccoupled;
         std::vector<int64_t> Np64(Np.begin(), Np.end());
         // device uploads
@@ -637,6 +641,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         CK(h, upload(h->d_bptr, bptr, st), "upload");
         CK(h, upload(h->d_fcc, fcc, st), "upload");
         CK(h, upload(h->d_sfronts, sfronts, st), "upload");
+        CK(h, upload(h->d_tentries, tentries, st), "upload");
         CK(h, upload(h->d_sverts, sverts, st), "upload");
         CK(h, upload(h->d_pnt, pnt, st), "upload");
         CK(h, upload(h->d_sroots, sroots, st), "upload");
@@ -645,7 +650,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         CK(h, upload(h->d_spending0, spending0, st), "upload");
         CK(h, upload(h->d_sdone0, sdone0, st), "upload");
         CK(h, upload(h->d_tpending0, tpending0, st), "upload");
-        CK(h, h->d_sync.ensure(sizeof(int) * (32 * nf + 16)), "upload");
+        CK(h, h->d_sync.ensure(sizeof(int) * sync_ints(nf, 256)), "upload");
         CK(h, h->d_err.ensure(sizeof(int) * 4), "upload");
         CK(h, cudaMemsetAsync(h->d_err.p, 0, sizeof(int) * 4, st), "upload");
         CK(h, cudaStreamSynchronize(st), "upload");
@@ -675,6 +680,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         d.mld = nullptr;
         d.fws = nullptr;
         hp.d_sfronts = h->d_sfronts.as<int>();
+        hp.d_tentries = reinterpret_cast<const int2 *>(h->d_tentries.p);
         hp.d_sverts = h->d_sverts.as<int>();
         hp.d_rel = h->d_rel.as<int>();
         hp.d_spending0 = h->d_spending0.as<int>();
@@ -685,7 +691,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         hp.d_tpending0 = h->d_tpending0.as<int>();
         hp.d_sync = h->d_sync.as<int>();
         hp.d_err = h->d_err.as<int>();
-        hp.sync_cap = 32 * nf + 16;
+        hp.sync_cap = sync_ints(nf, 256);
         hp.sm_count = h->sm_count;
         hp.ev_bottom = h->ev_bottom;
         hp.ev_factored = h->ev_factored;
@@ -1147,7 +1153,7 @@ static double solve_pairs_per_rhs(const HostPlan &hp) {
 
 // the per-(tile, front) counters of the persistent sweeps for k right-hand sides
 static int32_t ensure_sync(pp_handle *h, int64_t k) {
-    const int64_t need = ((k + 31) / 32) * (int64_t)h->hp.nf + 16;
+    const int64_t need = sync_ints(h->hp.nf, k);
     if (need <= h->hp.sync_cap) return PP_OK;
     if (need_memory(h, sizeof(int) * need, "sweep counters") != PP_OK) return PP_ENOMEM;
     h->d_sync.release();
@@ -1306,7 +1312,7 @@ size_t pp_internal_lmul_scratch_bytes(const pp_handle *h, int64_t k) {
     if (!h || !h->ops || k <= 0) return 0;
     const int64_t ldx = (k + 3) & ~(int64_t)3;
     const size_t xbytes = ((h->ops->esize * (size_t)h->hp.n * ldx) + 255) & ~(size_t)255;
-    const int64_t counters = ((k + 31) / 32) * (int64_t)h->hp.nf + 16;
+    const int64_t counters = sync_ints(h->hp.nf, k);
     return xbytes + sizeof(int) * (size_t)counters;
 }
 

@@ -139,18 +139,20 @@ struct Engine {
             attr[dev] = true;
         }
         const int ntiles = (k + SW_CT - 1) / SW_CT;
+        const size_t cells = (size_t)ntiles * hp.nf;  // per (tile, front)
         if (FWD) {
             PP_TRY(reset_sync(hp, hp.d_tpending0, ntiles, st));
+            PP_TRY(cudaMemsetAsync(hp.d_sync + 16 + cells, 0, sizeof(int) * 2 * cells, st));  // blocks done
         } else {
             PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int), st));
-            PP_TRY(cudaMemsetAsync(hp.d_sync + 16, 0, sizeof(int) * (size_t)ntiles * hp.nf, st));
+            PP_TRY(cudaMemsetAsync(hp.d_sync + 16, 0, sizeof(int) * 2 * cells, st));  // done flags, blocks done
         }
         int per_sm = 1;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_top_kernel<SR, T, FWD, TRANS>, 256, smem);
         const int64_t tasks = (int64_t)wl.second * ntiles;
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tasks, std::max(per_sm, 1) * hp.sm_count));
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD : K_SWEEP_BWD, st) : -1;
-        sweep_top_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev, Dv,
+        sweep_top_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_tentries + wl.first, wl.second, hp.dev, Dv,
                                                                      Ov, X, ldx, k, unit, hp.d_sync + 16, hp.d_sync,
                                                                      hp.d_err);
         PP_TRY(cudaGetLastError());

@@ -104,6 +104,7 @@ struct HostPlan {
     // solve schedules (lmul: components after their coupling successors; rmul: after their predecessors)
     std::vector<Stage> lstages, rstages;
     const int *d_sfronts = nullptr;   // fronts of every stage's levels (both schedules)
+    const int2 *d_tentries = nullptr;  // (front, block) entries of the top sweeps' work lists
     const int *d_sverts = nullptr;    // vertices of every stage (both schedules)
     const int *d_rel = nullptr;
     DevPlan dev{};

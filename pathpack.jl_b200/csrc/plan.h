@@ -18,6 +18,12 @@ constexpr int SWEEP_NJW = 64;
 constexpr int SUBTREE_ROWS = 64;
 // tile edge of the persistent factorization of the top of the tree
 constexpr int TOP_TILE = 64;
+// rows of a block task of the top sweeps
+constexpr int TOP_SWEEP_ROWS = 64;
+
+// ints of the sweeps' scratch for k right-hand sides (tiles of 32 columns): the task counter (16 ints), then per
+// (tile, front) a counter or flag, the top sweep's residual blocks done and its separator blocks done
+inline int64_t sync_ints(int64_t nf, int64_t k) { return 3 * ((k + 31) / 32) * nf + 16; }
 
 // Device arrays of a structure (0-based, positions = permuted labels).  Per front f: the residual is
 // rlo[f] .. rlo[f]+nn[f]-1, the separator stgt[sptr[f] .. sptr[f+1]-1] with rel[] its positions in the

@@ -1,11 +1,14 @@
 // sweep_top.cuh — the triangular solves of the fronts above the bottom of the tree: ONE persistent launch per
 // sweep direction and coupling stage.
 //
-// Tasks are (front, 32 right-hand sides), fronts in height order (children first for the forward sweep,
-// parents first for the backward one), so every task waits only for tasks taken earlier: forward for a counter
-// of its top children (each finished child decrements it), backward for its parent's flag.  A task solves the
-// front's residual rows in blocks of 64 and then, forward, (+)-scatters L21 x to the separator rows with
-// atomics; backward it starts each block with the gather from the separator rows.  The off-diagonal products
+// Tasks are (front, block of 64 rows, 32 right-hand sides), the fronts schedule-ordered (children first for the
+// forward sweep, parents first for the backward one) and a front's blocks in solve order, so every task waits
+// only for tasks taken earlier: forward for a counter of its top children (the last separator task of a child
+// decrements it) and for the residual blocks before it, backward for its parent's flag and for the residual
+// blocks after it.  A residual-block task solves its 64 rows, applying the blocks it depends on one at a time
+// as they are published (so a large front's blocks proceed on several SMs at once); forward, separator-block
+// tasks then (+)-scatter their 64 rows of L21 x with atomics; backward, each block starts with the gather from
+// the separator rows.  The off-diagonal products
 // are register-tiled (2 rows x 4 right-hand sides per thread) over operand chunks staged in shared memory,
 // double-buffered; the 64 x 64 diagonal block is solved warp by warp (a warp holds 4 right-hand sides, a lane
 // 8 rows of one of them) with the pivot values broadcast by shuffles, so the solve needs no CTA barrier.  Per
@@ -19,7 +22,7 @@
 
 namespace pp {
 
-constexpr int SW_RB = 64;   // residual rows per block
+constexpr int SW_RB = TOP_SWEEP_ROWS;   // rows per block task
 constexpr int SW_CT = 32;   // right-hand sides per task
 constexpr int SW_KC = 16;   // operand chunk
 constexpr int SW_AL = SW_KC + 1;  // padded row of the staged matrix chunk
@@ -32,8 +35,41 @@ constexpr size_t sweep_top_smem() {
                         (size_t)SW_RB * SW_XL);
 }
 
+// thread 0 polls until the low 16 bits of a front's block counter reach target (bounded); every thread gets
+// the counter's value, or -1 when the wait failed.  Bit 16 and up: the forward sweep found the front's
+// right-hand sides all zero.
+__device__ __forceinline__ int cta_wait_blocks(const int *p, int target, int *err) {
+    __shared__ int s_v;
+    if (threadIdx.x == 0) {
+        long long it = 0;
+        int v;
+        while (true) {
+            v = *(volatile const int *)p;
+            if ((v & 0xffff) >= target) break;
+            if (*(volatile const int *)err) {
+                v = -1;
+                break;
+            }
+            if (++it > WAIT_LIMIT) {
+                atomicExch(err, 1);
+                v = -1;
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
+        s_v = v;
+    }
+    __syncthreads();
+    const int v = s_v;
+    __syncthreads();  // s_v is reused by the next wait
+    return v;
+}
+
+// flags: [tile * nf + f] the forward counters of top children / backward done flags, then per (tile, front) the
+// residual blocks done and (forward) the separator tasks done.  wl[i] = (front, block).
 template <int SR, typename T, bool FWD, bool TRANS>
-__global__ void __launch_bounds__(256) sweep_top_kernel(const int *__restrict__ wl, int count, DevPlan P,
+__global__ void __launch_bounds__(256) sweep_top_kernel(const int2 *__restrict__ wl, int count, DevPlan P,
                                                         const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
                                                         int64_t ldx, int k, int unit, int *flags, int *next,
                                                         int *err) {
@@ -49,13 +85,16 @@ __global__ void __launch_bounds__(256) sweep_top_kernel(const int *__restrict__ 
     const int64_t ntask = (int64_t)count * ntiles;
     const T z = S::zero();
     const bool scale = !unit && !S::integral;
+    int *const bdone = flags + (int64_t)ntiles * nf, *const sdone = bdone + (int64_t)ntiles * nf;
 
     while (true) {
         const int t = cta_take(next);
         if (t >= ntask) return;
         const int idx = t / ntiles, tile = t - idx * ntiles;
-        const int f = wl[idx];
+        const int2 task = wl[idx];
+        const int f = task.x, b = task.y;
         int *fl = flags + (int64_t)tile * nf;
+        int *bd = bdone + (int64_t)tile * nf + f;
         const int p = P.pnt[f];
         if (FWD) {
             if (!cta_wait(fl + f, true, err)) return;
@@ -201,27 +240,47 @@ __global__ void __launch_bounds__(256) sweep_top_kernel(const int *__restrict__ 
             __syncthreads();
         };
 
-        bool live = true;
-        if (FWD && zero_absorbs<SR>) {
-            // the 32 right-hand sides are zero on the whole residual: the task changes nothing
-            bool nz = false;
-            for (int e = tid; e < nn * SW_CT; e += 256) {
-                const int c = c0 + e % SW_CT;
-                if (c < k) nz |= !(ld_cg(X + (int64_t)(rlo + e / SW_CT) * ldx + c) == z);
+        const int kb = (nn + SW_RB - 1) / SW_RB, sbk = (na + SW_RB - 1) / SW_RB;
+        if (FWD && b < kb) {
+            // residual block b: its rows (+)= the solved blocks before it, then the diagonal solve
+            const int r0 = b * SW_RB, nv = min(SW_RB, nn - r0);
+            bool live = true;
+            if (b == 0) {
+                if (zero_absorbs<SR>) {
+                    // the 32 right-hand sides are zero on the whole residual: the front changes nothing
+                    bool nz = false;
+                    for (int e = tid; e < nn * SW_CT; e += 256) {
+                        const int c = c0 + e % SW_CT;
+                        if (c < k) nz |= !(ld_cg(X + (int64_t)(rlo + e / SW_CT) * ldx + c) == z);
+                    }
+                    live = __syncthreads_or(nz) != 0;
+                }
+            } else {
+                const int v = cta_wait_blocks(bd, 1, err);
+                if (v < 0) return;
+                live = (v >> 16) == 0;
             }
-            live = __syncthreads_or(nz) != 0;
-        }
-        if (FWD && live) {
-            for (int r0 = 0; r0 < nn; r0 += SW_RB) {
-                const int nv = min(SW_RB, nn - r0);
+            if (live) {
                 load_acc(rlo + r0, nv, true);
-                accum(r0, nv, 0, r0, false, Te, xres);
+                for (int j = 0; j < b; j++) {
+                    if (j > 0 && cta_wait_blocks(bd, j + 1, err) < 0) return;
+                    accum(r0, nv, j * SW_RB, (j + 1) * SW_RB, false, Te, xres);
+                }
                 diag_solve(r0, nv);
             }
-            // separator: X[sep_i] (+)= (L21 x)_i
-            auto Of = [&](int i, int q) -> T { return TRANS ? O[q + (int64_t)i * nn] : O[i + (int64_t)q * na]; };
-            for (int i0 = 0; i0 < na; i0 += SW_RB) {
-                const int nv = min(SW_RB, na - i0);
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();
+                atomicAdd(bd, (b == 0 && !live) ? 0x10001 : 1);
+                if (b == kb - 1 && sbk == 0 && p >= 0) atomicSub(fl + p, 1);
+            }
+        } else if (FWD) {
+            // separator block b - kb: X[sep_i] (+)= (L21 x)_i for its 64 rows, once every residual block is solved
+            const int v = cta_wait_blocks(bd, kb, err);
+            if (v < 0) return;
+            if ((v >> 16) == 0) {
+                auto Of = [&](int i, int q) -> T { return TRANS ? O[q + (int64_t)i * nn] : O[i + (int64_t)q * na]; };
+                const int i0 = (b - kb) * SW_RB, nv = min(SW_RB, na - i0);
                 load_acc(0, 0, false);
                 accum(i0, nv, 0, nn, false, Of, xres);
 #pragma unroll
@@ -232,23 +291,28 @@ __global__ void __launch_bounds__(256) sweep_top_kernel(const int *__restrict__ 
                         if (r < nv && c < k) S::atomic_add(X + (int64_t)sep[i0 + r] * ldx + c, acc[i][j]);
                     }
             }
-        } else if (!FWD) {
-            auto Ob = [&](int r, int i) -> T { return TRANS ? O[i + (int64_t)r * na] : O[r + (int64_t)i * nn]; };
-            for (int r1 = nn; r1 > 0; r1 -= SW_RB) {
-                const int r0 = max(0, r1 - SW_RB), nv = r1 - r0;
-                load_acc(rlo + r0, nv, true);
-                accum(r0, nv, 0, na, false, Ob, xsep);
-                accum(r0, nv, r1, nn, true, Te, xres);
-                diag_solve(r0, nv);
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();
+                if (atomicAdd(sdone + (int64_t)tile * nf + f, 1) == sbk - 1 && p >= 0) atomicSub(fl + p, 1);
             }
-        }
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            if (FWD) {
-                if (p >= 0) atomicSub(fl + p, 1);
-            } else {
-                atomicExch(fl + f, 1);
+        } else {
+            // residual block b, backward: the gather from the separator, the solved blocks after it (descending),
+            // then the diagonal solve
+            auto Ob = [&](int r, int i) -> T { return TRANS ? O[i + (int64_t)r * na] : O[r + (int64_t)i * nn]; };
+            const int r0 = b * SW_RB, r1 = min(nn, r0 + SW_RB), nv = r1 - r0;
+            load_acc(rlo + r0, nv, true);
+            accum(r0, nv, 0, na, false, Ob, xsep);
+            for (int j = kb - 1; j > b; j--) {
+                if (cta_wait_blocks(bd, kb - j, err) < 0) return;
+                accum(r0, nv, j * SW_RB, min(nn, (j + 1) * SW_RB), true, Te, xres);
+            }
+            diag_solve(r0, nv);
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();
+                atomicAdd(bd, 1);
+                if (b == 0) atomicExch(fl + f, 1);
             }
         }
     }

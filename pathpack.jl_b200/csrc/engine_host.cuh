@@ -10,6 +10,7 @@
 
 #include <algorithm>
 
+#include "getrf.cuh"
 #include "ops.h"
 #include "persist.cuh"
 #include "sweep_top.cuh"
@@ -338,6 +339,23 @@ struct Engine {
     }
 
     static cudaError_t getrf_batched(int n, int64_t count, void *A, cudaStream_t st) {
+        if (n <= 128) {  // register-resident, one CTA per block
+            T *a = static_cast<T *>(A);
+            for (int64_t b0 = 0; b0 < count; b0 += (int64_t)1 << 30) {
+                const unsigned cnt = (unsigned)std::min<int64_t>(count - b0, (int64_t)1 << 30);
+                T *ab = a + b0 * n * n;
+                if (n <= 16)
+                    getrf_reg_kernel<SR, T, 1><<<cnt, 256, 0, st>>>(n, ab);
+                else if (n <= 32)
+                    getrf_reg_kernel<SR, T, 2><<<cnt, 256, 0, st>>>(n, ab);
+                else if (n <= 64)
+                    getrf_reg_kernel<SR, T, 4><<<cnt, 256, 0, st>>>(n, ab);
+                else
+                    getrf_reg_kernel<SR, T, 8><<<cnt, 256, 0, st>>>(n, ab);
+                PP_TRY(cudaGetLastError());
+            }
+            return cudaSuccess;
+        }
         const size_t smem = (size_t)n * n * sizeof(T);
         if (smem > SMALL_FRONT_SMEM) return cudaErrorInvalidValue;
         int dev = 0;

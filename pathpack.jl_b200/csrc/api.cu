@@ -101,6 +101,7 @@ struct pp_handle {
     HostPlan hp;
     // host copies used by the drivers
     std::vector<int> invp;
+    std::vector<int> star_host;  // pp_star's panel order: positions, then output columns
     // device structure
     DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
         d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_sfronts, d_sverts, d_pnt, d_fbottom,
@@ -110,7 +111,7 @@ struct pp_handle {
     std::vector<int> sfronts, sroots;  // host copies of the solve work lists (reordered by prepare_workspace)
     int maxh = 0;
     // values and work
-    DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val;
+    DevBuf LD, LL, UD, UL, Nval, W, X, stage_in, stage_out, csc_ptr, csc_row, csc_val, star_map;
     int64_t nD = 0, nL = 0;
     int64_t nnz_assembled = -1;
     size_t ws_esize = 0;
@@ -1334,9 +1335,13 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
     if (!C || ldc < n) return fail(h, PP_EINVAL, "pp_star: C / ldc");
     cudaSetDevice(h->device);
     const size_t es = h->ops->esize;
-    // panel width: about 256 MB of right-hand sides per panel, a multiple of 32 columns
-    int64_t pw = ((int64_t)1 << 28) / std::max<int64_t>((int64_t)es * n, 1);
-    pw = std::max<int64_t>(32, std::min<int64_t>(pw & ~(int64_t)31, 4096));
+    // panel width, a multiple of 32 columns: wide panels give the sweeps of the top fronts, whose 64-row blocks
+    // form dependency chains, many independent column tiles to run beside each chain (about 2 GB of right-hand
+    // sides per panel, at most 16,384 columns); host output uses panels of about 256 MB so that the copy of one
+    // panel to the host overlaps the computation of the next
+    const int64_t budget = where == PP_DEVICE ? ((int64_t)1 << 31) : ((int64_t)1 << 28);
+    int64_t pw = budget / std::max<int64_t>((int64_t)es * n, 1);
+    pw = std::max<int64_t>(32, std::min<int64_t>(pw & ~(int64_t)31, where == PP_DEVICE ? 16384 : 4096));
     pw = std::min<int64_t>(pw, (ncols + 31) & ~(int64_t)31);
     const int64_t ldx = pw;
     const size_t xbytes = es * (size_t)n * ldx;
@@ -1348,6 +1353,25 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
     if (ensure_sync(h, pw) != PP_OK) return PP_ENOMEM;
     cudaStream_t st = h->stream;
     int64_t nl = 0;
+    // device output: the requested columns are taken in elimination order (sorted positions) and each panel
+    // column is written to its own column of C, so the 32 sources of a tile lie in a few neighbouring subtrees
+    // and the forward sweep skips every front outside their root paths (its zero test is per tile)
+    const bool mapped = where == PP_DEVICE && ncols > 32;
+    const int *d_pos = nullptr, *d_cmap = nullptr;
+    if (mapped) {
+        std::vector<int> &hm = h->star_host;
+        hm.resize(2 * (size_t)ncols);
+        for (int64_t c = 0; c < ncols; c++) hm[ncols + c] = (int)(col0 + c);
+        std::sort(hm.begin() + ncols, hm.end(), [&](int a, int b) { return h->invp[a] < h->invp[b]; });
+        for (int64_t c = 0; c < ncols; c++) {
+            hm[c] = h->invp[hm[ncols + c]];
+            hm[ncols + c] -= (int)col0;
+        }
+        CK(h, h->star_map.ensure(sizeof(int) * hm.size()), who);
+        CK(h, cudaMemcpyAsync(h->star_map.p, hm.data(), sizeof(int) * hm.size(), cudaMemcpyHostToDevice, st), who);
+        d_pos = h->star_map.as<int>();
+        d_cmap = d_pos + ncols;
+    }
     CK(h, cudaEventRecord(h->ev0, st), who);
     // host output: panel i is written to staging buffer i % 2 and copied to C on the copy stream while panel
     // i + 1 is computed; panel i + 2 waits for that copy before it reuses the buffer
@@ -1356,14 +1380,20 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
         const int w = (int)std::min<int64_t>(pw, ncols - c0);
         const int buf = (int)(panel & 1);
         CK(h, h->ops->fill_zero(h->X.p, (int64_t)n * ldx, st), who);
-        CK(h, h->ops->unit_sources(h->X.p, ldx, h->hp.dev.invp, col0 + c0, w, st), who);
+        if (mapped)
+            CK(h, h->ops->unit_positions(h->X.p, ldx, d_pos + c0, w, st), who);
+        else
+            CK(h, h->ops->unit_sources(h->X.p, ldx, h->hp.dev.invp, col0 + c0, w, st), who);
         CK(h, h->ops->solve(h->hp, values_of(h), 1, h->X.p, ldx, w, st, &nl), who);
         void *stage = static_cast<char *>(h->stage_out.p) + (size_t)buf * es * (size_t)n * pw;
         void *dst = where == PP_HOST ? stage : (void *)(static_cast<char *>(C) + es * (size_t)c0 * ldc);
         const int64_t lddst = where == PP_HOST ? n : ldc;
         if (where == PP_HOST && panel >= 2) CK(h, cudaStreamWaitEvent(st, h->panel_copied[buf], 0), who);
         const int pi = h->prof.begin(K_PERMUTE, st);
-        CK(h, h->ops->rows_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
+        if (mapped)
+            CK(h, h->ops->rows_out_mapped(C, ldc, h->X.p, ldx, h->hp.dev.invp, d_cmap + c0, n, w, st), who);
+        else
+            CK(h, h->ops->rows_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
         h->prof.end(pi, st, 2.0 * n * w, 0);
         nl += 3;
         if (where == PP_HOST) {

@@ -207,10 +207,10 @@ __global__ void rows_in_kernel(const T *__restrict__ B, int64_t ldb, T *__restri
 }
 
 // B[i + c * ldb] = X[invp[i]][c] (lmul!: permuterows!(B, cperm) out of the internal layout; also the star's
-// column panels)
+// column panels); with a column map, column c of the panel goes to column cmap[c] of B
 template <typename T>
 __global__ void rows_out_kernel(T *__restrict__ B, int64_t ldb, const T *__restrict__ X, int64_t ldx,
-                                const int *__restrict__ invp, int n, int k) {
+                                const int *__restrict__ invp, int n, int k, const int *__restrict__ cmap) {
     __shared__ T t[32][33];
     const int i0 = blockIdx.x * 32, c0 = blockIdx.y * 32, tx = threadIdx.x, ty = threadIdx.y;
     for (int ii = ty; ii < 32; ii += 8) {
@@ -220,7 +220,7 @@ __global__ void rows_out_kernel(T *__restrict__ B, int64_t ldb, const T *__restr
     __syncthreads();
     for (int cc = ty; cc < 32; cc += 8) {
         const int i = i0 + tx, c = c0 + cc;
-        if (i < n && c < k) B[i + (int64_t)c * ldb] = t[tx][cc];
+        if (i < n && c < k) B[i + (int64_t)(cmap ? cmap[c] : c) * ldb] = t[tx][cc];
     }
 }
 
@@ -250,6 +250,13 @@ __global__ void unit_sources_kernel(T *__restrict__ X, int64_t ldx, const int *_
                                     int k) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c < k) X[(int64_t)invp[col0 + c] * ldx + c] = Sem<SR, T>::one();
+}
+
+// X[pos[c]][c] = one: unit sources at given positions (the star's panels in elimination order)
+template <int SR, typename T>
+__global__ void unit_positions_kernel(T *__restrict__ X, int64_t ldx, const int *__restrict__ pos, int k) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c < k) X[(int64_t)pos[c] * ldx + c] = Sem<SR, T>::one();
 }
 
 // copyto!(F, A) on the device (scopyto_loop!, src/CPU/chordal_slu.jl:221-321): a warp per column of A

@@ -309,6 +309,19 @@ struct Engine {
         return cudaGetLastError();
     }
 
+    static cudaError_t unit_positions(void *X, int64_t ldx, const int *pos, int k, cudaStream_t st) {
+        unit_positions_kernel<SR, T><<<(k + 255) / 256, 256, 0, st>>>(static_cast<T *>(X), ldx, pos, k);
+        return cudaGetLastError();
+    }
+
+    static cudaError_t rows_out_mapped(void *B, int64_t ldb, const void *X, int64_t ldx, const int *invp,
+                                       const int *cmap, int n, int k, cudaStream_t st) {
+        dim3 grid((n + 31) / 32, (k + 31) / 32), block(32, 8);
+        rows_out_kernel<T><<<grid, block, 0, st>>>(static_cast<T *>(B), ldb, static_cast<const T *>(X), ldx, invp, n, k,
+                                                   cmap);
+        return cudaGetLastError();
+    }
+
     static cudaError_t rows_in(const void *B, int64_t ldb, void *X, int64_t ldx, const int *invp, int n, int k,
                                cudaStream_t st) {
         dim3 grid((n + 31) / 32, (k + 31) / 32), block(32, 8);
@@ -318,7 +331,8 @@ struct Engine {
     static cudaError_t rows_out(void *B, int64_t ldb, const void *X, int64_t ldx, const int *invp, int n, int k,
                                 cudaStream_t st) {
         dim3 grid((n + 31) / 32, (k + 31) / 32), block(32, 8);
-        rows_out_kernel<T><<<grid, block, 0, st>>>(static_cast<T *>(B), ldb, static_cast<const T *>(X), ldx, invp, n, k);
+        rows_out_kernel<T><<<grid, block, 0, st>>>(static_cast<T *>(B), ldb, static_cast<const T *>(X), ldx, invp, n, k,
+                                                   nullptr);
         return cudaGetLastError();
     }
     static cudaError_t cols_in(const void *B, int64_t ldb, void *X, int64_t ldx, const int *invp, int n, int k,
@@ -388,6 +402,8 @@ struct Engine {
         o.unit_sources = &unit_sources;
         o.rows_in = &rows_in;
         o.rows_out = &rows_out;
+        o.unit_positions = &unit_positions;
+        o.rows_out_mapped = &rows_out_mapped;
         o.cols_in = &cols_in;
         o.cols_out = &cols_out;
         o.gemm = &gemm;

@@ -161,6 +161,9 @@ struct Ops {
                            cudaStream_t st);
     cudaError_t (*rows_out)(void *B, int64_t ldb, const void *X, int64_t ldx, const int *invp, int n, int k,
                             cudaStream_t st);
+    cudaError_t (*unit_positions)(void *X, int64_t ldx, const int *pos, int k, cudaStream_t st);
+    cudaError_t (*rows_out_mapped)(void *B, int64_t ldb, const void *X, int64_t ldx, const int *invp, const int *cmap,
+                                   int n, int k, cudaStream_t st);
     cudaError_t (*cols_in)(const void *B, int64_t ldb, void *X, int64_t ldx, const int *invp, int n, int k,
                            cudaStream_t st);
     cudaError_t (*cols_out)(void *B, int64_t ldb, const void *X, int64_t ldx, const int *invp, int n, int k,

@@ -92,6 +92,14 @@ def test_config4_knn_star_columns(gpu):
         assert np.array_equal(np.isinf(C), np.isinf(want))
         f = np.isfinite(want)
         np.testing.assert_allclose(C[f], want[f], rtol=1e-5)
+        # the whole star into device memory (two wide panels in elimination order): the same columns, bit for bit
+        import torch
+
+        D = torch.empty((n, n), dtype=torch.float32, device="cuda:0").t()
+        F.star(out=D)
+        got = D[:, torch.from_numpy(cols).cuda()].cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), C.view(np.uint32))
+        del D
     finally:
         F.close()
 

@@ -175,3 +175,22 @@ def test_star_panels(gpu, name, dtype):
             same(C, full, name, dtype, "star from %d panels" % world)
     finally:
         F.close()
+
+
+@pytest.mark.parametrize("name,dtype", [("MinPlus", np.float64), ("MaxMin", np.float32), ("PlusProd", np.float64),
+                                        ("OrAnd", np.int32)])
+@pytest.mark.parametrize("kind", ["grid3d", "knn"])
+def test_star_device_output(gpu, name, dtype, kind):
+    """Matrix(F) into device memory (its columns taken in elimination order and written to their own columns)
+    equals the star into host memory (columns in label order), for whole and partial column ranges."""
+    import torch
+
+    n, S, F, O = factor_both(kind, name, dtype)
+    try:
+        for col0, ncols in [(0, n), (7, n - 20), (n // 3, 33), (5, 32), (n - 1, 1)]:
+            host = F.star(col0, ncols)
+            dev = torch.empty((ncols, n), dtype=torch_dt(dtype), device="cuda:0").t()
+            F.star(col0, ncols, out=dev)
+            same(dev.cpu().numpy(), host, name, dtype, "%s device star [%d, +%d)" % (kind, col0, ncols))
+    finally:
+        F.close()

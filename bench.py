@@ -435,7 +435,7 @@ def _roofline_alu(prof, steps, semiring, dtype, pk):
             "GB_per_s": d["bytes"] / (d["ms"] / 1e3) / 1e9 if d["ms"] > 0 else 0.0}
 
 
-def measure_star(key, rank, world, dev, steps, warmup, e2e=True, cpu=False, w=None):
+def measure_star(key, rank, world, dev, steps, warmup, e2e=True, cpu=False, w=None, columns=None):
     """mlu + this rank's column panel of Matrix(F) for a star workload; returns the numbers of one rank (times
     already the max over ranks)."""
     import torch
@@ -450,6 +450,8 @@ def measure_star(key, rank, world, dev, steps, warmup, e2e=True, cpu=False, w=No
     tdt = {np.dtype(np.float32): torch.float32, np.dtype(np.float64): torch.float64}[np.dtype(w["dtype"])]
     es = np.dtype(w["dtype"]).itemsize
     col0, ncols = column_panels(n, world)[rank]
+    if columns:  # a smaller case of the same kernels (profiling captures): the first columns of the panel
+        ncols = min(ncols, int(columns))
     F = pp.B200SLU(sr, w["dtype"], S, device=dev)
     F.assemble_csc(w["cp"], w["rv"], w["nz"]).factor()
     stream = torch.cuda.ExternalStream(F.stream(), device=dev)
@@ -490,7 +492,8 @@ def measure_star(key, rank, world, dev, steps, warmup, e2e=True, cpu=False, w=No
     pairs = _sum_over_ranks(pairs_rank, dev, world)  # every rank factors: its pairs count
     r = {"ms_per_step": ms / steps, "wall_s": ms / steps / 1e3, "pairs_per_step": pairs,
          "value": pairs * steps / (ms / 1e3), "launches": launches * steps, "clocks": clk.summary(),
-         "columns_per_rank": [c for _, c in column_panels(n, world)], "symbolic_s": w["symbolic_s"]}
+         "columns_per_rank": [min(c, int(columns)) if columns else c for _, c in column_panels(n, world)],
+         "symbolic_s": w["symbolic_s"]}
     if e2e:
         # host weights in, the rank's panel of the star out into pinned host memory, both inside the call
         host = torch.empty((max(ncols, 1), n), dtype=tdt, pin_memory=True)
@@ -551,7 +554,7 @@ def run_star(args, rank, world, local):
     key = args.workload
     w = star_workload(key)
     r = measure_star(key, rank, world, local, args.steps, args.warmup, e2e=not args.no_e2e,
-                     cpu=not args.no_cpu_baseline, w=w)
+                     cpu=not args.no_cpu_baseline and not args.columns, w=w, columns=args.columns)
     if rank != 0:
         return
     pk, _ = peaks()
@@ -814,6 +817,9 @@ def main():
                          "over the ranks) or a config-5 kernel")
     ap.add_argument("--no-e2e", action="store_true", help="star workloads: skip the host-output e2e calls")
     ap.add_argument("--no-mstar", action="store_true", help="config2: skip the config-4 mstar sub-measurement")
+    ap.add_argument("--columns", type=int, default=None,
+                    help="star workloads: compute only the first C columns of each rank's panel (a smaller case "
+                         "of the same kernels, for profiling captures; the line then covers those columns)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -14,6 +14,7 @@
 #include "ops.h"
 #include "persist.cuh"
 #include "sweep_top.cuh"
+#include "sweep_wide.cuh"
 #include "top.cuh"
 
 namespace pp {
@@ -124,12 +125,54 @@ struct Engine {
         return cudaSuccess;
     }
 
+    template <bool FWD, bool TRANS>
+    static cudaError_t sweep_wide(const HostPlan &hp, const std::pair<int64_t, int> &wl, const SLevel &cost,
+                                  const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
+                                  int64_t *nl) {
+        constexpr size_t smem = sweep_wide_smem<T>();
+        int dev = 0;
+        cudaGetDevice(&dev);
+        static bool attr[64] = {};
+        if (dev < 64 && !attr[dev]) {
+            PP_TRY(cudaFuncSetAttribute(sweep_wide_kernel<SR, T, FWD, TRANS>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attr[dev] = true;
+        }
+        const int ntiles = (k + SWW_CT - 1) / SWW_CT;
+        const size_t cells = (size_t)ntiles * hp.nf;  // per (tile, front)
+        if (FWD) {
+            PP_TRY(reset_sync(hp, hp.d_tpending0, ntiles, st));
+            PP_TRY(cudaMemsetAsync(hp.d_sync + 16 + cells, 0, sizeof(int) * 2 * cells, st));  // blocks done
+        } else {
+            PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int), st));
+            PP_TRY(cudaMemsetAsync(hp.d_sync + 16, 0, sizeof(int) * 2 * cells, st));  // done flags, blocks done
+        }
+        int per_sm = 1;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_wide_kernel<SR, T, FWD, TRANS>, 256, smem);
+        const int64_t tasks = (int64_t)wl.second * ntiles;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tasks, std::max(per_sm, 1) * hp.sm_count));
+        const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD : K_SWEEP_BWD, st) : -1;
+        sweep_wide_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_tentries + wl.first, wl.second, hp.dev, Dv,
+                                                                      Ov, X, ldx, k, unit, hp.d_sync + 16, hp.d_sync,
+                                                                      hp.d_err);
+        PP_TRY(cudaGetLastError());
+        if (pi >= 0)
+            hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
+                         (double)k * cost.pairs_col);
+        (*nl)++;
+        return cudaSuccess;
+    }
+
     // the top fronts of a stage: one persistent launch (sweep_top_kernel), counters reset from a template
     template <bool FWD, bool TRANS>
     static cudaError_t sweep_top(const HostPlan &hp, const std::pair<int64_t, int> &wl, const SLevel &cost,
                                  const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
                                  int64_t *nl) {
         if (wl.second == 0) return cudaSuccess;
+        // many right-hand sides (the star's panels, wide solves): 128-column tasks, when the rows of X allow
+        // 16-byte vector loads
+        if (k > 256 && ldx % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0)
+            return sweep_wide<FWD, TRANS>(hp, wl, cost, Dv, Ov, X, ldx, k, unit, st, nl);
         constexpr size_t smem = sweep_top_smem<T>();
         int dev = 0;
         cudaGetDevice(&dev);

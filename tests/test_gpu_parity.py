@@ -194,3 +194,22 @@ def test_star_device_output(gpu, name, dtype, kind):
             same(dev.cpu().numpy(), host, name, dtype, "%s device star [%d, +%d)" % (kind, col0, ncols))
     finally:
         F.close()
+
+
+@pytest.mark.parametrize("name,dtype", [("MinPlus", np.float64), ("MaxMin", np.float32), ("PlusProd", np.float64),
+                                        ("OrAnd", np.int32), ("MaxPlus", np.float32)])
+@pytest.mark.parametrize("k", [300, 513])
+def test_wide_solves(gpu, name, dtype, k):
+    """lmul! and rmul! with more than 256 right-hand sides (the top fronts' 128-column tasks) against the oracle."""
+    n, S, F, O = factor_both("grid3d", name, dtype)
+    try:
+        rng = np.random.default_rng(k)
+        z, one = SR[name].zero(dtype), SR[name].one(dtype)
+        B = np.full((n, k), z, dtype=dtype, order="F")
+        B[rng.integers(0, n, size=k), np.arange(k)] = one
+        B[rng.random(B.shape) < 0.02] = one
+        same(pp.lmul_(F, B.copy(order="F")), O.lmul(B), name, dtype, "wide lmul k=%d" % k)
+        R = np.asfortranarray(B.T)
+        same(pp.rmul_(R.copy(order="F"), F), O.rmul(R), name, dtype, "wide rmul k=%d" % k)
+    finally:
+        F.close()

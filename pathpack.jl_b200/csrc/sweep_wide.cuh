@@ -16,6 +16,8 @@
 // sgemx2! (src/CPU/dense/strsx.jl:596-672, src/CPU/chordal/strsx.jl:187-265, 783-830).
 #pragma once
 
+#include <type_traits>
+
 #include "sweep_top.cuh"
 
 namespace pp {
@@ -63,8 +65,7 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
     using VT = typename Vec16<T>::V;
     constexpr int NV = Vec16<T>::n;                      // elements per 16-byte vector
     constexpr int XV = SW_KC * SWW_CT / NV / 256;        // right-hand-side vectors per thread per chunk
-    constexpr int AE = SW_KC * SW_RB / 256;              // matrix elements per thread per chunk
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+        extern __shared__ __align__(16) unsigned char smem_raw[];
     T *As = reinterpret_cast<T *>(smem_raw);              // 2 x [SW_KC][SWW_AL]
     T *Xs = As + 2 * SW_KC * SWW_AL;                      // 2 x [SW_KC][SWW_CT]
     T *Ys = As;                                           // [SW_RB][SWW_YL], aliases the chunks
@@ -100,32 +101,37 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
         auto xres = [&](int q) { return rlo + q; };
         auto xsep = [&](int i) { return sep[i]; };
 
+        // tile rows per task: 64 (4 per thread), or 16 (1 per thread) when the task has at most 16 rows (most top
+        // fronts have a few pivots; their 64-row tiles were mostly padding).  R is std::integral_constant<int, 4 or 1>.
         T acc[4][8];
-        auto load_acc = [&](int rowbase, int nrows, bool from_x) {
+        auto row_of = [&](auto R, int i) { return decltype(R)::value == 4 ? 4 * tr + i : tr; };
+        auto load_acc = [&](auto R, int rowbase, int nrows, bool from_x) {
+            constexpr int RPT = decltype(R)::value;
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int i = 0; i < RPT; i++)
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    const int r = 4 * tr + i, c = c0 + 8 * tc + j;
+                    const int r = row_of(R, i), c = c0 + 8 * tc + j;
                     acc[i][j] = (from_x && r < nrows && c < k) ? ld_cg(X + (int64_t)(rowbase + r) * ldx + c) : z;
                 }
         };
         // acc[i][j] (+)= M(rb + row_i, kidx) (x) X[xrow(kidx)][col_j] for kidx in [kb, ke), ascending or
         // descending; chunk ch + 1 is fetched into registers while chunk ch is used
-        auto accum = [&](int rb, int nrows, int kb, int ke, bool desc, auto M, auto xrow) {
+        auto accum = [&](auto R, int rb, int nrows, int kb, int ke, bool desc, auto M, auto xrow) {
+            constexpr int RPT = decltype(R)::value, TR = 16 * RPT, AER = SW_KC * TR / 256;
             const int kn = ke - kb;
             if (kn <= 0) return;
             const int nch = (kn + SW_KC - 1) / SW_KC;
-            T ra[AE];
+            T ra[AER];
             VT rx[XV];
             auto fetch = [&](int ch) {
                 const int kc = min(SW_KC, kn - ch * SW_KC);
                 const int cb = desc ? ke - ch * SW_KC - kc : kb + ch * SW_KC;
 #pragma unroll
-                for (int q = 0; q < AE; q++) {
+                for (int q = 0; q < AER; q++) {
                     // consecutive threads read consecutive addresses: rows of the stored blocks, or (TRANS) columns
                     const int e = tid + 256 * q;
-                    const int r = TRANS ? e / SW_KC : e % SW_RB, kk = TRANS ? e % SW_KC : e / SW_RB;
+                    const int r = TRANS ? e / SW_KC : e % TR, kk = TRANS ? e % SW_KC : e / TR;
                     ra[q] = (r < nrows && kk < kc) ? M(rb + r, cb + kk) : z;
                 }
 #pragma unroll
@@ -144,9 +150,9 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
                 T *a = As + buf * SW_KC * SWW_AL;
                 T *x = Xs + buf * SW_KC * SWW_CT;
 #pragma unroll
-                for (int q = 0; q < AE; q++) {
+                for (int q = 0; q < AER; q++) {
                     const int e = tid + 256 * q;
-                    const int r = TRANS ? e / SW_KC : e % SW_RB, kk = TRANS ? e % SW_KC : e / SW_RB;
+                    const int r = TRANS ? e / SW_KC : e % TR, kk = TRANS ? e % SW_KC : e / TR;
                     a[kk * SWW_AL + r] = ra[q];
                 }
 #pragma unroll
@@ -161,19 +167,24 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
             for (int ch = 0; ch < nch; ch++) {
                 if (ch + 1 < nch) fetch(ch + 1);
                 const int kc = min(SW_KC, kn - ch * SW_KC);
-                const T *a = As + (ch & 1) * SW_KC * SWW_AL + 4 * tr;
+                const T *a = As + (ch & 1) * SW_KC * SWW_AL + (RPT == 4 ? 4 * tr : tr);
                 const T *x = Xs + (ch & 1) * SW_KC * SWW_CT + 8 * tc;
                 for (int u = 0; u < kc; u++) {
                     const int kk = desc ? kc - 1 - u : u;
                     T av[4], xv[8];
+                    if (RPT == 4) {
 #pragma unroll
-                    for (int q = 0; q < 4 / NV; q++)
-                        *reinterpret_cast<VT *>(av + q * NV) = *reinterpret_cast<const VT *>(a + kk * SWW_AL + q * NV);
+                        for (int q = 0; q < 4 / NV; q++)
+                            *reinterpret_cast<VT *>(av + q * NV) =
+                                *reinterpret_cast<const VT *>(a + kk * SWW_AL + q * NV);
+                    } else {
+                        av[0] = a[kk * SWW_AL];
+                    }
 #pragma unroll
                     for (int q = 0; q < 8 / NV; q++)
                         *reinterpret_cast<VT *>(xv + q * NV) = *reinterpret_cast<const VT *>(x + kk * SWW_CT + q * NV);
 #pragma unroll
-                    for (int i = 0; i < 4; i++)
+                    for (int i = 0; i < RPT; i++)
 #pragma unroll
                         for (int j = 0; j < 8; j++) acc[i][j] = S::muladd(av[i], xv[j], acc[i][j]);
                 }
@@ -183,16 +194,19 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
                 __syncthreads();
             }
         };
-        auto acc_to_ys = [&]() {
+        auto acc_to_ys = [&](auto R) {
+            constexpr int RPT = decltype(R)::value;
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int i = 0; i < RPT; i++)
 #pragma unroll
-                for (int j = 0; j < 8; j++) Ys[(4 * tr + i) * SWW_YL + 8 * tc + j] = acc[i][j];
+                for (int j = 0; j < 8; j++) Ys[row_of(R, i) * SWW_YL + 8 * tc + j] = acc[i][j];
         };
+        using R4 = std::integral_constant<int, 4>;
+        using R1 = std::integral_constant<int, 1>;
 
         // the diagonal block of rows r0 .. r0 + nv - 1: acc -> Ys, solved warp by warp, written to X
-        auto diag_solve = [&](int r0, int nv) {
-            acc_to_ys();
+        auto diag_solve = [&](auto R, int r0, int nv) {
+            acc_to_ys(R);
             for (int e = tid; e < SW_RB * SW_RB; e += 256) {
                 const int q = TRANS ? e / SW_RB : e % SW_RB, c = TRANS ? e % SW_RB : e / SW_RB;
                 Dd[q * SW_DL + c] = (q < nv && c < nv) ? Te(r0 + q, r0 + c) : z;
@@ -268,12 +282,16 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
                 live = (v >> 16) == 0;
             }
             if (live) {
-                load_acc(rlo + r0, nv, true);
-                for (int j = 0; j < b; j++) {
-                    if (j > 0 && cta_wait_blocks(bd, j + 1, err) < 0) return;
-                    accum(r0, nv, j * SW_RB, (j + 1) * SW_RB, false, Te, xres);
-                }
-                diag_solve(r0, nv);
+                auto body = [&](auto R) -> bool {
+                    load_acc(R, rlo + r0, nv, true);
+                    for (int j = 0; j < b; j++) {
+                        if (j > 0 && cta_wait_blocks(bd, j + 1, err) < 0) return false;
+                        accum(R, r0, nv, j * SW_RB, (j + 1) * SW_RB, false, Te, xres);
+                    }
+                    diag_solve(R, r0, nv);
+                    return true;
+                };
+                if (!(nv <= 16 ? body(R1{}) : body(R4{}))) return;
             }
             __syncthreads();
             if (tid == 0) {
@@ -288,9 +306,15 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
             if ((v >> 16) == 0) {
                 auto Of = [&](int i, int q) -> T { return TRANS ? O[q + (int64_t)i * nn] : O[i + (int64_t)q * na]; };
                 const int i0 = (b - kb) * SW_RB, nv = min(SW_RB, na - i0);
-                load_acc(0, 0, false);
-                accum(i0, nv, 0, nn, false, Of, xres);
-                acc_to_ys();
+                auto body = [&](auto R) {
+                    load_acc(R, 0, 0, false);
+                    accum(R, i0, nv, 0, nn, false, Of, xres);
+                    acc_to_ys(R);
+                };
+                if (nv <= 16)
+                    body(R1{});
+                else
+                    body(R4{});
                 __syncthreads();
                 for (int e = tid; e < SW_RB * SWW_CT; e += 256) {
                     const int r = e / SWW_CT, c = e % SWW_CT;
@@ -307,13 +331,17 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
             // then the diagonal solve
             auto Ob = [&](int r, int i) -> T { return TRANS ? O[i + (int64_t)r * na] : O[r + (int64_t)i * nn]; };
             const int r0 = b * SW_RB, r1 = min(nn, r0 + SW_RB), nv = r1 - r0;
-            load_acc(rlo + r0, nv, true);
-            accum(r0, nv, 0, na, false, Ob, xsep);
-            for (int j = kb - 1; j > b; j--) {
-                if (cta_wait_blocks(bd, kb - j, err) < 0) return;
-                accum(r0, nv, j * SW_RB, min(nn, (j + 1) * SW_RB), true, Te, xres);
-            }
-            diag_solve(r0, nv);
+            auto body = [&](auto R) -> bool {
+                load_acc(R, rlo + r0, nv, true);
+                accum(R, r0, nv, 0, na, false, Ob, xsep);
+                for (int j = kb - 1; j > b; j--) {
+                    if (cta_wait_blocks(bd, kb - j, err) < 0) return false;
+                    accum(R, r0, nv, j * SW_RB, min(nn, (j + 1) * SW_RB), true, Te, xres);
+                }
+                diag_solve(R, r0, nv);
+                return true;
+            };
+            if (!(nv <= 16 ? body(R1{}) : body(R4{}))) return;
             __syncthreads();
             if (tid == 0) {
                 __threadfence();

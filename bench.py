@@ -159,6 +159,11 @@ class Clocks:
             self.f = open(self.path, "w")
             self.p = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
                                        "-i", str(self.index), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+            # a timed region of a few tens of ms fits between two samples: start timing once the sampler runs, so
+            # that at least the sample taken right after the warm-up (clocks under load) is recorded
+            t0 = time.time()
+            while time.time() - t0 < 3.0 and os.path.getsize(self.path) == 0:
+                time.sleep(0.01)
         except Exception:
             self.p = None
         return self

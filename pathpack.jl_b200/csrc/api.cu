@@ -517,6 +517,21 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         std::vector<double> subtree_cost(nf, 0.0);  // of a subtree root: its fronts' estimated task times
         for (int64_t f = 0; f < nf; f++)
             if (covered[f]) subtree_cost[sroot_of[f]] += scost[f];
+        hp.stree_pairs.assign(nf, 0.0);
+        hp.stree_res.assign(nf, 0.0);
+        hp.stree_sep.assign(nf, 0.0);
+        hp.stree_fac.assign(nf, 0.0);
+        for (int64_t f = 0; f < nf; f++) {
+            if (!covered[f]) continue;
+            const int r = sroot_of[f];
+            const double nn = hp.nn[f], na = hp.na[f];
+            hp.stree_pairs[r] += nn * (nn - 1) / 2 + nn * na;
+            hp.stree_fac[r] += nn * nn + nn * na;
+            if (r == f) {
+                hp.stree_res[r] = (double)(R[f + 1] - R[fdsc[f]]);
+                hp.stree_sep[r] = na;
+            }
+        }
         auto build_stages = [&](const std::vector<int> &stage_of, std::vector<Stage> &out, std::vector<int> &sfronts,
                                 std::vector<int> &sverts, std::vector<std::pair<int64_t, int>> &bfwd,
                                 std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost,
@@ -807,6 +822,17 @@ static int32_t prepare_workspace(pp_handle *h) {
             int *b = h->sfronts.data() + fw[0].first;
             hp.early_bot[d] = (int)(std::stable_partition(b, b + fw[0].second, in_bottom) - b);
         }
+    }
+    hp.sroot_pairs.resize(h->sroots.size());
+    hp.sroot_res.resize(h->sroots.size());
+    hp.sroot_sep.resize(h->sroots.size());
+    hp.sroot_fac.resize(h->sroots.size());
+    for (size_t i = 0; i < h->sroots.size(); i++) {
+        const int r = h->sroots[i];
+        hp.sroot_pairs[i] = hp.stree_pairs[r];
+        hp.sroot_res[i] = hp.stree_res[r];
+        hp.sroot_sep[i] = hp.stree_sep[r];
+        hp.sroot_fac[i] = hp.stree_fac[r];
     }
     CK(h, upload(h->d_sroots, h->sroots, st), "upload");
     CK(h, upload(h->d_sfronts, h->sfronts, st), "upload");

@@ -263,7 +263,14 @@ struct Engine {
         sweep_subtree_kernel<SR, T, FWD, TRANS><<<(unsigned)((tasks + 3) / 4), 128, smem, st>>>(
             hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit);
         PP_TRY(cudaGetLastError());
-        if (pi >= 0) hp.prof->end(pi, st, 0, 0);
+        if (pi >= 0) {
+            double pairs = 0, elems = 0;
+            for (int64_t i = sl.off; i < sl.off + sl.count && i < (int64_t)hp.sroot_pairs.size(); i++) {
+                pairs += hp.sroot_pairs[i];
+                elems += hp.sroot_fac[i] / k + 2.0 * hp.sroot_res[i] + (FWD ? 2.0 : 1.0) * hp.sroot_sep[i];
+            }
+            hp.prof->end(pi, st, elems * k, pairs * k);
+        }
         (*nl)++;
         return cudaSuccess;
     }

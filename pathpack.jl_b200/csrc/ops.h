@@ -122,6 +122,10 @@ struct HostPlan {
     const int *d_spending0 = nullptr;  // bottom children per front (forward counters)
     // subtrees solved in shared memory (per stage), their roots, first descendants and separator slots
     std::vector<SubtreeList> sub_l, sub_r;
+    // profiler sums of a subtree, by root front: (x)(+) pairs per column, rows per column (residual range and
+    // root separator), factor elements; sroot_cost holds them in the order of the device root list
+    std::vector<double> stree_pairs, stree_res, stree_sep, stree_fac;
+    std::vector<double> sroot_pairs, sroot_res, sroot_sep, sroot_fac;
     const int *d_sroots = nullptr, *d_fdsc = nullptr, *d_slot = nullptr;
     int bot_fmax = 0, bot_namax = 0;   // largest nn * nn + nn * na and na of the other bottom fronts
     const int *d_sdone0 = nullptr;     // 1 for fronts outside the bottom, 0 inside (backward flags)

@@ -208,11 +208,11 @@ __global__ void __launch_bounds__(256) sweep_top_kernel(const int2 *__restrict__
                         T yq = __shfl_sync(0xffffffffu, y[u], src | g);
                         if (scale) yq = S::mul(yq, S::star(Dd[q * SW_DL + q]));
                         if (dg == g) y[u] = yq;
+                        // rows dg + 8 v below pivot 8 u + g: v > u, or v == u and dg > g (u is unrolled, so only
+                        // slot u is tested); rows at or past nv hold values that are never pivots or stored
 #pragma unroll
-                        for (int v = 0; v < 8; v++) {
-                            const int r = dg + 8 * v;
-                            if (r > q && r < nv) y[v] = S::muladd(Dd[r * SW_DL + q], yq, y[v]);
-                        }
+                        for (int v = u; v < 8; v++)
+                            if (v > u || dg > g) y[v] = S::muladd(Dd[(dg + 8 * v) * SW_DL + q], yq, y[v]);
                     }
             } else {
 #pragma unroll
@@ -223,11 +223,10 @@ __global__ void __launch_bounds__(256) sweep_top_kernel(const int2 *__restrict__
                         T yq = __shfl_sync(0xffffffffu, y[u], src | g);
                         if (scale) yq = S::mul(S::star(Dd[q * SW_DL + q]), yq);
                         if (dg == g) y[u] = yq;
+                        // rows dg + 8 v above pivot 8 u + g: v < u, or v == u and dg < g
 #pragma unroll
-                        for (int v = 0; v < 8; v++) {
-                            const int r = dg + 8 * v;
-                            if (r < q) y[v] = S::muladd(Dd[r * SW_DL + q], yq, y[v]);
-                        }
+                        for (int v = 0; v <= u; v++)
+                            if (v < u || dg < g) y[v] = S::muladd(Dd[(dg + 8 * v) * SW_DL + q], yq, y[v]);
                     }
             }
 #pragma unroll

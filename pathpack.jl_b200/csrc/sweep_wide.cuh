@@ -169,9 +169,7 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
                 const int kc = min(SW_KC, kn - ch * SW_KC);
                 const T *a = As + (ch & 1) * SW_KC * SWW_AL + (RPT == 4 ? 4 * tr : tr);
                 const T *x = Xs + (ch & 1) * SW_KC * SWW_CT + 8 * tc;
-                for (int u = 0; u < kc; u++) {
-                    const int kk = desc ? kc - 1 - u : u;
-                    T av[4], xv[8];
+                auto ldrow = [&](int kk, T *av, T *xv) {
                     if (RPT == 4) {
 #pragma unroll
                         for (int q = 0; q < 4 / NV; q++)
@@ -183,6 +181,26 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
 #pragma unroll
                     for (int q = 0; q < 8 / NV; q++)
                         *reinterpret_cast<VT *>(xv + q * NV) = *reinterpret_cast<const VT *>(x + kk * SWW_CT + q * NV);
+                };
+                // MaxMin / MinMax in 4-byte types: two k per step (muladd2: min, min and one 3-input max, 3 ALU
+                // instructions for 2 pairs instead of 4), the two terms in the sweep's order.  Elsewhere one k
+                // (measured: the packed-add form of MinPlus Float32 ran slower here; 8-byte types run out of
+                // registers)
+                constexpr bool kpair = sizeof(T) == 4 && (SR == MAXMIN || SR == MINMAX);
+                int u = 0;
+                for (; kpair && u + 1 < kc; u += 2) {
+                    const int k0 = desc ? kc - 1 - u : u, k1 = desc ? k0 - 1 : k0 + 1;
+                    T av0[4], xv0[8], av1[4], xv1[8];
+                    ldrow(k0, av0, xv0);
+                    ldrow(k1, av1, xv1);
+#pragma unroll
+                    for (int i = 0; i < RPT; i++)
+#pragma unroll
+                        for (int j = 0; j < 8; j++) acc[i][j] = S::muladd2(acc[i][j], av0[i], av1[i], xv0[j], xv1[j]);
+                }
+                for (; u < kc; u++) {
+                    T av[4], xv[8];
+                    ldrow(desc ? kc - 1 - u : u, av, xv);
 #pragma unroll
                     for (int i = 0; i < RPT; i++)
 #pragma unroll
@@ -228,11 +246,11 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
                             T yq = __shfl_sync(0xffffffffu, y[u], src | g);
                             if (scale) yq = S::mul(yq, S::star(Dd[q * SW_DL + q]));
                             if (dg == g) y[u] = yq;
+                        // rows dg + 8 v below pivot 8 u + g: v > u, or v == u and dg > g (u is unrolled, so only
+                        // slot u is tested); rows at or past nv hold values that are never pivots or stored
 #pragma unroll
-                            for (int v = 0; v < 8; v++) {
-                                const int r = dg + 8 * v;
-                                if (r > q && r < nv) y[v] = S::muladd(Dd[r * SW_DL + q], yq, y[v]);
-                            }
+                        for (int v = u; v < 8; v++)
+                            if (v > u || dg > g) y[v] = S::muladd(Dd[(dg + 8 * v) * SW_DL + q], yq, y[v]);
                         }
                 } else {
 #pragma unroll
@@ -243,11 +261,10 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
                             T yq = __shfl_sync(0xffffffffu, y[u], src | g);
                             if (scale) yq = S::mul(S::star(Dd[q * SW_DL + q]), yq);
                             if (dg == g) y[u] = yq;
+                        // rows dg + 8 v above pivot 8 u + g: v < u, or v == u and dg < g
 #pragma unroll
-                            for (int v = 0; v < 8; v++) {
-                                const int r = dg + 8 * v;
-                                if (r < q) y[v] = S::muladd(Dd[r * SW_DL + q], yq, y[v]);
-                            }
+                        for (int v = 0; v <= u; v++)
+                            if (v < u || dg < g) y[v] = S::muladd(Dd[(dg + 8 * v) * SW_DL + q], yq, y[v]);
                         }
                 }
 #pragma unroll

@@ -366,7 +366,21 @@ __device__ __forceinline__ void subtree_front(int nn, int na, T *xg, T *xs, cons
         }
     } else {
         const int ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
-        for (int i = 0; i < na; i++) {
+        // four separator rows per step, their slots and values loaded together; per element the terms in
+        // increasing i as before
+        int i = 0;
+        for (; i + 4 <= na; i += 4) {
+            T xi[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) xi[j] = xs[32 * sl[i + j]];
+#pragma unroll
+            for (int p = 0; p < NMAX; p++)
+                if (p < nn) {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) x[p] = S::muladd(O[p * ors + (i + j) * ocs], xi[j], x[p]);
+                }
+        }
+        for (; i < na; i++) {
             const T xi = xs[32 * sl[i]];
 #pragma unroll
             for (int p = 0; p < NMAX; p++)

@@ -218,7 +218,7 @@ __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &
 #pragma unroll
             for (int p = 0; p < NMAX; p++)
                 if (p < nn) a = S::muladd(Os[i * ors + p * ocs], x[p], a);
-            if (ok) S::atomic_add(Xc + (int64_t)sb[i] * ldx, a);
+            if (ok && !(a == z)) S::atomic_add(Xc + (int64_t)sb[i] * ldx, a);  // (+) zero changes nothing
         }
     } else {
         const int ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
@@ -470,7 +470,10 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     if (!ok) return;
     for (int s = 0; s < nres; s++) Xc[(int64_t)(rlo0 + s) * ldx] = xs[32 * s];
     if (FWD)
-        for (int i = 0; i < nsep; i++) S::atomic_add(Xc + (int64_t)sepr[i] * ldx, xs[32 * (nres + i)]);
+        for (int i = 0; i < nsep; i++) {
+            const T v = xs[32 * (nres + i)];
+            if (!(v == z)) S::atomic_add(Xc + (int64_t)sepr[i] * ldx, v);  // (+) zero changes nothing
+        }
 }
 
 // flags[t * nf + f] = init[f] for every tile t

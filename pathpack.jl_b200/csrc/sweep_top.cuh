@@ -287,7 +287,10 @@ __global__ void __launch_bounds__(256) sweep_top_kernel(const int2 *__restrict__
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
                         const int r = tr + 32 * i, c = c0 + tc + 8 * j;
-                        if (r < nv && c < k) S::atomic_add(X + (int64_t)sep[i0 + r] * ldx + c, acc[i][j]);
+                        // (+) with zero changes nothing: zero sums (columns whose sources lie outside the front's
+                        // subtree) are not scattered
+                        if (r < nv && c < k && !(acc[i][j] == z))
+                            S::atomic_add(X + (int64_t)sep[i0 + r] * ldx + c, acc[i][j]);
                     }
             }
             __syncthreads();

@@ -335,7 +335,9 @@ __global__ void __launch_bounds__(256, 2) sweep_wide_kernel(const int2 *__restri
                 __syncthreads();
                 for (int e = tid; e < SW_RB * SWW_CT; e += 256) {
                     const int r = e / SWW_CT, c = e % SWW_CT;
-                    if (r < nv && c0 + c < k) S::atomic_add(X + (int64_t)sep[i0 + r] * ldx + c0 + c, Ys[r * SWW_YL + c]);
+                    const T v = Ys[r * SWW_YL + c];
+                    // (+) with zero changes nothing: zero sums are not scattered
+                    if (r < nv && c0 + c < k && !(v == z)) S::atomic_add(X + (int64_t)sep[i0 + r] * ldx + c0 + c, v);
                 }
             }
             __syncthreads();

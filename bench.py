@@ -729,9 +729,13 @@ def run_kernel(args, rank, world, local):
     sms = torch.cuda.get_device_properties(local).multi_processor_count
     peak = alu_peak(w["semiring"], w["dtype"], sms, float(pk.get("sm_max_mhz", 1965.0)))
     per_launch = ms / 1e3 / args.steps
-    roof = {"kernel": "getrf_batched_kernel" if key == "config5a" else "gemm_kernel", "bound": "alu",
+    dmma = key == "config5b-f64"
+    roof = {"kernel": "getrf_reg_kernel" if key == "config5a" else ("gemm_dmma_kernel" if dmma else "gemm_kernel"),
+            "bound": "tensor" if dmma else "alu",
             "achieved": x["pairs"] / per_launch, "peak": peak, "unit": "pairs/s", "frac": x["pairs"] / per_launch / peak,
-            "traffic": None, "peak_source": "nominal ALU issue rate (SMs x max SM clock x lanes / instructions per pair)",
+            "traffic": None,
+            "peak_source": ("nominal FP64 tensor (DMMA) rate: SMs x max SM clock x 64 multiply-adds per clock" if dmma
+                            else "nominal ALU issue rate (SMs x max SM clock x lanes / instructions per pair)"),
             "hbm_GB_per_s": nbytes / per_launch / 1e9, "hbm_frac": nbytes / per_launch / 1e9 / float(pk["hbm_gbs"])}
     line = {"metric": "(x)(+) pairs/s (%s)" % key, "value": value, "unit": "pairs/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,

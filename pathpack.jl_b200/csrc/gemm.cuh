@@ -18,6 +18,8 @@
 // and take k in increasing order, which for PlusProd is the order of the reference's sgemx2!.
 #pragma once
 
+#include <type_traits>
+
 #include "semiring.cuh"
 
 namespace pp {
@@ -234,12 +236,107 @@ __global__ void __launch_bounds__(256, 1)
     }
 }
 
+// PlusProd Float64: C <- C + A B on the FP64 tensor cores (DMMA, mma.sync m8n8k4 f64; tcgen05 has no f64 kind).
+// A CTA of 4 warps computes a 64 x 64 tile of C, each warp 32 x 32 as 4 x 4 fragments of 8 x 8, over 16-deep
+// k-chunks of A (As[k][m]) and B (Bs[k][n]) staged in shared memory, double-buffered.  Fragments (PTX m8n8k4
+// .row.col): lane l holds A(l / 4, l % 4), B(l % 4, l / 4) and C(l / 4, 2 (l % 4) + {0, 1}).  Out-of-range
+// operands read as 0.  The products of one instruction are summed in the tensor core's order, so results agree
+// with the sequential sgemx2! within rounding (the PlusProd tolerance), not bit for bit.
+constexpr int DM_BM = 64, DM_BN = 64, DM_BK = 16, DM_LD = 64 + 2;  // padded rows of the staged chunks
+
+__device__ __forceinline__ void dmma_8x8x4(double &d0, double &d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
+
+template <typename T>  // T = double (a template, so that only the translation unit that launches it defines it)
+__global__ void __launch_bounds__(128) gemm_dmma_kernel(int M, int N, int K, T *__restrict__ C, int64_t ldc,
+                                                        const T *__restrict__ A, int64_t lda,
+                                                        const T *__restrict__ B, int64_t ldb) {
+    static_assert(std::is_same<T, double>::value, "DMMA f64");
+    __shared__ __align__(16) double As[2][DM_BK][DM_LD];
+    __shared__ __align__(16) double Bs[2][DM_BK][DM_LD];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int wm = (w & 1) * 32, wn = (w >> 1) * 32;  // the warp's 32 x 32 block of the tile
+    const int g = lane >> 2, q = lane & 3;
+    const int m0 = blockIdx.x * DM_BM, n0 = blockIdx.y * DM_BN;
+    double acc[4][4][2];
+#pragma unroll
+    for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+        for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int m = m0 + wm + mt * 8 + g, n = n0 + wn + nt * 8 + 2 * q + h;
+                acc[mt][nt][h] = (m < M && n < N) ? C[(int64_t)m + (int64_t)n * ldc] : 0.0;
+            }
+    // staging: A chunk 64 x 16 (rows m contiguous in memory), B chunk 16 x 64 (k contiguous); 8 each per thread
+    double ra[8], rb[8];
+    auto load = [&](int k0) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int idx = tid + 128 * e;          // A: m = idx % 64, k = idx / 64
+            const int m = m0 + (idx & 63), k = k0 + (idx >> 6);
+            ra[e] = (m < M && k < K) ? A[(int64_t)m + (int64_t)k * lda] : 0.0;
+            const int kb = k0 + (idx & 15), n = n0 + (idx >> 4);  // B: k = idx % 16, n = idx / 16
+            rb[e] = (kb < K && n < N) ? B[(int64_t)kb + (int64_t)n * ldb] : 0.0;
+        }
+    };
+    auto store = [&](int buf) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int idx = tid + 128 * e;
+            As[buf][idx >> 6][idx & 63] = ra[e];
+            Bs[buf][idx & 15][idx >> 4] = rb[e];
+        }
+    };
+    const int nk = (K + DM_BK - 1) / DM_BK;
+    if (nk > 0) {
+        load(0);
+        store(0);
+    }
+    __syncthreads();
+    for (int kt = 0; kt < nk; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < nk) load((kt + 1) * DM_BK);
+#pragma unroll
+        for (int ks = 0; ks < DM_BK; ks += 4) {
+            double af[4], bf[4];
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++) af[mt] = As[buf][ks + q][wm + mt * 8 + g];
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++) bf[nt] = Bs[buf][ks + q][wn + nt * 8 + g];
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++) dmma_8x8x4(acc[mt][nt][0], acc[mt][nt][1], af[mt], bf[nt]);
+        }
+        if (kt + 1 < nk) store(buf ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+        for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int m = m0 + wm + mt * 8 + g, n = n0 + wn + nt * 8 + 2 * q + h;
+                if (m < M && n < N) C[(int64_t)m + (int64_t)n * ldc] = acc[mt][nt][h];
+            }
+}
+
 // host launcher
 template <int SR, typename T>
 cudaError_t launch_gemm(int64_t M, int64_t N, int64_t K, T *C, int64_t ldc, const T *A, int64_t lda, const T *B,
                         int64_t ldb, cudaStream_t st) {
     using G = GemmKernel<SR, T>;
     if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+    if constexpr (SR == PLUSPROD && std::is_same<T, double>::value) {
+        dim3 grid((unsigned)((M + DM_BM - 1) / DM_BM), (unsigned)((N + DM_BN - 1) / DM_BN));
+        gemm_dmma_kernel<T><<<grid, 128, 0, st>>>((int)M, (int)N, (int)K, C, ldc, A, lda, B, ldb);
+        return cudaGetLastError();
+    }
     int dev = 0;
     cudaGetDevice(&dev);
     static bool attr[64] = {};

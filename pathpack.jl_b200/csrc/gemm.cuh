@@ -33,7 +33,7 @@ template <typename T>
 struct GemmCfg;
 template <>
 struct GemmCfg<float> {
-    static constexpr int TM = 8, TN = 8, BK = 16;
+    static constexpr int TM = 8, TN = 4, BK = 16;  // 128 registers: two CTAs (16 warps) per SM
 };
 template <>
 struct GemmCfg<int32_t> {
@@ -76,7 +76,7 @@ struct Vec<double, 2> {
 };
 
 template <int SR, typename T>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(256, sizeof(T) == 4 && GemmCfg<T>::TN == 4 ? 2 : 1)
     gemm_kernel(int M, int N, int K, T *__restrict__ C, int64_t ldc, const T *__restrict__ A, int64_t lda,
                 const T *__restrict__ B, int64_t ldb) {
     using G = GemmKernel<SR, T>;

@@ -57,7 +57,7 @@ struct Vec16<double> {
 };
 
 template <int SR, typename T, bool FWD, bool TRANS>
-__global__ void __launch_bounds__(256, 3) sweep_wide_kernel(const int2 *__restrict__ wl, int count, DevPlan P,
+__global__ void __launch_bounds__(256, sizeof(T) == 8 ? 2 : (FWD ? 4 : 3)) sweep_wide_kernel(const int2 *__restrict__ wl, int count, DevPlan P,
                                                          const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
                                                          int64_t ldx, int k, int unit, int *flags, int *next,
                                                          int *err) {

@@ -4,9 +4,9 @@
 // ordering and clique tree) and only its output crosses the C ABI (pp_set_structure).  This file produces the
 // same kind of output for callers without Julia (the Python host package, the tests and bench.py):
 //
-//   1. strongly connected components, by the reference's non-recursive Tarjan walk over the in-neighbours
-//      of each vertex (sccs!, src/CPU/utils.jl:18-70), so components come sources first and every arc
-//      between components goes from an earlier one to a later one;
+//   1. strongly connected components (Kosaraju's two passes), listed sources first so that every arc
+//      between components goes from an earlier one to a later one, as the reference's sccs!
+//      (src/CPU/utils.jl:18-70) lists them;
 //   2. per component (scliquetree, src/CPU/chordal_ssymbolic.jl:59-184): one front for components of one or
 //      two vertices, otherwise a fill-reducing ordering of the symmetrised component (nested dissection by
 //      breadth-first level structures, minimum degree inside the small pieces; CliqueTrees' default AMF is
@@ -38,69 +38,93 @@ struct Graph {  // compressed adjacency
     std::vector<i32> tgt;
 };
 
-// ---------------------------------------------------------------- SCCs (sccs!, src/CPU/utils.jl:18-70)
-// neighbors(v) are the rows of column v of A: the in-neighbours of v.  Returns the component pointers and
-// the vertices listed component by component.
+// ---------------------------------------------------------------- strongly connected components
+// Kosaraju's two depth-first passes, iterative (an explicit stack of (vertex, next arc)).  neighbors(v) are
+// the rows of column v of A: the in-neighbours of v.  Pass 1 searches along in-arcs and records vertices as
+// they finish; pass 2 searches along out-arcs, starting from the unvisited vertex that finished last, and
+// each of its search trees is one component.  Pass 2 meets the components sinks first (a sink component's
+// search cannot leave it), so reversing its list puts them sources first: every arc between two components
+// then goes from an earlier one to a later one, the order the blocked solves need (the property the
+// reference's sccs!, src/CPU/utils.jl:18-70, guarantees; any such order gives the same star).
+// Returns the component pointers and the vertices listed component by component.
 void sccs(const Graph &g, std::vector<i64> &cptr, std::vector<i32> &ctgt) {
-    const i64 n = g.n, np1 = n + 1;
-    // 1-based restatement of the reference walk
-    std::vector<i64> low(n + 1, 0), arc(n + 2, 0), ptr(n + 2, 0), tgt(n + 1, 0);
-    i64 r = np1, c = 0, i = 1;
-    for (i64 u = 1; u <= n; u++) {
-        if (low[u] != 0) continue;
-        r -= 1;
-        tgt[r] = u;
-        i64 l = low[u] = np1 - r;
-        i64 d = 1;
-        ptr[np1 - d] = r;
-        i64 v = u, p = g.ptr[v - 1], pstop = g.ptr[v];
-        while (true) {
-            if (p < pstop) {
-                const i64 w = (i64)g.tgt[p] + 1;
-                p += 1;
-                const i64 m = low[w];
-                if (m == 0) {
-                    low[v] = l;
-                    arc[d] = p;
-                    r -= 1;
-                    tgt[r] = w;
-                    l = low[w] = np1 - r;
-                    d += 1;
-                    ptr[np1 - d] = r;
-                    v = w;
-                    p = g.ptr[v - 1];
-                    pstop = g.ptr[v];
-                } else {
-                    l = std::min(l, m);
+    const i32 n = g.n;
+    const i64 m = g.ptr[n];
+    // out-arcs: the transpose of the in-neighbour lists
+    std::vector<i64> optr(n + 1, 0);
+    for (i64 p = 0; p < m; p++) optr[(i64)g.tgt[p] + 1]++;
+    for (i32 v = 0; v < n; v++) optr[v + 1] += optr[v];
+    std::vector<i32> otgt(std::max<i64>(m, 1));
+    {
+        std::vector<i64> next(optr.begin(), optr.end() - 1);
+        for (i32 v = 0; v < n; v++)
+            for (i64 p = g.ptr[v]; p < g.ptr[v + 1]; p++) otgt[next[g.tgt[p]]++] = v;
+    }
+    std::vector<std::pair<i32, i64>> stack;
+    stack.reserve(64);
+    // pass 1: finishing order of a search along in-arcs
+    std::vector<i32> finished;
+    finished.reserve(n);
+    std::vector<char> seen(n, 0);
+    for (i32 s = 0; s < n; s++) {
+        if (seen[s]) continue;
+        seen[s] = 1;
+        stack.push_back({s, g.ptr[s]});
+        while (!stack.empty()) {
+            const i32 v = stack.back().first;
+            const i64 p = stack.back().second;
+            if (p < g.ptr[v + 1]) {
+                stack.back().second = p + 1;
+                const i32 w = g.tgt[p];
+                if (!seen[w]) {
+                    seen[w] = 1;
+                    stack.push_back({w, g.ptr[w]});
                 }
             } else {
-                const i64 rstop = ptr[np1 - d];
-                if (l + rstop == np1) {
-                    c += 1;
-                    ptr[c] = i;
-                    for (i64 j = r; j <= rstop; j++) {
-                        const i64 w = tgt[i] = tgt[j];
-                        low[w] = np1;
-                        i += 1;
-                    }
-                    r = rstop + 1;
-                } else {
-                    low[v] = l;
-                }
-                d -= 1;
-                if (d == 0) break;
-                v = tgt[ptr[np1 - d]];
-                l = std::min(low[v], l);
-                p = arc[d];
-                pstop = g.ptr[v];
+                finished.push_back(v);
+                stack.pop_back();
             }
         }
     }
-    ptr[c + 1] = i;
-    cptr.assign(c + 1, 0);
-    for (i64 k = 0; k <= c; k++) cptr[k] = ptr[k + 1] - 1;
+    // pass 2: search trees along out-arcs, latest finisher first; comp[v] = index of v's tree
+    std::vector<i32> comp(n, -1), order;
+    order.reserve(n);
+    std::vector<i64> tree_start;
+    for (i32 t = n - 1; t >= 0; t--) {
+        const i32 s = finished[t];
+        if (comp[s] >= 0) continue;
+        const i32 c = (i32)tree_start.size();
+        tree_start.push_back((i64)order.size());
+        comp[s] = c;
+        order.push_back(s);
+        stack.push_back({s, optr[s]});
+        while (!stack.empty()) {
+            const i32 v = stack.back().first;
+            const i64 p = stack.back().second;
+            if (p < optr[v + 1]) {
+                stack.back().second = p + 1;
+                const i32 w = otgt[p];
+                if (comp[w] < 0) {
+                    comp[w] = c;
+                    order.push_back(w);
+                    stack.push_back({w, optr[w]});
+                }
+            } else {
+                stack.pop_back();
+            }
+        }
+    }
+    tree_start.push_back((i64)order.size());
+    // the trees in reverse: sources first
+    const i64 nc = (i64)tree_start.size() - 1;
+    cptr.assign(nc + 1, 0);
     ctgt.assign(n, 0);
-    for (i64 k = 0; k < n; k++) ctgt[k] = (i32)(tgt[k + 1] - 1);
+    i64 at = 0;
+    for (i64 c = nc - 1; c >= 0; c--) {
+        cptr[nc - 1 - c] = at;
+        for (i64 q = tree_start[c]; q < tree_start[c + 1]; q++) ctgt[at++] = order[q];
+    }
+    cptr[nc] = at;
 }
 
 // ---------------------------------------------------------------- ordering of one component

@@ -103,3 +103,27 @@ def test_readme_graph_components():
     S = pp.ssymbolic(5, A.indptr.astype(np.int64), A.indices.astype(np.int64))
     assert S.nB == 2 and sorted(np.diff(S.Bptr).tolist()) == [1, 4]
     assert S.perm[S.Bptr[1]] == 4 or S.perm[0] == 4
+
+
+@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.parametrize("density", [0.004, 0.012, 0.03])
+def test_components_match_scipy(seed, density):
+    """The components are exactly scipy's strongly connected components (same partition of the vertices),
+    listed sources first: no arc goes from a later component to an earlier one."""
+    rng = np.random.default_rng(seed)
+    n = 300
+    A = sp.random(n, n, density=density, random_state=rng, format="csc")
+    A.setdiag(0)
+    A.eliminate_zeros()
+    A.sort_indices()
+    cp, rv = A.indptr.astype(np.int64), A.indices.astype(np.int64)
+    S = pp.ssymbolic(n, cp, rv)
+    ncomp, lab = connected_components(A, directed=True, connection="strong")
+    assert S.nB == ncomp
+    comp_of_pos = np.repeat(np.arange(S.nB), np.diff(S.Bptr))
+    ours = comp_of_pos[S.invp]  # component of each original vertex
+    # the same partition: a bijection between the two labellings
+    pairs = set(zip(ours.tolist(), lab.tolist()))
+    assert len(pairs) == ncomp
+    i, j = arcs_in_positions(n, cp, rv, S)
+    assert np.all(comp_of_pos[i] <= comp_of_pos[j]), "an arc goes back to an earlier component"

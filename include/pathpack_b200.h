@@ -136,18 +136,20 @@ int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols,
 int32_t pp_sync(pp_handle *h);
 
 /* ---- lmul! allocating nothing (no counterpart in the reference) ----
-   pp_lmul_static is pp_lmul for device-resident B (n x k, leading dimension ldb) that allocates nothing:
-   no device memory, no host staging, no profiler events.  It is for callers that must not allocate while
-   solving, such as a serving process that reserves all device memory at startup (its pool leaves cudaMalloc
-   nothing to give, and a cudaMalloc may synchronise the device and stall the other streams' work).  Its
-   scratch, the right-hand sides in the device layout and the sweep counters, is one static device array of
-   PP_STATIC_SCRATCH_BYTES per device inside the library's device image: n * (k rounded up to 4) * element
-   size, rounded up to 256 bytes, plus 4 * (ceil(k / 32) * nfronts + 16) bytes must fit, else the call
-   returns PP_EINVAL and touches nothing.  Nothing in the array has to start at zero: the counters are reset
-   by the solve itself.  The first call on a device looks up the array's address (setup); make it before any
-   stream capture.  All calls on one device share the array, so two calls that overlap in time (from
-   different host threads, on any handles) race on it and return wrong results; each call returns only after
-   its work on the device is complete. */
+   pp_lmul_static is pp_lmul for device-resident B (n x k, leading dimension ldb, on the handle's device) that
+   allocates nothing: no device memory, no host staging, no profiler events.  It is for callers that must not
+   allocate while solving, such as a serving process that reserves all device memory at startup (its pool
+   leaves cudaMalloc nothing to give, and a cudaMalloc may synchronise the device and stall the other streams'
+   work).  Its scratch, the right-hand sides in the device layout and the sweep counters, is one static device
+   array of PP_STATIC_SCRATCH_BYTES per device inside the library's device image:
+       n * (k rounded up to 4) * element size, rounded up to 256 bytes, plus 4 * (3 * ceil(k / 32) * nfronts + 16)
+   bytes must fit, else the call returns PP_EINVAL and touches nothing.  Nothing in the array has to start at
+   zero: the counters are reset by the solve itself.  Each call looks up the array's address on the handle's
+   device.  The first call on a device is also where the CUDA runtime (lazy module loading, the CUDA 12
+   default) loads the library's device code on that device and so reserves the array's 32 MiB: make that first
+   call before the caller reserves its memory pool, and before any stream capture.  All calls on one device
+   share the array, so two calls that overlap in time (from different host threads, on any handles) race on it
+   and return wrong results.  The call is synchronous: it returns after its work on the device is complete. */
 #define PP_STATIC_SCRATCH_BYTES (32u << 20)
 int32_t pp_lmul_static(pp_handle *h, void *B, int64_t ldb, int64_t k);
 

@@ -206,7 +206,8 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
 
 extern "C" int32_t pp_destroy(pp_handle *h) {
     if (!h) return PP_OK;
-    cudaSetDevice(h->device);
+    // best effort: the handle is released whatever the device's state
+    if (cudaSetDevice(h->device) != cudaSuccess) cudaGetLastError();
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
@@ -311,7 +312,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
     if (n > 0 && (!Rptr || !Sptr || !Bptr || !Fptr || !Nptr || !perm))
         return fail(h, PP_EINVAL, "pp_set_structure: null array");
     if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_set_structure: base must be 0 or 1");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_set_structure");
     if (h->factor_stream) cudaStreamSynchronize(h->factor_stream);  // nothing in flight reads the old plan
     h->have_structure = h->have_values = h->factored = false;
     h->nnz_assembled = -1;
@@ -991,7 +992,7 @@ extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, co
     if (!h) return fail(nullptr, PP_EINVAL, "pp_assemble: null handle");
     if (!h->have_structure) return fail(h, PP_ESTATE, "pp_assemble: no structure (call pp_set_structure first)");
     if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_assemble: base must be 0 or 1");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_assemble");
     CK(h, cudaStreamSynchronize(h->factor_stream), "pp_assemble");  // buffers may be reallocated below
     int32_t r = set_semiring(h, semiring, dtype, "pp_assemble");
     if (r != PP_OK) return r;
@@ -1053,7 +1054,7 @@ extern "C" int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t whe
     if (where != PP_HOST && where != PP_DEVICE) return fail(h, PP_EINVAL, "pp_update_values: where");
     const int64_t nnz = h->nnz_assembled;
     if (nnz > 0 && !nzval) return fail(h, PP_EINVAL, "pp_update_values: null nzval");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_update_values");
     const size_t es = h->ops->esize;
     if (where == PP_HOST && h->sr == PP_MINPLUS && h->dt == PP_I32) {
         const int32_t *a = static_cast<const int32_t *>(nzval);
@@ -1080,7 +1081,7 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
                                  const void *UD, const void *UL, const void *Nval) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_set_values: null handle");
     if (!h->have_structure) return fail(h, PP_ESTATE, "pp_set_values: no structure");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_set_values");
     CK(h, cudaStreamSynchronize(h->factor_stream), "pp_set_values");
     int32_t r = set_semiring(h, semiring, dtype, "pp_set_values");
     if (r != PP_OK) return r;
@@ -1131,7 +1132,7 @@ static int32_t settle(pp_handle *h, const char *who) {
 extern "C" int32_t pp_factor(pp_handle *h) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_factor: null handle");
     if (!h->have_values) return fail(h, PP_ESTATE, "pp_factor: no values (call pp_assemble or pp_set_values)");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_factor");
     const size_t wbytes = h->ops->esize * std::max<int64_t>(h->hp.ws_elems, 1);
     if (wbytes > h->W.bytes) {
         CK(h, cudaStreamSynchronize(h->factor_stream), "pp_factor");
@@ -1156,7 +1157,7 @@ extern "C" int32_t pp_factor(pp_handle *h) {
 extern "C" int32_t pp_get_factor(pp_handle *h, void *LD, void *LL, void *UD, void *UL) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_get_factor: null handle");
     if (!h->have_values) return fail(h, PP_ESTATE, "pp_get_factor: no values");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_get_factor");
     const size_t es = h->ops->esize;
     cudaStream_t st = h->stream;
     if (LD && h->nD) CK(h, cudaMemcpyAsync(LD, h->LD.p, es * h->nD, cudaMemcpyDeviceToHost, st), "pp_get_factor");
@@ -1204,7 +1205,7 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
     }
     if (!B) return fail(h, PP_EINVAL, "%s: null B", who);
     if (left ? ldb < n : ldb < k) return fail(h, PP_EINVAL, "%s: leading dimension %lld", who, (long long)ldb);
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), who);
     const size_t es = h->ops->esize;
     const int64_t ldx = (k + 3) & ~(int64_t)3;
     const size_t xbytes = es * (size_t)n * ldx;
@@ -1293,6 +1294,8 @@ int32_t pp_internal_lmul_scratch(pp_handle *h, void *B, int64_t ldb, int64_t k, 
     CK(h, cudaPointerGetAttributes(&pa, B), who);
     if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
         return fail(h, PP_EINVAL, "%s: B must be device memory", who);
+    if (pa.type == cudaMemoryTypeDevice && pa.device != h->device)
+        return fail(h, PP_EINVAL, "%s: B is on device %d, the handle on device %d", who, pa.device, h->device);
     const size_t es = h->ops->esize;
     const int64_t ldx = (k + 3) & ~(int64_t)3;
     const size_t xbytes = ((es * (size_t)n * ldx) + 255) & ~(size_t)255;
@@ -1359,7 +1362,7 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
         return PP_OK;
     }
     if (!C || ldc < n) return fail(h, PP_EINVAL, "pp_star: C / ldc");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_star");
     const size_t es = h->ops->esize;
     // panel width, a multiple of 32 columns: wide panels give the sweeps of the top fronts, whose 64-row blocks
     // form dependency chains, many independent column tiles to run beside each chain (about 2 GB of right-hand
@@ -1449,7 +1452,7 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
 
 extern "C" int32_t pp_sync(pp_handle *h) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_sync: null handle");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_sync");
     const int32_t r = settle(h, "pp_sync");
     if (r != PP_OK) return r;
     ok(h);
@@ -1458,7 +1461,7 @@ extern "C" int32_t pp_sync(pp_handle *h) {
 
 extern "C" int32_t pp_get_stats(pp_handle *h, pp_stats *s) {
     if (!h || !s) return fail(h, PP_EINVAL, "pp_get_stats: null argument");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_get_stats");
     const int32_t r = settle(h, "pp_get_stats");
     if (r != PP_OK) return r;
     int64_t bytes = 0;
@@ -1476,7 +1479,7 @@ extern "C" int32_t pp_get_stats(pp_handle *h, pp_stats *s) {
 
 extern "C" int32_t pp_set_profile(pp_handle *h, int32_t on) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_set_profile: null handle");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_set_profile");
     const int32_t r = settle(h, "pp_set_profile");
     if (r != PP_OK) return r;
     h->prof.reset();
@@ -1487,7 +1490,7 @@ extern "C" int32_t pp_set_profile(pp_handle *h, int32_t on) {
 
 extern "C" int32_t pp_get_profile(pp_handle *h, pp_kernel_class *out, int32_t max, int32_t *count) {
     if (!h || (!out && max > 0)) return fail(h, PP_EINVAL, "pp_get_profile: null argument");
-    cudaSetDevice(h->device);
+    CK(h, cudaSetDevice(h->device), "pp_get_profile");
     const int32_t r = settle(h, "pp_get_profile");
     if (r != PP_OK) return r;
     int c = 0;

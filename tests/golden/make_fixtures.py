@@ -130,4 +130,6 @@ def main(root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_fixtures.py <path of a PATHPACK.jl checkout>")
+    main(sys.argv[1])

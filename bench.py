@@ -58,16 +58,30 @@ def peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
-def profiled_traffic(kernel):
-    """DRAM bytes per launch of the kernel (dram__bytes_read.sum + dram__bytes_write.sum) from the committed ncu
-    summary profiles/<kernel>_config2.md, or None."""
-    path = os.path.join(REPO, "profiles", "%s_config2.md" % kernel.split("(")[0])
-    if not os.path.exists(path):
+def ncu_traffic(path, kernel):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, averaged over the captured launches)
+    of the kernel in an ncu raw CSV export (`ncu -i <rep> --page raw --csv`) given with --traffic-csv, or None
+    when no export is given."""
+    if not path or not os.path.exists(path):
         return None
-    for line in open(path):
-        if line.startswith("traffic_bytes_per_launch:"):
-            return float(line.split(":")[1])
-    return None
+    import csv
+
+    rows = list(csv.reader(open(path)))
+    if len(rows) < 3:
+        return None
+    head = rows[0]
+    try:
+        kn, rd, wr = head.index("Kernel Name"), head.index("dram__bytes_read.sum"), head.index("dram__bytes_write.sum")
+    except ValueError:
+        return None
+    unit = rows[1]
+    scale = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    vals = []
+    for r in rows[2:]:
+        if len(r) > max(kn, rd, wr) and kernel.split("(")[0] in r[kn]:
+            f = lambda i: float(r[i].replace(",", "")) * scale.get(unit[i], 1.0)
+            vals.append(f(rd) + f(wr))
+    return float(np.mean(vals)) if vals else None
 
 
 # ----------------------------------------------------------------------------------------------- workloads
@@ -285,23 +299,31 @@ def run_ours(args, rank, world, local):
         Bw.copy_(B0)
     pp.lmul_(F, Bw.T)
     launches_per_step += F.stats()["kernel_launches"]
-    for _ in range(args.warmup):
-        step()
-    F.sync()
-    torch.cuda.synchronize(dev)
-    if dist:
-        tdist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     gidx = int(vis.split(",")[dev]) if vis else dev
+    # the clock sampler starts before the warm-up, so that its start (NVML initialisation) is not inside the
+    # timed region; every step is bracketed by its own pair of events on the library's stream and the host
+    # time to enqueue it is recorded, so that a stall shows as one slow step or as host-bound enqueueing
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    enqueue_ms = []
     with Clocks(gidx) as clk:
-        torch.cuda.synchronize(dev)
-        e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(args.warmup):
             step()
-        e1.record(stream)
+        F.sync()
+        torch.cuda.synchronize(dev)
+        if dist:
+            tdist.barrier()
+        torch.cuda.synchronize(dev)
+        evs[0].record(stream)
+        for i in range(args.steps):
+            t0 = time.perf_counter()
+            step()
+            evs[i + 1].record(stream)
+            enqueue_ms.append(1e3 * (time.perf_counter() - t0))
         torch.cuda.synchronize(dev)
         F.sync()  # reports a device error of the timed steps
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    e0, e1 = evs[0], evs[-1]
     launches = launches_per_step * args.steps
     ms = e0.elapsed_time(e1)
     clocks = clk.summary()
@@ -346,11 +368,23 @@ def run_ours(args, rank, world, local):
     top = max(prof.items(), key=lambda kv: kv[1]["ms"])
     name, d = top
     per_launch_s = d["ms"] / 1e3 / d["launches"]
-    achieved = d["bytes"] / d["launches"] / per_launch_s / 1e9
-    roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": float(pk["hbm_gbs"]), "unit": "GB/s",
-            "frac": achieved / float(pk["hbm_gbs"]), "traffic": profiled_traffic(name), "peak_source": src,
-            "launches_per_step": d["launches"] / args.steps, "ms_per_step": d["ms"] / args.steps,
-            "pairs_per_s": d["pairs"] / (d["ms"] / 1e3) if d["ms"] > 0 else 0.0}
+    # the dominant kernel (the top factorization) is bound by its ALU issue rate along the tree's critical
+    # path, not by HBM: its fraction is (x)(+) pairs per second against the nominal Float64 ALU pair peak
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    apeak = alu_peak("MinPlus", np.float64, sms, float(pk.get("sm_max_mhz", 1965.0)))
+    achieved = d["pairs"] / d["launches"] / per_launch_s
+    gbs = d["bytes"] / d["launches"] / per_launch_s / 1e9
+    roof = {"kernel": name, "bound": "alu", "achieved": achieved, "peak": apeak, "unit": "pairs/s",
+            "frac": achieved / apeak,
+            "peak_source": "nominal Float64 ALU issue rate: SMs x max SM clock (MEASURED_PEAKS sm_max_mhz) x 64 "
+                           "lanes / 2 instructions per (x)(+) pair",
+            "traffic": ncu_traffic(args.traffic_csv, name),
+            "traffic_source": args.traffic_csv or "none given (--traffic-csv); see profiles/ for the ncu capture",
+            "hbm_achieved_GB_per_s": gbs, "hbm_peak_GB_per_s": float(pk["hbm_gbs"]),
+            "hbm_frac": gbs / float(pk["hbm_gbs"]), "hbm_peak_source": src,
+            "algorithmic_bytes_per_launch": d["bytes"] / d["launches"],
+            "pairs_per_launch": d["pairs"] / d["launches"],
+            "launches_per_step": d["launches"] / args.steps, "ms_per_step": d["ms"] / args.steps}
     kernels = {k_: {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps,
                     "GB_per_s": v["bytes"] / (v["ms"] / 1e3) / 1e9 if v["ms"] > 0 else 0.0,
                     "Tpairs_per_s": v["pairs"] / (v["ms"] / 1e3) / 1e12 if v["ms"] > 0 else 0.0}
@@ -391,6 +425,10 @@ def run_ours(args, rank, world, local):
                         "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * e2e_t / args.steps,
                         "step_ms_min": min(e2e_steps), "step_ms_median": float(np.median(e2e_steps)),
                         "clock": "host wall clock per step (perf_counter), summed over the K steps"},
+                "step_ms": {"median": float(np.median(step_ms)), "min": min(step_ms), "max": max(step_ms),
+                            "clock": "CUDA events on the library's stream around each timed step"},
+                "enqueue_ms": {"median": float(np.median(enqueue_ms)), "max": max(enqueue_ms),
+                               "clock": "host perf_counter around enqueueing each timed step"},
                 "gpu_launches": launches, "roofline": roof, "kernels": kernels, "clocks": clocks,
                 "cpu_baseline": cpu, "mstar": mstar}
         print(json.dumps(line), flush=True)
@@ -434,7 +472,7 @@ def _roofline_alu(prof, steps, semiring, dtype, pk):
     peak = alu_peak(semiring, dtype, sms, float(pk.get("sm_max_mhz", 1965.0)))
     achieved = d["pairs"] / (d["ms"] / 1e3) if d["ms"] > 0 else 0.0
     return {"kernel": name, "bound": "alu", "achieved": achieved, "peak": peak, "unit": "pairs/s",
-            "frac": achieved / peak, "traffic": profiled_traffic(name), "peak_source": "nominal ALU issue rate "
+            "frac": achieved / peak, "traffic": None, "peak_source": "nominal ALU issue rate "
             "(SMs x max SM clock x lanes / instructions per pair)", "ms_per_step": d["ms"] / steps,
             "launches_per_step": d["launches"] / steps,
             "GB_per_s": d["bytes"] / (d["ms"] / 1e3) / 1e9 if d["ms"] > 0 else 0.0}
@@ -826,6 +864,8 @@ def main():
                          "over the ranks) or a config-5 kernel")
     ap.add_argument("--no-e2e", action="store_true", help="star workloads: skip the host-output e2e calls")
     ap.add_argument("--no-mstar", action="store_true", help="config2: skip the config-4 mstar sub-measurement")
+    ap.add_argument("--traffic-csv", default=None,
+                    help="an ncu raw CSV export (ncu -i <rep> --page raw --csv) of this build: fills roofline.traffic")
     ap.add_argument("--columns", type=int, default=None,
                     help="star workloads: compute only the first C columns of each rank's panel (a smaller case "
                          "of the same kernels, for profiling captures; the line then covers those columns)")

@@ -127,6 +127,12 @@ int32_t pp_lmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where);
 /* B <- B A*: rmul!(B, F), src/CPU/abstract_slu.jl:142-145.  B is k x n, column-major, leading dimension ldb. */
 int32_t pp_rmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where);
 
+/* The transposed factor: B <- (A*)^T B = (A^T)* B, lmul!(transpose(F), B), and B <- B (A*)^T,
+   rmul!(B, transpose(F)); src/CPU/abstract_slu.jl:131-145 with unwrap(F) giving trans = Val(:T), which
+   sgetrs! (src/CPU/chordal/sgetrs.jl:88-110) runs as U* first, then L*.  Layouts as pp_lmul / pp_rmul. */
+int32_t pp_lmul_t(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where);
+int32_t pp_rmul_t(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where);
+
 /* Columns col0 .. col0+ncols-1 of the star A* (original labels) into C (n x ncols, column-major, leading
    dimension ldc).  ncols = n and col0 = 0 is Matrix(F), src/CPU/abstract_slu.jl:10-14; column panels let
    several GPUs share one star. */

@@ -1192,8 +1192,13 @@ static int32_t ensure_sync(pp_handle *h, int64_t k) {
     return PP_OK;
 }
 
-// lmul! / rmul! on the device layout X[position][rhs]
-static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where, int left, const char *who) {
+// lmul! / rmul! on the device layout X[position][rhs].  `left` selects the caller's layout (B n x k for
+// lmul!, k x n for rmul!), `trans` the transposed factor: lmul!(transpose(F), B) = (rmul!(B^T, F))^T and
+// rmul!(B, transpose(F)) = (lmul!(F, B^T))^T for the commutative (x) of every semiring here, so a transposed
+// solve runs the other direction's sweeps (U* forward then L* backward for lmul!, src/CPU/chordal/sgetrs.jl:
+// 88-110 with trans = :T) on this layout.
+static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where, int left, int trans,
+                         const char *who) {
     if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
     if (!h->factored) return fail(h, PP_ESTATE, "%s: no factorization (call pp_factor)", who);
     const int n = h->hp.n;
@@ -1240,7 +1245,7 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
     else
         CK(h, h->ops->cols_in(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
     h->prof.end(pi, st, 2.0 * n * k, 0);
-    CK(h, h->ops->solve(h->hp, values_of(h), left, h->X.p, ldx, (int)k, st, &nl), who);
+    CK(h, h->ops->solve(h->hp, values_of(h), trans ? !left : left, h->X.p, ldx, (int)k, st, &nl), who);
     pi = h->prof.begin(K_PERMUTE, st);
     if (left)
         CK(h, h->ops->rows_out(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
@@ -1264,7 +1269,11 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
 }
 
 extern "C" int32_t pp_lmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where) {
-    return run_solve(h, B, ldb, k, where, 1, "pp_lmul");
+    return run_solve(h, B, ldb, k, where, 1, 0, "pp_lmul");
+}
+
+extern "C" int32_t pp_lmul_t(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where) {
+    return run_solve(h, B, ldb, k, where, 1, 1, "pp_lmul_t");
 }
 
 // lmul! on device-resident B with the caller's scratch instead of the handle's: the right-hand-side
@@ -1347,7 +1356,11 @@ size_t pp_internal_lmul_scratch_bytes(const pp_handle *h, int64_t k) {
 }
 
 extern "C" int32_t pp_rmul(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where) {
-    return run_solve(h, B, ldb, k, where, 0, "pp_rmul");
+    return run_solve(h, B, ldb, k, where, 0, 0, "pp_rmul");
+}
+
+extern "C" int32_t pp_rmul_t(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where) {
+    return run_solve(h, B, ldb, k, where, 0, 1, "pp_rmul_t");
 }
 
 extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where) {

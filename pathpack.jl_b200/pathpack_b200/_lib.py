@@ -52,6 +52,8 @@ SIGNATURES = {
     "pp_get_factor": (C.c_int32, [_P, _P, _P, _P, _P]),
     "pp_lmul": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int32]),
     "pp_rmul": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int32]),
+    "pp_lmul_t": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int32]),
+    "pp_rmul_t": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int32]),
     "pp_lmul_static": (C.c_int32, [_P, _P, C.c_int64, C.c_int64]),
     "pp_star": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int64, C.c_int32]),
     "pp_sync": (C.c_int32, [_P]),

@@ -162,9 +162,10 @@ class B200SLU:
         check(lib().pp_lmul_static(self._h, vptr(B), ld, k), self._h)
         return B
 
-    def _solve(self, B, left, sync=True):
+    def _solve(self, B, left, sync=True, trans=False):
         n = self.S.n
-        fn = lib().pp_lmul if left else lib().pp_rmul
+        L = lib()
+        fn = (L.pp_lmul_t if left else L.pp_rmul_t) if trans else (L.pp_lmul if left else L.pp_rmul)
         if hasattr(B, "data_ptr"):  # a CUDA torch tensor, used in place
             if B.dtype.itemsize != self.dtype.itemsize or not B.is_cuda:
                 raise TypeError("B must be a CUDA tensor of the factor's element type")
@@ -210,6 +211,26 @@ class B200SLU:
         return out
 
 
+class TransposedSLU:
+    """transpose(F): the factorization of (A*)^T = (A^T)* on the same device data (the reference's
+    TransposeFactorization, which lmul! / rmul! unwrap to trans = Val(:T), src/CPU/abstract_slu.jl:131-145)."""
+
+    def __init__(self, F):
+        self.parent = F
+
+    @property
+    def shape(self):
+        return self.parent.shape
+
+    def _solve(self, B, left, sync=True):
+        return self.parent._solve(B, left, sync, trans=True)
+
+
+def transpose(F):
+    """transpose(F) for lmul_(transpose(F), B) = (A*)^T B and rmul_(B, transpose(F)) = B (A*)^T."""
+    return F.parent if isinstance(F, TransposedSLU) else TransposedSLU(F)
+
+
 def mlu(s, A, *, dtype=None, structure=None, device=0, method="nd"):
     """F = mlu(s, A): symbolic analysis (host), assembly and factorization of the star on the GPU."""
     n, cp, rv, nz = _csc(A, dtype)
@@ -226,12 +247,12 @@ def lu_(F):
 
 
 def lmul_(F, B):
-    """lmul!(F, B): B <- A* B, the least solution of X = A X (+) B."""
+    """lmul!(F, B): B <- A* B, the least solution of X = A X (+) B (F may be transpose(F))."""
     return F._solve(B, True)
 
 
 def rmul_(B, F):
-    """rmul!(B, F): B <- B A*, the least solution of X = X A (+) B."""
+    """rmul!(B, F): B <- B A*, the least solution of X = X A (+) B (F may be transpose(F))."""
     return F._solve(B, False)
 
 

@@ -282,23 +282,23 @@ def run_ours(args, rank, world, local):
     B0 = torch.from_numpy(np.ascontiguousarray(w["B"].T)).to(f"cuda:{dev}")  # (k, n): column-major n x k
     Bw = torch.empty_like(B0)
 
-    def step():
-        # everything is enqueued on the library's stream: no host synchronisation inside the step
+    def step_calls():
+        # the step as separate C-ABI calls, everything enqueued on the library's stream (no host wait)
         F.update_values(nz_d)  # 5 fills + the assembly kernel
         F.factor(sync=False)
         with torch.cuda.stream(stream):
             Bw.copy_(B0)
         F._solve(Bw.T, True, sync=False)
 
-    # the library's kernel launches of one step (the same every step): factorization + solve + 6 for the
-    # re-assembly (stats() waits, so it is read outside the timed region)
-    F.update_values(nz_d)
-    F.factor()
-    launches_per_step = 6 + F.stats()["kernel_launches"]
-    with torch.cuda.stream(stream):
-        Bw.copy_(B0)
-    pp.lmul_(F, Bw.T)
-    launches_per_step += F.stats()["kernel_launches"]
+    # the timed step: the same calls captured once as a CUDA graph by the library (pp_plan_lmul: re-assembly
+    # from the device weights, factorization, lmul! of B0 into Bw), so that one graph launch enqueues the
+    # whole step and the host's speed does not enter the device time
+    plan = F.plan_lmul(nz_d, B0.T, Bw.T)
+    launches_per_step = plan.launches
+
+    def step():
+        plan.launch()
+
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     gidx = int(vis.split(",")[dev]) if vis else dev
     # the clock sampler starts before the warm-up, so that its start (NVML initialisation) is not inside the
@@ -325,6 +325,17 @@ def run_ours(args, rank, world, local):
     step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
     e0, e1 = evs[0], evs[-1]
     launches = launches_per_step * args.steps
+    # for comparison: the same steps enqueued call by call (not part of the value)
+    for _ in range(2):
+        step_calls()
+    F.sync()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    for _ in range(args.steps):
+        step_calls()
+    c1.record(stream)
+    F.sync()
+    calls_ms = c0.elapsed_time(c1) / args.steps
     ms = e0.elapsed_time(e1)
     clocks = clk.summary()
     if dist:
@@ -360,7 +371,7 @@ def run_ours(args, rank, world, local):
     # roofline of the dominant kernel class, measured with CUDA events on the library's stream over K steps
     F.set_profile(True)
     for _ in range(args.steps):
-        step()
+        step_calls()  # the profiler brackets the library's launches with events: call by call, not the graph
     F.sync()
     prof = F.profile()
     F.set_profile(False)
@@ -426,12 +437,16 @@ def run_ours(args, rank, world, local):
                         "step_ms_min": min(e2e_steps), "step_ms_median": float(np.median(e2e_steps)),
                         "clock": "host wall clock per step (perf_counter), summed over the K steps"},
                 "step_ms": {"median": float(np.median(step_ms)), "min": min(step_ms), "max": max(step_ms),
-                            "clock": "CUDA events on the library's stream around each timed step"},
+                            "clock": "CUDA events on the library's stream around each timed step",
+                            "step": "one launch of the library's captured plan (pp_plan_lmul): re-assembly, "
+                                    "factorization, lmul!",
+                            "call_by_call_ms_per_step": calls_ms},
                 "enqueue_ms": {"median": float(np.median(enqueue_ms)), "max": max(enqueue_ms),
                                "clock": "host perf_counter around enqueueing each timed step"},
                 "gpu_launches": launches, "roofline": roof, "kernels": kernels, "clocks": clocks,
                 "cpu_baseline": cpu, "mstar": mstar}
         print(json.dumps(line), flush=True)
+    plan.close()
     F.close()
 
 

@@ -159,6 +159,26 @@ int32_t pp_sync(pp_handle *h);
 #define PP_STATIC_SCRATCH_BYTES (32u << 20)
 int32_t pp_lmul_static(pp_handle *h, void *B, int64_t ldb, int64_t k);
 
+/* ---- plans: refactorization with new weights and a solve, replayed as one CUDA graph ----
+   The reference's plans for repeated solves on one pattern (FactorPlan with graph replay,
+   ext/PATHPACKCUDAExt/chordal/sgetrf.jl:710-740; APSPPlan, ext/PATHPACKCUDAExt/api.jl:547-668).
+   pp_plan_lmul captures one step on the handle: pp_update_values from nzval (device memory, the order of
+   the last pp_assemble), pp_factor, and Bout <- A* Bin (lmul!, Bin and Bout n x k column-major device arrays
+   with leading dimension ldb; Bin may equal Bout).  It runs the step once uncaptured first, so that
+   everything the step needs is allocated and errors are reported, then records it into a CUDA graph.
+   pp_plan_launch enqueues one step on the handle's stream (pp_stream) and returns: write new weights into
+   nzval (or new right-hand sides into Bin) on that stream first and launch again.  A device error of a
+   launch is reported by the next call that waits (pp_sync).  The plan keeps the handle's buffers and the
+   three arrays' addresses: keep them alive and do not change the handle's structure or semiring while a
+   plan exists; pp_plan_destroy releases the graph (not the handle). */
+typedef struct pp_plan pp_plan;
+int32_t pp_plan_lmul(pp_handle *h, const void *nzval, const void *Bin, void *Bout, int64_t ldb, int64_t k,
+                     pp_plan **plan);
+int32_t pp_plan_launch(pp_plan *plan);
+/* kernels one launch of the plan runs */
+int32_t pp_plan_launches(const pp_plan *plan, int64_t *launches);
+int32_t pp_plan_destroy(pp_plan *plan);
+
 /* Counters of the handle (sizes, pair counts, device times of the last calls). */
 int32_t pp_get_stats(pp_handle *h, pp_stats *s);
 

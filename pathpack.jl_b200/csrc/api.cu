@@ -94,6 +94,9 @@ struct pp_handle {
     cudaEvent_t copy_ev = nullptr;
     cudaEvent_t panel_ready[2] = {}, panel_copied[2] = {};  // double-buffered star panels to host memory
     bool factor_pending = false, solve_pending = false;  // enqueued, times not yet read
+    // set while a plan (pp_plan_lmul) captures the handle's calls into a CUDA graph: no timing events, no
+    // profiler, and no wait for the previous factorization (a graph launch is ordered as a whole)
+    bool capturing = false;
     std::string err;
     bool have_structure = false, have_values = false, factored = false;
     int sr = -1, dt = -1;
@@ -942,6 +945,7 @@ static int32_t prepare_workspace(pp_handle *h) {
 }
 
 static int32_t need_memory(pp_handle *h, size_t bytes, const char *what) {
+    if (bytes == 0) return PP_OK;  // nothing to allocate: no driver query on the solve path
     size_t fr = 0, tot = 0;
     if (cudaMemGetInfo(&fr, &tot) == cudaSuccess && bytes > fr)
         return fail(h, PP_ENOMEM, "%s: needs %.3f GB of device memory, %.3f GB free", what, bytes / 1e9, fr / 1e9);
@@ -985,7 +989,14 @@ static Values values_of(pp_handle *h) {
 
 // The handle's stream waits for the top of the last factorization (a no-op if there was none): every call that
 // writes the factor's values or workspace orders itself after it this way.
-static cudaError_t after_factor(pp_handle *h) { return cudaStreamWaitEvent(h->stream, h->ev_factored, 0); }
+static cudaError_t after_factor(pp_handle *h) {
+    return h->capturing ? cudaSuccess : cudaStreamWaitEvent(h->stream, h->ev_factored, 0);
+}
+
+// timing events of the last factorization / solve (not while a plan is captured)
+static cudaError_t record_timing(pp_handle *h, cudaEvent_t ev, cudaStream_t st) {
+    return h->capturing ? cudaSuccess : cudaEventRecord(ev, st);
+}
 
 extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, const int64_t *colptr,
                                const int64_t *rowval, const void *nzval, int32_t base) {
@@ -1144,10 +1155,10 @@ extern "C" int32_t pp_factor(pp_handle *h) {
     cudaStream_t st = h->stream;
     int64_t nl = 0;
     CK(h, after_factor(h), "pp_factor");  // the previous top factorization reads the bottom's update matrices
-    CK(h, cudaEventRecord(h->fev0, st), "pp_factor");
+    CK(h, record_timing(h, h->fev0, st), "pp_factor");
     CK(h, h->ops->factor(h->hp, values_of(h), st, &nl), "pp_factor");
-    CK(h, cudaEventRecord(h->fev1, h->factor_stream), "pp_factor");  // the top of the tree ends there
-    h->factor_pending = true;
+    CK(h, record_timing(h, h->fev1, h->factor_stream), "pp_factor");  // the top of the tree ends there
+    h->factor_pending = !h->capturing;
     h->st.kernel_launches = nl;
     h->factored = true;
     ok(h);
@@ -1189,6 +1200,35 @@ static int32_t ensure_sync(pp_handle *h, int64_t k) {
     if (e != cudaSuccess) return cuda_fail(h, e, "sweep counters");
     h->hp.d_sync = h->d_sync.as<int>();
     h->hp.sync_cap = need;
+    return PP_OK;
+}
+
+// The device part of a solve on caller-layout device buffers: Bin permuted into X, the sweeps, X permuted
+// out into Bout (Bin == Bout in place; both leading dimension ldb).  X and the counters must be allocated.
+static int32_t enqueue_solve(pp_handle *h, const void *Bin, void *Bout, int64_t ldb, int64_t k, int left, int trans,
+                             const char *who) {
+    const int n = h->hp.n;
+    const int64_t ldx = (k + 3) & ~(int64_t)3;
+    cudaStream_t st = h->stream;
+    int64_t nl = 0;
+    CK(h, record_timing(h, h->ev0, st), who);
+    int pi = h->prof.begin(K_PERMUTE, st);
+    if (left)
+        CK(h, h->ops->rows_in(Bin, ldb, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    else
+        CK(h, h->ops->cols_in(Bin, ldb, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    h->prof.end(pi, st, 2.0 * n * k, 0);
+    CK(h, h->ops->solve(h->hp, values_of(h), trans ? !left : left, h->X.p, ldx, (int)k, st, &nl), who);
+    pi = h->prof.begin(K_PERMUTE, st);
+    if (left)
+        CK(h, h->ops->rows_out(Bout, ldb, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    else
+        CK(h, h->ops->cols_out(Bout, ldb, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
+    h->prof.end(pi, st, 2.0 * n * k, 0);
+    CK(h, record_timing(h, h->ev1, st), who);
+    h->solve_pending = !h->capturing;
+    h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)k;
+    h->st.kernel_launches = nl + 2;
     return PP_OK;
 }
 
@@ -1237,32 +1277,15 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
         CK(h, cudaEventRecord(h->copy_ev, h->copy_stream), who);
         CK(h, cudaStreamWaitEvent(st, h->copy_ev, 0), who);
     }
-    int64_t nl = 0;
-    CK(h, cudaEventRecord(h->ev0, st), who);
-    int pi = h->prof.begin(K_PERMUTE, st);
-    if (left)
-        CK(h, h->ops->rows_in(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
-    else
-        CK(h, h->ops->cols_in(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
-    h->prof.end(pi, st, 2.0 * n * k, 0);
-    CK(h, h->ops->solve(h->hp, values_of(h), trans ? !left : left, h->X.p, ldx, (int)k, st, &nl), who);
-    pi = h->prof.begin(K_PERMUTE, st);
-    if (left)
-        CK(h, h->ops->rows_out(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
-    else
-        CK(h, h->ops->cols_out(Bd, ldbd, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
-    h->prof.end(pi, st, 2.0 * n * k, 0);
-    CK(h, cudaEventRecord(h->ev1, st), who);
-    h->solve_pending = true;
-    h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)k;
-    h->st.kernel_launches = nl + 2;
+    const int32_t r = enqueue_solve(h, Bd, Bd, ldbd, k, left, trans, who);
+    if (r != PP_OK) return r;
     if (where == PP_HOST) {
         if (left)
             CK(h, cudaMemcpy2DAsync(B, es * ldb, Bd, es * n, es * n, k, cudaMemcpyDeviceToHost, st), who);
         else
             CK(h, cudaMemcpy2DAsync(B, es * ldb, Bd, es * k, es * k, n, cudaMemcpyDeviceToHost, st), who);
-        const int32_t r = settle(h, who);  // the result is in host memory when the call returns
-        if (r != PP_OK) return r;
+        const int32_t r2 = settle(h, who);  // the result is in host memory when the call returns
+        if (r2 != PP_OK) return r2;
     }
     ok(h);
     return PP_OK;
@@ -1519,6 +1542,114 @@ extern "C" int32_t pp_get_profile(pp_handle *h, pp_kernel_class *out, int32_t ma
     }
     if (count) *count = c;
     ok(h);
+    return PP_OK;
+}
+
+// ---------------------------------------------------------------- plans: refactor + solve as one CUDA graph
+
+struct pp_plan {
+    pp_handle *h = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int64_t launches = 0;
+};
+
+// The calls of one plan step, enqueued on the handle's stream: new weights from device memory re-assembled,
+// the factorization, and lmul! of Bin into Bout.
+static int32_t plan_step(pp_handle *h, const void *nzval, const void *Bin, void *Bout, int64_t ldb, int64_t k,
+                         int64_t *launches) {
+    int32_t r = pp_update_values(h, nzval, PP_DEVICE);
+    if (r != PP_OK) return r;
+    r = pp_factor(h);
+    if (r != PP_OK) return r;
+    int64_t nl = 6 + h->st.kernel_launches;  // the re-assembly's fills and kernel, then the factorization's
+    r = enqueue_solve(h, Bin, Bout, ldb, k, 1, 0, "pp_plan_lmul");
+    if (r != PP_OK) return r;
+    if (launches) *launches = nl + h->st.kernel_launches;
+    return PP_OK;
+}
+
+extern "C" int32_t pp_plan_lmul(pp_handle *h, const void *nzval, const void *Bin, void *Bout, int64_t ldb, int64_t k,
+                                pp_plan **out) {
+    const char *who = "pp_plan_lmul";
+    if (!out) return fail(h, PP_EINVAL, "%s: null output pointer", who);
+    *out = nullptr;
+    if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
+    if (!h->have_structure || h->nnz_assembled < 0)
+        return fail(h, PP_ESTATE, "%s: no pattern (call pp_assemble first)", who);
+    const int n = h->hp.n;
+    if (n == 0 || k <= 0 || k >= INT32_MAX / 2) return fail(h, PP_EINVAL, "%s: n = %d, k = %lld", who, n, (long long)k);
+    if ((h->nnz_assembled > 0 && !nzval) || !Bin || !Bout || ldb < n) return fail(h, PP_EINVAL, "%s: arrays", who);
+    CK(h, cudaSetDevice(h->device), who);
+    for (const void *p : {nzval, Bin, (const void *)Bout}) {
+        if (!p) continue;
+        cudaPointerAttributes pa{};
+        CK(h, cudaPointerGetAttributes(&pa, p), who);
+        if ((pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged) ||
+            (pa.type == cudaMemoryTypeDevice && pa.device != h->device))
+            return fail(h, PP_EINVAL, "%s: nzval, Bin and Bout must be memory of the handle's device", who);
+    }
+    // one uncaptured step allocates everything the step uses (workspace, right-hand sides, counters) and
+    // reports any error; the captured step then allocates nothing
+    const size_t es = h->ops ? h->ops->esize : 8;
+    const int64_t ldx = (k + 3) & ~(int64_t)3;
+    const size_t xbytes = es * (size_t)n * ldx;
+    if (need_memory(h, xbytes > h->X.bytes ? xbytes : 0, who) != PP_OK) return PP_ENOMEM;
+    CK(h, h->X.ensure(xbytes), who);
+    if (ensure_sync(h, k) != PP_OK) return PP_ENOMEM;
+    int32_t r = plan_step(h, nzval, Bin, Bout, ldb, k, nullptr);
+    if (r != PP_OK) return r;
+    r = settle(h, who);
+    if (r != PP_OK) return r;
+    auto *p = new (std::nothrow) pp_plan();
+    if (!p) return fail(h, PP_ENOMEM, "%s: out of host memory", who);
+    p->h = h;
+    Profiler *const save_prof = h->hp.prof;
+    h->hp.prof = nullptr;
+    h->capturing = true;
+    cudaError_t e = cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeRelaxed);
+    if (e == cudaSuccess) {
+        r = plan_step(h, nzval, Bin, Bout, ldb, k, &p->launches);
+        e = cudaStreamEndCapture(h->stream, &p->graph);  // also ends a capture that a failed call left open
+    }
+    h->capturing = false;
+    h->hp.prof = save_prof;
+    if (e == cudaSuccess && r == PP_OK) e = cudaGraphInstantiate(&p->exec, p->graph, 0);
+    if (e != cudaSuccess || r != PP_OK) {
+        if (p->graph) cudaGraphDestroy(p->graph);
+        delete p;
+        cudaGetLastError();
+        return r != PP_OK ? r : cuda_fail(h, e, who);
+    }
+    *out = p;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_plan_launch(pp_plan *p) {
+    if (!p || !p->exec) return fail(nullptr, PP_EINVAL, "pp_plan_launch: null plan");
+    pp_handle *h = p->h;
+    CK(h, cudaSetDevice(h->device), "pp_plan_launch");
+    CK(h, cudaGraphLaunch(p->exec, h->stream), "pp_plan_launch");
+    h->factored = true;
+    h->have_values = true;
+    h->st.kernel_launches = p->launches;
+    ok(h);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_plan_launches(const pp_plan *p, int64_t *launches) {
+    if (!p || !launches) return fail(nullptr, PP_EINVAL, "pp_plan_launches: null argument");
+    *launches = p->launches;
+    return PP_OK;
+}
+
+extern "C" int32_t pp_plan_destroy(pp_plan *p) {
+    if (!p) return PP_OK;
+    if (p->h && cudaSetDevice(p->h->device) == cudaSuccess) cudaStreamSynchronize(p->h->stream);
+    if (p->exec) cudaGraphExecDestroy(p->exec);
+    if (p->graph) cudaGraphDestroy(p->graph);
+    delete p;
     return PP_OK;
 }
 

@@ -57,6 +57,10 @@ SIGNATURES = {
     "pp_lmul_static": (C.c_int32, [_P, _P, C.c_int64, C.c_int64]),
     "pp_star": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int64, C.c_int32]),
     "pp_sync": (C.c_int32, [_P]),
+    "pp_plan_lmul": (C.c_int32, [_P, _P, _P, _P, C.c_int64, C.c_int64, C.POINTER(_P)]),
+    "pp_plan_launch": (C.c_int32, [_P]),
+    "pp_plan_launches": (C.c_int32, [_P, C.POINTER(C.c_int64)]),
+    "pp_plan_destroy": (C.c_int32, [_P]),
     "pp_get_stats": (C.c_int32, [_P, C.POINTER(pp_stats)]),
     "pp_stream": (_P, [_P]),
     "pp_set_profile": (C.c_int32, [_P, C.c_int32]),

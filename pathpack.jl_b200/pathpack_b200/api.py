@@ -146,6 +146,19 @@ class B200SLU:
     def sync(self):
         check(lib().pp_sync(self._h), self._h)
 
+    # --- plans
+    def plan_lmul(self, nzval, Bin, Bout=None):
+        """A Plan replaying one step as a CUDA graph (pp_plan_lmul): new weights from the CUDA tensor nzval
+        re-assembled, the factorization, and Bout <- A* Bin (column-major n x k CUDA tensors; Bout = Bin by
+        default).  Plan.launch() enqueues a step on the handle's stream."""
+        Bout = Bin if Bout is None else Bout
+        for t in (nzval, Bin, Bout):
+            if not hasattr(t, "data_ptr") or not t.is_cuda or t.dtype.itemsize != self.dtype.itemsize:
+                raise TypeError("nzval, Bin and Bout must be CUDA tensors of the factor's element type")
+        if Bin.dim() != 2 or Bin.stride(0) != 1 or Bout.shape != Bin.shape or Bout.stride() != Bin.stride():
+            raise ValueError("Bin and Bout must be column-major n x k tensors of the same layout")
+        return Plan(self, nzval, Bin, Bout)
+
     # --- solves
     def lmul_static(self, B):
         """B <- A* B for a column-major CUDA tensor B, through pp_lmul_static: the solve allocates nothing and
@@ -209,6 +222,37 @@ class B200SLU:
                 raise ValueError("out must be column-major")
             check(lib().pp_star(self._h, vptr(out), n, col0, ncols, PP_HOST), self._h)
         return out
+
+
+class Plan:
+    """A captured refactor + lmul! step of a B200SLU (see B200SLU.plan_lmul)."""
+
+    def __init__(self, F, nzval, Bin, Bout):
+        self.F, self._keep = F, (nzval, Bin, Bout)
+        p = C.c_void_p()
+        check(lib().pp_plan_lmul(F._h, vptr(nzval), vptr(Bin), vptr(Bout), Bin.stride(1), Bin.shape[1],
+                                 C.byref(p)), F._h)
+        self._p = p
+
+    def launch(self):
+        check(lib().pp_plan_launch(self._p), self.F._h)
+
+    @property
+    def launches(self):
+        n = C.c_int64()
+        check(lib().pp_plan_launches(self._p, C.byref(n)))
+        return n.value
+
+    def close(self):
+        if getattr(self, "_p", None):
+            lib().pp_plan_destroy(self._p)
+            self._p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class TransposedSLU:

@@ -171,15 +171,19 @@ def equal_values(a, b, what=""):
         raise AssertionError("%s: %d entries differ, e.g. %s vs %s" % (what, bad.sum(), a.ravel()[i], b.ravel()[i]))
 
 
-def bits_equal(a, b, name, dtype, what=""):
-    """Bit-exact, except that Float32 results may differ in the sign of a zero: the device's Float32 min/max
-    are the hardware min/max (the reference's GPU kernels use the same, llvm.minnum), which order -0.0 below
-    +0.0, where the reference CPU's select ifelse(x < y, x, y) returns its second operand on a tie."""
+def bits_equal(a, b, name, dtype, what="", solve=False):
+    """Bit-exact, except for the sign of a zero in two places.  (1) Float32 min/max on the device are the
+    hardware min/max (the reference's GPU kernels use the same, llvm.minnum), which order -0.0 below +0.0,
+    where the reference CPU's select ifelse(x < y, x, y) returns its second operand on a tie.  (2) With
+    solve=True (lmul!, rmul!, the star), for every element type: the solves' separator scatters combine the
+    contributions of several fronts with atomics in whatever order they arrive, and with a select-based (+)
+    the sign of a zero sum depends on that order (the reference's GPU scatters, atomic_splus!, have the same
+    freedom)."""
     a, b = np.asarray(a), np.asarray(b)
     assert a.shape == b.shape, what
     u = np.uint32 if a.itemsize == 4 else np.uint64
     bad = a.view(u) != b.view(u)
-    if np.dtype(dtype) == np.float32:
+    if np.dtype(dtype).kind == "f" and (np.dtype(dtype) == np.float32 or solve):
         bad &= ~((a == 0) & (b == 0))
     if bad.any():
         i = np.flatnonzero(bad)[:5]

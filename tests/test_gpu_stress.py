@@ -3,8 +3,7 @@
 Per case (seeded graph family, zero and signed-zero weights, negative arcs, one negative cycle, duplicate
 arcs, self-loops, positive cycles for MaxPlus/MaxProd, coupled components) the factor, lmul!, rmul! and
 Matrix(F) computed through the C ABI are compared with the oracle: bit for bit for every semiring but PlusProd
-(Float32 results may differ from the reference CPU's select in the sign of a zero, see
-tests/stress.py:bits_equal), within rtol 1e-5 / 1e-12 and identical +-Inf patterns for PlusProd.  The star is
+(the sign of a zero may differ where tests/stress.py:bits_equal says why), within rtol 1e-5 / 1e-12 and identical +-Inf patterns for PlusProd.  The star is
 also checked against Kleene's algorithm, which shares no code with either.  Repeated runs must give the same
 bits for the idempotent semirings (the reference's test/gpu/stress_large.jl:1-3).
 """
@@ -23,13 +22,13 @@ SR = {s.__class__.__name__: s for s in [pp.MinPlus(), pp.MaxPlus(), pp.MaxMin(),
                                          pp.PlusProd(), pp.OrAnd()]}
 
 
-def check(got, want, name, dtype, what):
+def check(got, want, name, dtype, what, solve=True):
     if name == "PlusProd":
         from tests.helpers import close
 
         close(got, want, name, dtype, what)
     else:
-        stress.bits_equal(got, want, name, dtype, what)
+        stress.bits_equal(got, want, name, dtype, what, solve)
 
 
 def run_case(c, k=19):
@@ -39,7 +38,7 @@ def run_case(c, k=19):
     try:
         O = OracleLU(name, dtype, S).assemble(c["cp"], c["rv"], c["nz"]).factor()
         for got, want, what in zip(F.factors(), (O.LD, O.LL, O.UD, O.UL), ("LD", "LL", "UD", "UL")):
-            check(got, want, name, dtype, "%s %s" % (c["tag"], what))
+            check(got, want, name, dtype, "%s %s" % (c["tag"], what), solve=False)
         rng = np.random.default_rng(n)
         z, one = SR[name].zero(dtype), SR[name].one(dtype)
         B = np.full((n, k), z, dtype=dtype, order="F")

@@ -76,6 +76,30 @@ const char *pp_last_error(const pp_handle *h);
 
 /* Create a handle on a CUDA device (stream, device structures created lazily). */
 int32_t pp_create(int32_t device, pp_handle **h);
+
+/* Handle options (the pp_options of the reference-facing plan: pp_create(device, const pp_options*, ...)).
+   Start from pp_default_options and change fields.
+     wait_timeout_us   bound of every device-side wait of the persistent kernels on another block's progress,
+                       in microseconds; 0 = the default, 2 s.  A wait that runs out makes the kernels of the
+                       call return early and the call report PP_ETIMEOUT at its next wait for the stream (the
+                       results of that call are then undefined; the handle stays usable).  Raise it when the
+                       GPU is time-sliced with other work.
+     fail_alloc_after  testing: when >= 0, that many device allocations of the handle succeed and the next
+                       one fails as if the device were out of memory (the call returns PP_ENOMEM, having freed
+                       nothing it still needs and leaked nothing); -1 (default) = off.
+     profile           1: per-launch timing (pp_set_profile). */
+typedef struct pp_options {
+    int64_t wait_timeout_us;
+    int64_t fail_alloc_after;
+    int32_t profile;
+    int32_t reserved;
+} pp_options;
+void pp_default_options(pp_options *opt);
+/* pp_create with options (opt may be NULL: the defaults). */
+int32_t pp_create_with(int32_t device, const pp_options *opt, pp_handle **h);
+/* Change the options of a handle (waits for the handle's work first). */
+int32_t pp_set_options(pp_handle *h, const pp_options *opt);
+int32_t pp_get_options(const pp_handle *h, pp_options *opt);
 /* Release everything the handle holds.  Safe on NULL. */
 int32_t pp_destroy(pp_handle *h);
 
@@ -168,9 +192,11 @@ int32_t pp_lmul_static(pp_handle *h, void *B, int64_t ldb, int64_t k);
    everything the step needs is allocated and errors are reported, then records it into a CUDA graph.
    pp_plan_launch enqueues one step on the handle's stream (pp_stream) and returns: write new weights into
    nzval (or new right-hand sides into Bin) on that stream first and launch again.  A device error of a
-   launch is reported by the next call that waits (pp_sync).  The plan keeps the handle's buffers and the
-   three arrays' addresses: keep them alive and do not change the handle's structure or semiring while a
-   plan exists; pp_plan_destroy releases the graph (not the handle). */
+   launch is reported by the next call that waits (pp_sync).  The graph works on the handle's factor arrays
+   and workspace, on scratch of its own (the right-hand sides in the device layout and the kernels' counters,
+   so that the handle's other calls stay free to grow their buffers) and on the three arrays, whose addresses
+   it keeps: keep them alive and do not change the handle's structure or semiring while a plan exists;
+   pp_plan_destroy releases the graph and its scratch (not the handle). */
 typedef struct pp_plan pp_plan;
 int32_t pp_plan_lmul(pp_handle *h, const void *nzval, const void *Bin, void *Bout, int64_t ldb, int64_t k,
                      pp_plan **plan);

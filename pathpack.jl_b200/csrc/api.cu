@@ -57,6 +57,10 @@ using namespace pp;
 
 static thread_local std::string g_err;
 
+// The allocation budget of the handle whose call is running on this thread (pp_options.fail_alloc_after):
+// when it is >= 0, the allocation that finds it at 0 fails as if the device were out of memory.
+static thread_local int64_t *t_alloc_budget = nullptr;
+
 struct DevBuf {
     void *p = nullptr;
     size_t bytes = 0;
@@ -70,8 +74,12 @@ struct DevBuf {
         if (b <= bytes && p) return cudaSuccess;
         release();
         if (b == 0) b = 16;
+        if (t_alloc_budget && *t_alloc_budget >= 0 && (*t_alloc_budget)-- == 0) return cudaErrorMemoryAllocation;
         cudaError_t e = cudaMalloc(&p, b);
-        if (e == cudaSuccess) bytes = b;
+        if (e == cudaSuccess)
+            bytes = b;
+        else
+            cudaGetLastError();  // a failed allocation must not surface as the error of a later launch
         return e;
     }
     template <typename U>
@@ -121,6 +129,17 @@ struct pp_handle {
     pp_stats st{};
     Profiler prof;
     int sm_count = 148;
+    // options (pp_options): the bound of the device waits on other CTAs (nanoseconds, kept on the device in
+    // d_err[2..3]) and the allocation test hook
+    uint64_t wait_ns = 0;
+    int64_t fail_alloc_after = -1;
+};
+
+// Makes the handle's allocation budget the one DevBuf::ensure consults for the rest of the enclosing call.
+struct AllocScope {
+    int64_t *prev;
+    explicit AllocScope(pp_handle *h) : prev(t_alloc_budget) { t_alloc_budget = h ? &h->fail_alloc_after : nullptr; }
+    ~AllocScope() { t_alloc_budget = prev; }
 };
 
 static int32_t fail(pp_handle *h, int32_t code, const char *fmt, ...) {
@@ -135,6 +154,7 @@ static int32_t fail(pp_handle *h, int32_t code, const char *fmt, ...) {
 }
 
 static int32_t cuda_fail(pp_handle *h, cudaError_t e, const char *what) {
+    if (e == cudaErrorMemoryAllocation) return fail(h, PP_ENOMEM, "%s: out of device memory", what);
     return fail(h, PP_EDEVICE, "%s: %s", what, cudaGetErrorString(e));
 }
 
@@ -238,6 +258,61 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
 
 extern "C" void *pp_stream(pp_handle *h) { return h ? (void *)h->stream : nullptr; }
 
+// ---------------------------------------------------------------- options
+
+extern "C" void pp_default_options(pp_options *o) {
+    if (!o) return;
+    memset(o, 0, sizeof *o);
+    o->wait_timeout_us = 0;
+    o->fail_alloc_after = -1;
+    o->profile = 0;
+}
+
+static int32_t apply_options(pp_handle *h, const pp_options *o, const char *who) {
+    if (o->wait_timeout_us < 0) return fail(h, PP_EINVAL, "%s: wait_timeout_us = %lld", who, (long long)o->wait_timeout_us);
+    if (o->wait_timeout_us > (int64_t)1 << 40) return fail(h, PP_EINVAL, "%s: wait_timeout_us too large", who);
+    h->wait_ns = (uint64_t)o->wait_timeout_us * 1000u;
+    h->fail_alloc_after = o->fail_alloc_after < 0 ? -1 : o->fail_alloc_after;
+    if (h->d_err.p) {
+        // nothing of the handle may be running while the bound changes; the copy is synchronous
+        CK(h, cudaStreamSynchronize(h->factor_stream), who);
+        CK(h, cudaStreamSynchronize(h->stream), who);
+        CK(h, cudaMemcpy(h->d_err.as<int>() + 2, &h->wait_ns, sizeof(uint64_t), cudaMemcpyHostToDevice), who);
+    }
+    h->prof.on = o->profile != 0;
+    return PP_OK;
+}
+
+extern "C" int32_t pp_create_with(int32_t device, const pp_options *opt, pp_handle **out) {
+    const int32_t r = pp_create(device, out);
+    if (r != PP_OK || !opt) return r;
+    const int32_t r2 = apply_options(*out, opt, "pp_create_with");
+    if (r2 != PP_OK) {
+        const std::string msg = (*out)->err;
+        pp_destroy(*out);
+        *out = nullptr;
+        return fail(nullptr, r2, "%s", msg.c_str());
+    }
+    return PP_OK;
+}
+
+extern "C" int32_t pp_set_options(pp_handle *h, const pp_options *opt) {
+    if (!h || !opt) return fail(h, PP_EINVAL, "pp_set_options: null argument");
+    CK(h, cudaSetDevice(h->device), "pp_set_options");
+    const int32_t r = apply_options(h, opt, "pp_set_options");
+    if (r == PP_OK) ok(h);
+    return r;
+}
+
+extern "C" int32_t pp_get_options(const pp_handle *h, pp_options *opt) {
+    if (!h || !opt) return fail(nullptr, PP_EINVAL, "pp_get_options: null argument");
+    pp_default_options(opt);
+    opt->wait_timeout_us = (int64_t)(h->wait_ns / 1000u);
+    opt->fail_alloc_after = h->fail_alloc_after;
+    opt->profile = h->prof.on ? 1 : 0;
+    return PP_OK;
+}
+
 // ---------------------------------------------------------------- structure
 
 // Order of the fronts of one persistent launch (a bottom sweep, or the factorization of the bottom).  The
@@ -308,6 +383,7 @@ static std::vector<int> schedule_order(const std::vector<int> &fronts, const std
 extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, const int64_t *Rptr,
                                     const int64_t *Sptr, const int64_t *Stgt, const int64_t *Bptr, const int64_t *Fptr,
                                     const int64_t *Nptr, const int64_t *Ntgt, const int64_t *perm, int32_t base) {
+    AllocScope alloc_scope(h);
     if (!h) return fail(nullptr, PP_EINVAL, "pp_set_structure: null handle");
     if (n < 0 || nf < 0 || nB < 0 || (n > 0 && (nf < 1 || nB < 1)) || n >= INT32_MAX)
         return fail(h, PP_EINVAL, "pp_set_structure: sizes n=%lld nf=%lld nB=%lld", (long long)n, (long long)nf,
@@ -673,6 +749,8 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         CK(h, h->d_sync.ensure(sizeof(int) * sync_ints(nf, 256)), "upload");
         CK(h, h->d_err.ensure(sizeof(int) * 4), "upload");
         CK(h, cudaMemsetAsync(h->d_err.p, 0, sizeof(int) * 4, st), "upload");
+        CK(h, cudaMemcpyAsync(h->d_err.as<int>() + 2, &h->wait_ns, sizeof(uint64_t), cudaMemcpyHostToDevice, st),
+           "upload");
         CK(h, cudaStreamSynchronize(st), "upload");
         DevPlan &d = hp.dev;
         d.n = (int)n;
@@ -952,7 +1030,13 @@ static int32_t need_memory(pp_handle *h, size_t bytes, const char *what) {
     return PP_OK;
 }
 
+static int32_t ensure_sync(pp_handle *h, int64_t k);
+
 static int32_t set_semiring(pp_handle *h, int32_t sr, int32_t dt, const char *who) {
+    // the values are being replaced: until this call and its caller succeed there are none to factor or solve
+    // with (a failed allocation below may have released buffers the device plan points into)
+    h->have_values = h->factored = false;
+    h->nnz_assembled = -1;  // pp_update_values needs the pattern of a completed pp_assemble
     const Ops *o = get_ops(sr, dt);
     if (!o) return fail(h, PP_EUNSUPPORTED, "%s: semiring %d with element type %d is not supported", who, sr, dt);
     if (h->ops != o) {
@@ -1000,6 +1084,7 @@ static cudaError_t record_timing(pp_handle *h, cudaEvent_t ev, cudaStream_t st) 
 
 extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, const int64_t *colptr,
                                const int64_t *rowval, const void *nzval, int32_t base) {
+    AllocScope alloc_scope(h);
     if (!h) return fail(nullptr, PP_EINVAL, "pp_assemble: null handle");
     if (!h->have_structure) return fail(h, PP_ESTATE, "pp_assemble: no structure (call pp_set_structure first)");
     if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_assemble: base must be 0 or 1");
@@ -1059,6 +1144,7 @@ extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, co
 }
 
 extern "C" int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t where) {
+    AllocScope alloc_scope(h);
     if (!h) return fail(nullptr, PP_EINVAL, "pp_update_values: null handle");
     if (!h->have_structure || h->nnz_assembled < 0)
         return fail(h, PP_ESTATE, "pp_update_values: no pattern (call pp_assemble first)");
@@ -1090,6 +1176,7 @@ extern "C" int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t whe
 
 extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, const void *LD, const void *LL,
                                  const void *UD, const void *UL, const void *Nval) {
+    AllocScope alloc_scope(h);
     if (!h) return fail(nullptr, PP_EINVAL, "pp_set_values: null handle");
     if (!h->have_structure) return fail(h, PP_ESTATE, "pp_set_values: no structure");
     CK(h, cudaSetDevice(h->device), "pp_set_values");
@@ -1141,6 +1228,7 @@ static int32_t settle(pp_handle *h, const char *who) {
 }
 
 extern "C" int32_t pp_factor(pp_handle *h) {
+    AllocScope alloc_scope(h);
     if (!h) return fail(nullptr, PP_EINVAL, "pp_factor: null handle");
     if (!h->have_values) return fail(h, PP_ESTATE, "pp_factor: no values (call pp_assemble or pp_set_values)");
     CK(h, cudaSetDevice(h->device), "pp_factor");
@@ -1149,9 +1237,11 @@ extern "C" int32_t pp_factor(pp_handle *h) {
         CK(h, cudaStreamSynchronize(h->factor_stream), "pp_factor");
         CK(h, cudaStreamSynchronize(h->stream), "pp_factor");
         h->W.release();
+        h->factored = false;
         if (need_memory(h, wbytes, "pp_factor") != PP_OK) return PP_ENOMEM;
         CK(h, h->W.ensure(wbytes), "pp_factor");
     }
+    if (ensure_sync(h, 1) != PP_OK) return PP_ENOMEM;  // the bottom kernel's counters
     cudaStream_t st = h->stream;
     int64_t nl = 0;
     CK(h, after_factor(h), "pp_factor");  // the previous top factorization reads the bottom's update matrices
@@ -1196,6 +1286,8 @@ static int32_t ensure_sync(pp_handle *h, int64_t k) {
     if (need <= h->hp.sync_cap) return PP_OK;
     if (need_memory(h, sizeof(int) * need, "sweep counters") != PP_OK) return PP_ENOMEM;
     h->d_sync.release();
+    h->hp.d_sync = nullptr;  // no call may use the released counters
+    h->hp.sync_cap = 0;
     cudaError_t e = h->d_sync.ensure(sizeof(int) * need);
     if (e != cudaSuccess) return cuda_fail(h, e, "sweep counters");
     h->hp.d_sync = h->d_sync.as<int>();
@@ -1239,6 +1331,7 @@ static int32_t enqueue_solve(pp_handle *h, const void *Bin, void *Bout, int64_t 
 // 88-110 with trans = :T) on this layout.
 static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where, int left, int trans,
                          const char *who) {
+    AllocScope alloc_scope(h);
     if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
     if (!h->factored) return fail(h, PP_ESTATE, "%s: no factorization (call pp_factor)", who);
     const int n = h->hp.n;
@@ -1387,6 +1480,7 @@ extern "C" int32_t pp_rmul_t(pp_handle *h, void *B, int64_t ldb, int64_t k, int3
 }
 
 extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where) {
+    AllocScope alloc_scope(h);
     const char *who = "pp_star";
     if (!h) return fail(nullptr, PP_EINVAL, "pp_star: null handle");
     if (!h->factored) return fail(h, PP_ESTATE, "pp_star: no factorization (call pp_factor)");
@@ -1547,11 +1641,23 @@ extern "C" int32_t pp_get_profile(pp_handle *h, pp_kernel_class *out, int32_t ma
 
 // ---------------------------------------------------------------- plans: refactor + solve as one CUDA graph
 
+// Record the events that order the handle's calls after a factorization (ev_bottom, ev_factored) on the
+// handle's stream, outside any capture, so that they mark everything enqueued on it so far.
+static cudaError_t uncapture_events(pp_handle *h) {
+    cudaError_t e = cudaEventRecord(h->ev_bottom, h->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(h->ev_factored, h->stream);
+    return e;
+}
+
+// A plan owns the scratch its graph uses (the right-hand sides in the device layout and the counters of the
+// persistent kernels), so that later calls of the handle, which may grow and so reallocate the handle's own
+// buffers, never free memory the graph points into.
 struct pp_plan {
     pp_handle *h = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int64_t launches = 0;
+    DevBuf X, sync;
 };
 
 // The calls of one plan step, enqueued on the handle's stream: new weights from device memory re-assembled,
@@ -1569,8 +1675,27 @@ static int32_t plan_step(pp_handle *h, const void *nzval, const void *Bin, void 
     return PP_OK;
 }
 
+// plan_step on the plan's own scratch: the handle's right-hand-side buffer and counters are swapped for the
+// plan's for the duration of the step (the captured graph then points into the plan's buffers only)
+static int32_t plan_step_own(pp_plan *p, const void *nzval, const void *Bin, void *Bout, int64_t ldb, int64_t k) {
+    pp_handle *h = p->h;
+    std::swap(h->X.p, p->X.p);
+    std::swap(h->X.bytes, p->X.bytes);
+    int *const save_sync = h->hp.d_sync;
+    const int64_t save_cap = h->hp.sync_cap;
+    h->hp.d_sync = p->sync.as<int>();
+    h->hp.sync_cap = (int64_t)(p->sync.bytes / sizeof(int));
+    const int32_t r = plan_step(h, nzval, Bin, Bout, ldb, k, &p->launches);
+    h->hp.d_sync = save_sync;
+    h->hp.sync_cap = save_cap;
+    std::swap(h->X.p, p->X.p);
+    std::swap(h->X.bytes, p->X.bytes);
+    return r;
+}
+
 extern "C" int32_t pp_plan_lmul(pp_handle *h, const void *nzval, const void *Bin, void *Bout, int64_t ldb, int64_t k,
                                 pp_plan **out) {
+    AllocScope alloc_scope(h);
     const char *who = "pp_plan_lmul";
     if (!out) return fail(h, PP_EINVAL, "%s: null output pointer", who);
     *out = nullptr;
@@ -1604,16 +1729,28 @@ extern "C" int32_t pp_plan_lmul(pp_handle *h, const void *nzval, const void *Bin
     auto *p = new (std::nothrow) pp_plan();
     if (!p) return fail(h, PP_ENOMEM, "%s: out of host memory", who);
     p->h = h;
+    {
+        const size_t sbytes = sizeof(int) * (size_t)sync_ints(h->hp.nf, k);
+        cudaError_t ea = p->X.ensure(xbytes);
+        if (ea == cudaSuccess) ea = p->sync.ensure(sbytes);
+        if (ea != cudaSuccess) {
+            delete p;
+            return cuda_fail(h, ea, who);
+        }
+    }
     Profiler *const save_prof = h->hp.prof;
     h->hp.prof = nullptr;
     h->capturing = true;
     cudaError_t e = cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeRelaxed);
     if (e == cudaSuccess) {
-        r = plan_step(h, nzval, Bin, Bout, ldb, k, &p->launches);
+        r = plan_step_own(p, nzval, Bin, Bout, ldb, k);
         e = cudaStreamEndCapture(h->stream, &p->graph);  // also ends a capture that a failed call left open
     }
     h->capturing = false;
     h->hp.prof = save_prof;
+    // the captured step recorded the handle's factorization events inside the graph, where later calls may not
+    // wait on them: record them again on the stream, after everything enqueued so far
+    uncapture_events(h);
     if (e == cudaSuccess && r == PP_OK) e = cudaGraphInstantiate(&p->exec, p->graph, 0);
     if (e != cudaSuccess || r != PP_OK) {
         if (p->graph) cudaGraphDestroy(p->graph);
@@ -1631,6 +1768,8 @@ extern "C" int32_t pp_plan_launch(pp_plan *p) {
     pp_handle *h = p->h;
     CK(h, cudaSetDevice(h->device), "pp_plan_launch");
     CK(h, cudaGraphLaunch(p->exec, h->stream), "pp_plan_launch");
+    // the graph's factorization ends inside the launch: later calls order themselves after the launch
+    CK(h, uncapture_events(h), "pp_plan_launch");
     h->factored = true;
     h->have_values = true;
     h->st.kernel_launches = p->launches;

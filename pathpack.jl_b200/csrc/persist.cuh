@@ -7,8 +7,8 @@
 // reference level-schedules the same work (ext/PATHPACKCUDAExt/chordal/sgetrf.jl:324-343, batched/sweep.jl:9-21)
 // with a launch per level.
 //
-// Every wait is bounded: after WAIT_LIMIT polls the kernel records the failure in *err and returns, and the
-// host reports PP_ETIMEOUT.  Data written by other CTAs during the same launch is read through L2
+// Every wait is bounded: after the handle's wait timeout the kernel records the failure in *err and returns,
+// and the host reports PP_ETIMEOUT.  Data written by other CTAs during the same launch is read through L2
 // (ld.global.cg) and published with __threadfence() before the counter update.
 #pragma once
 
@@ -16,13 +16,34 @@
 
 namespace pp {
 
-constexpr long long WAIT_LIMIT = 20000000;  // polls of ~100 ns each: about two seconds
+// polls of a wait on another warp of the same CTA (shared memory; that warp always progresses)
+constexpr long long WAIT_LIMIT = 20000000;
+// default bound of a wait on another CTA's progress, in nanoseconds (pp_options.wait_timeout_us overrides it)
+constexpr unsigned long long WAIT_NS_DEFAULT = 2000000000ull;
+
+// The error area of a handle: err[0] the error word, err[2..3] the bound of the waits on other CTAs in
+// nanoseconds (0: WAIT_NS_DEFAULT).  A wait reads the bound once, then checks the global timer every 16 polls.
+struct WaitBound {
+    unsigned long long t0, lim;
+    unsigned it = 0;
+    __device__ __forceinline__ explicit WaitBound(const int *err) {
+        const unsigned long long l = *(volatile const unsigned long long *)(err + 2);
+        lim = l ? l : WAIT_NS_DEFAULT;
+        t0 = now();
+    }
+    static __device__ __forceinline__ unsigned long long now() {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        return t;
+    }
+    __device__ __forceinline__ bool expired() { return (++it & 15) == 0 && now() - t0 > lim; }
+};
 
 // thread 0 of the CTA polls *p until it satisfies the predicate (or the limit expires); broadcast result
 __device__ __forceinline__ bool cta_wait(const int *p, bool for_zero, int *err) {
     __shared__ int s_ok;
     if (threadIdx.x == 0) {
-        long long it = 0;
+        WaitBound wb(err);
         int ok = 1;
         while (true) {
             const int v = *(volatile const int *)p;
@@ -31,7 +52,7 @@ __device__ __forceinline__ bool cta_wait(const int *p, bool for_zero, int *err) 
                 ok = 0;
                 break;
             }
-            if (++it > WAIT_LIMIT) {
+            if (wb.expired()) {
                 atomicExch(err, 1);
                 ok = 0;
                 break;
@@ -64,7 +85,7 @@ __device__ __forceinline__ int cta_take(int *next) {
 __device__ __forceinline__ int cta_claim(int *p, int *err) {
     __shared__ int s_r;
     if (threadIdx.x == 0) {
-        long long it = 0;
+        WaitBound wb(err);
         int r;
         while (true) {
             const int v = *(volatile const int *)p;
@@ -80,7 +101,7 @@ __device__ __forceinline__ int cta_claim(int *p, int *err) {
                 r = -1;
                 break;
             }
-            if (++it > WAIT_LIMIT) {
+            if (wb.expired()) {
                 atomicExch(err, 1);
                 r = -1;
                 break;
@@ -252,7 +273,7 @@ __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &
 __device__ __forceinline__ bool warp_wait(const int *p, bool for_zero, int *err) {
     int ok = 1;
     if ((threadIdx.x & 31) == 0) {
-        long long it = 0;
+        WaitBound wb(err);
         while (true) {
             const int v = *(volatile const int *)p;
             if (for_zero ? (v == 0) : (v != 0)) break;
@@ -260,7 +281,7 @@ __device__ __forceinline__ bool warp_wait(const int *p, bool for_zero, int *err)
                 ok = 0;
                 break;
             }
-            if (++it > WAIT_LIMIT) {
+            if (wb.expired()) {
                 atomicExch(err, 1);
                 ok = 0;
                 break;

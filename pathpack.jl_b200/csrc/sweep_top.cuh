@@ -41,7 +41,7 @@ constexpr size_t sweep_top_smem() {
 __device__ __forceinline__ int cta_wait_blocks(const int *p, int target, int *err) {
     __shared__ int s_v;
     if (threadIdx.x == 0) {
-        long long it = 0;
+        WaitBound wb(err);
         int v;
         while (true) {
             v = *(volatile const int *)p;
@@ -50,7 +50,7 @@ __device__ __forceinline__ int cta_wait_blocks(const int *p, int target, int *er
                 v = -1;
                 break;
             }
-            if (++it > WAIT_LIMIT) {
+            if (wb.expired()) {
                 atomicExch(err, 1);
                 v = -1;
                 break;

@@ -65,14 +65,14 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
 __device__ __forceinline__ bool cta_wait_geq(const int *p, int target, int *err) {
     __shared__ int s_ok;
     if (threadIdx.x == 0) {
-        long long it = 0;
+        WaitBound wb(err);
         int ok = 1;
         while (ld_acquire(p) < target) {
             if (*(volatile const int *)err) {
                 ok = 0;
                 break;
             }
-            if (++it > WAIT_LIMIT) {
+            if (wb.expired()) {
                 atomicExch(err, 1);
                 ok = 0;
                 break;
@@ -334,9 +334,9 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
                     const int ch = s_ctop[q];
                     if (ch < 0) continue;
                     const int sbc = (P.na[ch] + TB - 1) / TB, nbc = (P.nn[ch] + TB - 1) / TB + sbc;
-                    long long it = 0;
+                    WaitBound wb(err);
                     while (ld_acquire(flags + foff[ch] + nbc * nbc) < sbc * sbc) {
-                        if (*(volatile const int *)err || ++it > WAIT_LIMIT) {
+                        if (*(volatile const int *)err || wb.expired()) {
                             atomicExch(err, 1);
                             bad = 1;
                             break;

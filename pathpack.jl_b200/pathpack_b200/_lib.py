@@ -30,6 +30,11 @@ class pp_stats(C.Structure):
                 ("pairs_solve", C.c_double), ("device_bytes", C.c_int64), ("kernel_launches", C.c_int64)]
 
 
+class pp_options(C.Structure):
+    _fields_ = [("wait_timeout_us", C.c_int64), ("fail_alloc_after", C.c_int64), ("profile", C.c_int32),
+                ("reserved", C.c_int32)]
+
+
 class pp_kernel_class(C.Structure):
     _fields_ = [("name", C.c_char * 32), ("launches", C.c_int64), ("ms", C.c_double), ("bytes", C.c_double),
                 ("pairs", C.c_double)]
@@ -44,6 +49,10 @@ SIGNATURES = {
     "pp_last_error": (C.c_char_p, [_P]),
     "pp_create": (C.c_int32, [C.c_int32, C.POINTER(_P)]),
     "pp_destroy": (C.c_int32, [_P]),
+    "pp_default_options": (None, [C.c_void_p]),
+    "pp_create_with": (C.c_int32, [C.c_int32, C.c_void_p, C.POINTER(_P)]),
+    "pp_set_options": (C.c_int32, [_P, C.c_void_p]),
+    "pp_get_options": (C.c_int32, [_P, C.c_void_p]),
     "pp_set_structure": (C.c_int32, [_P, C.c_int64, C.c_int64, C.c_int64] + [_I64P] * 8 + [C.c_int32]),
     "pp_assemble": (C.c_int32, [_P, C.c_int32, C.c_int32, _I64P, _I64P, _P, C.c_int32]),
     "pp_update_values": (C.c_int32, [_P, _P, C.c_int32]),

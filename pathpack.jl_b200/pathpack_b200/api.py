@@ -17,7 +17,7 @@ import ctypes as C
 import numpy as np
 
 from . import semiring as sr
-from ._lib import PP_DEVICE, PP_HOST, check, i64ptr, lib, pp_stats, vptr
+from ._lib import PP_DEVICE, PP_HOST, check, i64ptr, lib, pp_options, pp_stats, vptr
 from .symbolic import Structure, ssymbolic
 
 
@@ -37,10 +37,20 @@ def _csc(A, dtype=None):
     return n, A.indptr.astype(np.int64), A.indices.astype(np.int64), np.ascontiguousarray(data)
 
 
+def _options(kw):
+    o = pp_options()
+    lib().pp_default_options(C.byref(o))
+    for k, v in kw.items():
+        if k not in dict(pp_options._fields_) or k == "reserved":
+            raise TypeError("unknown option %r" % k)
+        setattr(o, k, int(v))
+    return o
+
+
 class B200SLU:
     """A factorization of the star of A over a semiring, held on one GPU (mlu's result)."""
 
-    def __init__(self, s, dtype, structure, device=0):
+    def __init__(self, s, dtype, structure, device=0, **options):
         dtype = np.dtype(dtype)
         if not sr.supported(s, dtype):
             raise TypeError("%r over %s is not supported (pp_check_semiring)" % (s, dtype))
@@ -48,11 +58,25 @@ class B200SLU:
         self._dt = sr.DTYPES[dtype]
         L = lib()
         h = C.c_void_p()
-        check(L.pp_create(device, C.byref(h)))
+        check(L.pp_create_with(device, C.byref(_options(options)) if options else None, C.byref(h)))
         self._h = h
         S = structure
         check(L.pp_set_structure(h, S.n, S.nf, S.nB, i64ptr(S.Rptr), i64ptr(S.Sptr), i64ptr(S.Stgt), i64ptr(S.Bptr),
                                  i64ptr(S.Fptr), i64ptr(S.Nptr), i64ptr(S.Ntgt), i64ptr(S.perm), 0), h)
+
+    # --- options
+    def options(self):
+        """The handle's pp_options as a dict (wait_timeout_us, fail_alloc_after, profile)."""
+        o = pp_options()
+        check(lib().pp_get_options(self._h, C.byref(o)), self._h)
+        return {k: getattr(o, k) for k, _ in pp_options._fields_ if k != "reserved"}
+
+    def set_options(self, **options):
+        """Change options (keywords as in pp_options); the others keep their values."""
+        cur = self.options()
+        cur.update(options)
+        check(lib().pp_set_options(self._h, C.byref(_options(cur))), self._h)
+        return self
 
     # --- lifecycle
     def close(self):

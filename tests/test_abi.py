@@ -77,3 +77,16 @@ def test_create_without_gpu_fails_loudly():
     assert not h.value
     with pytest.raises(pp.PPError):
         pp.B200SLU(pp.MinPlus(), np.float64, pp.ssymbolic(3, np.array([0, 1, 2, 3]), np.array([1, 2, 0])))
+
+
+def test_default_options():
+    """pp_default_options: the default wait bound (0 = 2 s), the allocation hook off, profiling off."""
+    L = pp.lib()
+    o = _lib.pp_options()
+    o.wait_timeout_us, o.fail_alloc_after, o.profile = 7, 7, 7
+    L.pp_default_options(C.byref(o))
+    assert (o.wait_timeout_us, o.fail_alloc_after, o.profile) == (0, -1, 0)
+    assert L.pp_get_options(None, C.byref(o)) == _lib.PP_EINVAL
+    assert L.pp_set_options(None, C.byref(o)) == _lib.PP_EINVAL
+    with pytest.raises(TypeError):
+        pp.api._options({"no_such_option": 1})

@@ -134,9 +134,18 @@ def test_plan_rejects_host_memory(gpu):
     S = pp.ssymbolic(n, cp, rv)
     F = pp.B200SLU(pp.MinPlus(), np.float64, S, device=0).assemble_csc(cp, rv, nz)
     try:
+        import ctypes as C
+
         B = torch.full((4, n), np.inf, dtype=torch.float64).T  # host tensor
-        with pytest.raises(pp.PPError) as e:
+        with pytest.raises(TypeError):  # the Python layer refuses it first
             F.plan_lmul(torch.from_numpy(nz).to("cuda:0"), B)
-        assert e.value.code == pp._lib.PP_EINVAL
+        # and the C ABI itself, given the host pointer
+        nz_d = torch.from_numpy(nz).to("cuda:0")
+        p = C.c_void_p()
+        L = pp.lib()
+        r = L.pp_plan_lmul(F._h, C.c_void_p(nz_d.data_ptr()), C.c_void_p(B.data_ptr()), C.c_void_p(B.data_ptr()),
+                           n, 4, C.byref(p))
+        assert r == pp._lib.PP_EINVAL and not p.value
+        assert b"memory of the handle's device" in L.pp_last_error(F._h)
     finally:
         F.close()

@@ -60,6 +60,7 @@ typedef struct pp_stats {
     double pairs_solve;         /* (x)(+) pairs of the last solve */
     int64_t device_bytes;       /* device memory held by the handle */
     int64_t kernel_launches;    /* kernels launched by the last call */
+    int64_t plan_fronts;        /* fronts of the device plan: fewer than nf where chains of top fronts are merged */
 } pp_stats;
 
 /* The library's version, major * 10000 + minor * 100 + patch. */
@@ -87,12 +88,16 @@ int32_t pp_create(int32_t device, pp_handle **h);
      fail_alloc_after  testing: when >= 0, that many device allocations of the handle succeed and the next
                        one fails as if the device were out of memory (the call returns PP_ENOMEM, having freed
                        nothing it still needs and leaked nothing); -1 (default) = off.
-     profile           1: per-launch timing (pp_set_profile). */
+     profile           1: per-launch timing (pp_set_profile).
+     merge_width       amalgamation: the largest residual of a front merged from a chain of top fronts (the
+                       reference's GPU amalgamation, ext/PATHPACKCUDAExt/chordal/amalgamate.jl); 0 = the
+                       default, 64; 1 = no merging.  Read by pp_set_structure.  The factor arrays a caller
+                       exchanges (pp_set_values, pp_get_factor) keep the caller's structure either way. */
 typedef struct pp_options {
     int64_t wait_timeout_us;
     int64_t fail_alloc_after;
     int32_t profile;
-    int32_t reserved;
+    int32_t merge_width;
 } pp_options;
 void pp_default_options(pp_options *opt);
 /* pp_create with options (opt may be NULL: the defaults). */

@@ -133,6 +133,18 @@ struct pp_handle {
     // d_err[2..3]) and the allocation test hook
     uint64_t wait_ns = 0;
     int64_t fail_alloc_after = -1;
+    // amalgamation: the caller's structure (0-based) and, when it has chains of top fronts to merge, the merged
+    // one the device plan is built from (every semiring but PlusProd); group maps a caller's front to its
+    // merged front.  The factor arrays on the device are in the plan's layout; pp_get_factor / pp_set_values
+    // convert at the boundary.
+    struct Structure {
+        int64_t n = 0, nf = 0, nB = 0;
+        std::vector<int64_t> R, Sp, St, Bp, Fp, Np, Nt, perm;
+    } orig, mrg;
+    std::vector<int> group;
+    std::vector<double> ufac_pairs, ufac_elems, usolve_pairs;
+    bool mergeable = false, merged = false;
+    int merge_width = 64;
 };
 
 // Makes the handle's allocation budget the one DevBuf::ensure consults for the rest of the enclosing call.
@@ -270,6 +282,7 @@ extern "C" void pp_default_options(pp_options *o) {
 
 static int32_t apply_options(pp_handle *h, const pp_options *o, const char *who) {
     if (o->wait_timeout_us < 0) return fail(h, PP_EINVAL, "%s: wait_timeout_us = %lld", who, (long long)o->wait_timeout_us);
+    if (o->merge_width < 0) return fail(h, PP_EINVAL, "%s: merge_width = %d", who, o->merge_width);
     if (o->wait_timeout_us > (int64_t)1 << 40) return fail(h, PP_EINVAL, "%s: wait_timeout_us too large", who);
     h->wait_ns = (uint64_t)o->wait_timeout_us * 1000u;
     h->fail_alloc_after = o->fail_alloc_after < 0 ? -1 : o->fail_alloc_after;
@@ -280,6 +293,7 @@ static int32_t apply_options(pp_handle *h, const pp_options *o, const char *who)
         CK(h, cudaMemcpy(h->d_err.as<int>() + 2, &h->wait_ns, sizeof(uint64_t), cudaMemcpyHostToDevice), who);
     }
     h->prof.on = o->profile != 0;
+    h->merge_width = o->merge_width == 0 ? 64 : o->merge_width;
     return PP_OK;
 }
 
@@ -310,6 +324,7 @@ extern "C" int32_t pp_get_options(const pp_handle *h, pp_options *opt) {
     opt->wait_timeout_us = (int64_t)(h->wait_ns / 1000u);
     opt->fail_alloc_after = h->fail_alloc_after;
     opt->profile = h->prof.on ? 1 : 0;
+    opt->merge_width = h->merge_width;
     return PP_OK;
 }
 
@@ -380,10 +395,17 @@ static std::vector<int> schedule_order(const std::vector<int> &fronts, const std
     return order;
 }
 
-extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, const int64_t *Rptr,
-                                    const int64_t *Sptr, const int64_t *Stgt, const int64_t *Bptr, const int64_t *Fptr,
-                                    const int64_t *Nptr, const int64_t *Ntgt, const int64_t *perm, int32_t base) {
-    AllocScope alloc_scope(h);
+// Unpadded algorithmic costs per front of a merged plan (see HostPlan::ufac_pairs).
+struct UCost {
+    std::vector<double> fpairs, felems, spairs;
+};
+
+// Check the structure and build the device plan from it (pp_set_structure's work).  uc: the unpadded costs
+// when the structure is a merged one.
+static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, const int64_t *Rptr,
+                               const int64_t *Sptr, const int64_t *Stgt, const int64_t *Bptr, const int64_t *Fptr,
+                               const int64_t *Nptr, const int64_t *Ntgt, const int64_t *perm, int32_t base,
+                               const UCost *uc) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_set_structure: null handle");
     if (n < 0 || nf < 0 || nB < 0 || (n > 0 && (nf < 1 || nB < 1)) || n >= INT32_MAX)
         return fail(h, PP_EINVAL, "pp_set_structure: sizes n=%lld nf=%lld nB=%lld", (long long)n, (long long)nf,
@@ -612,6 +634,17 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                 hp.stree_sep[r] = na;
             }
         }
+        if (uc) {
+            hp.ufac_pairs = uc->fpairs;
+            hp.ufac_elems = uc->felems;
+            hp.usolve_pairs = uc->spairs;
+        }
+        // (x)(+) pairs of one right-hand side through the L* (or U*) part of front f, unpadded
+        auto col_pairs = [&](int64_t f) {
+            if (!hp.usolve_pairs.empty()) return hp.usolve_pairs[f];
+            const double nn = hp.nn[f], na = hp.na[f];
+            return nn * (nn - 1) / 2 + nn * na;
+        };
         auto build_stages = [&](const std::vector<int> &stage_of, std::vector<Stage> &out, std::vector<int> &sfronts,
                                 std::vector<int> &sverts, std::vector<std::pair<int64_t, int>> &bfwd,
                                 std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost,
@@ -663,7 +696,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                     bc.res_rows += nn;
                     bc.sep_rows += na;
                     bc.blk_elems += nn * nn + nn * na;
-                    bc.pairs_col += nn * (nn - 1) / 2 + nn * na;
+                    bc.pairs_col += col_pairs(f);
                 }
                 fw.second = (int)(sfronts.size() - fw.first);
                 std::pair<int64_t, int> bw{(int64_t)sfronts.size(), 0};
@@ -690,7 +723,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
                     tc.res_rows += nn;
                     tc.sep_rows += na;
                     tc.blk_elems += nn * nn + nn * na;
-                    tc.pairs_col += nn * (nn - 1) / 2 + nn * na;
+                    tc.pairs_col += col_pairs(f);
                 }
                 tf.second = (int)(tentries.size() / 2 - tf.first);
                 std::pair<int64_t, int> tb{(int64_t)tentries.size() / 2, 0};
@@ -822,11 +855,12 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
         for (int64_t f = 0; f < nf; f++) {
             const double nn = h->hp.nn[f], na = h->hp.na[f], nj = nn + na;
             auto S2 = [](double m) { return (m - 1) * m * (2 * m - 1) / 6; };
-            pairs += S2(nj) - S2(na);
+            pairs += uc ? uc->fpairs[f] : S2(nj) - S2(na);
             mx = std::max<int64_t>(mx, (int64_t)nj);
         }
         s.pairs_factor = pairs;
         s.max_front = mx;
+        s.plan_fronts = nf;
     } catch (const std::bad_alloc &) {
         return fail(h, PP_ENOMEM, "pp_set_structure: out of host memory");
     }
@@ -835,9 +869,227 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
     return PP_OK;
 }
 
+// ---------------------------------------------------------------- amalgamation
+
+// Chains of top fronts merged into one front (a relaxed supernode partition of the same elimination order):
+// front c joins its parent f = c + 1 when c is f's last child (so the chain's residual vertices are
+// contiguous), both fronts are too large for the bottom kernels (nn + na > 64), the merged residual stays
+// within `nmax` vertices, and the zero padding the merge adds to the chain's columns, width x (na(f) -
+// |sep(c) & sep(f)|), stays within max(8, alpha x width x na(c)).  This is the join rule of the reference's
+// GPU amalgamation (ext/PATHPACKCUDAExt/chordal/amalgamate.jl:48-121), restricted to the top of the tree.
+// The merged front has the union of the residuals and the last member's separator; by the clique-tree
+// property every separator vertex of a member is in the merged residual or in that separator, so the
+// member's blocks are sub-blocks of the merged ones and the rest is the semiring's zero, which the (x)
+// absorbs: the partial LU of the merged front performs the members' operations on the same operands (plus
+// products with zero), and the factor entries are the members' (up to the order in which equal values meet
+// in (+), which can decide the sign of a zero).  Returns whether any front joined.
+static bool merge_chains(const pp_handle::Structure &o, int nmax, double alpha, pp_handle::Structure &m,
+                         std::vector<int> &group, UCost &uc) {
+    const int64_t n = o.n, nf = o.nf;
+    if (nf < 2) return false;
+    std::vector<int> idx(n), pnt(nf, -1);
+    for (int64_t f = 0; f < nf; f++)
+        for (int64_t v = o.R[f]; v < o.R[f + 1]; v++) idx[v] = (int)f;
+    auto nn = [&](int64_t f) { return o.R[f + 1] - o.R[f]; };
+    auto na = [&](int64_t f) { return o.Sp[f + 1] - o.Sp[f]; };
+    for (int64_t f = 0; f < nf; f++)
+        if (na(f) > 0) pnt[f] = idx[o.St[o.Sp[f]]];
+    std::vector<int64_t> width(nf);
+    std::vector<char> joins(nf, 0);
+    for (int64_t f = 0; f < nf; f++) width[f] = nn(f);
+    bool any = false;
+    for (int64_t f = 1; f < nf; f++) {
+        const int64_t c = f - 1;
+        if (pnt[c] != f || nn(c) + na(c) <= 64 || nn(f) + na(f) <= 64) continue;
+        const int64_t w = width[c] + nn(f);
+        if (w > nmax) continue;
+        int64_t common = 0;  // |sep(c) & sep(f)|, both sorted
+        for (int64_t a = o.Sp[c], b = o.Sp[f]; a < o.Sp[c + 1] && b < o.Sp[f + 1];) {
+            const int64_t x = o.St[a], y = o.St[b];
+            common += x == y;
+            a += x <= y;
+            b += y <= x;
+        }
+        const double zeros = (double)width[c] * (double)(na(f) - common);
+        if (zeros > std::max(8.0, alpha * (double)width[c] * (double)std::max<int64_t>(na(c), 1))) continue;
+        joins[c] = 1;
+        width[f] = w;
+        any = true;
+    }
+    if (!any) return false;
+    group.assign(nf, 0);
+    m.n = n;
+    m.nB = o.nB;
+    m.R.clear();
+    m.Sp.assign(1, 0);
+    m.St.clear();
+    int ng = 0;
+    for (int64_t f = 0, h0 = 0; f < nf; f++) {
+        group[f] = ng;
+        if (joins[f]) continue;
+        m.R.push_back(o.R[h0]);
+        m.St.insert(m.St.end(), o.St.begin() + o.Sp[f], o.St.begin() + o.Sp[f + 1]);
+        m.Sp.push_back((int64_t)m.St.size());
+        ng++;
+        h0 = f + 1;
+    }
+    m.R.push_back(n);
+    m.nf = ng;
+    m.Bp = o.Bp;
+    m.Fp.assign(o.nB + 1, ng);
+    for (int64_t c = 0; c < o.nB; c++) m.Fp[c] = o.Fp[c] < nf ? group[o.Fp[c]] : ng;
+    m.Np = o.Np;
+    m.Nt = o.Nt;
+    m.perm = o.perm;
+    auto S2 = [](double x) { return (x - 1) * x * (2 * x - 1) / 6; };
+    uc.fpairs.assign(ng, 0.0);
+    uc.felems.assign(ng, 0.0);
+    uc.spairs.assign(ng, 0.0);
+    for (int64_t f = 0; f < nf; f++) {
+        const double a = (double)nn(f), b = (double)na(f);
+        const int q = group[f];
+        uc.fpairs[q] += S2(a + b) - S2(b);
+        uc.felems[q] += 4.0 * (a * a + a * b) + b * b;
+        uc.spairs[q] += a * (a - 1) / 2 + a * b;
+        if (pnt[f] >= 0) uc.felems[group[pnt[f]]] += b * b;  // the parent reads this update matrix
+    }
+    return true;
+}
+
+// Build the device plan from the caller's structure (merged = false) or from its merged one; the counters
+// describe the caller's structure either way.
+static int32_t use_plan(pp_handle *h, bool merged) {
+    const pp_handle::Structure &s = merged ? h->mrg : h->orig;
+    UCost uc;
+    if (merged) {
+        uc.fpairs = h->ufac_pairs;
+        uc.felems = h->ufac_elems;
+        uc.spairs = h->usolve_pairs;
+    }
+    const int32_t r = build_structure(h, s.n, s.nf, s.nB, s.R.data(), s.Sp.data(), s.St.data(), s.Bp.data(),
+                                      s.Fp.data(), s.Np.data(), s.Nt.data(), s.perm.data(), 0, merged ? &uc : nullptr);
+    if (r != PP_OK) return r;
+    h->merged = merged;
+    h->st.plan_fronts = h->hp.nf;
+    h->st.nf = h->orig.nf;
+    h->st.nD = h->st.nL = 0;
+    for (int64_t f = 0; f < h->orig.nf; f++) {
+        const int64_t a = h->orig.R[f + 1] - h->orig.R[f], b = h->orig.Sp[f + 1] - h->orig.Sp[f];
+        h->st.nD += a * a;
+        h->st.nL += a * b;
+    }
+    return PP_OK;
+}
+
+extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, const int64_t *Rptr,
+                                    const int64_t *Sptr, const int64_t *Stgt, const int64_t *Bptr, const int64_t *Fptr,
+                                    const int64_t *Nptr, const int64_t *Ntgt, const int64_t *perm, int32_t base) {
+    AllocScope alloc_scope(h);
+    int32_t r = build_structure(h, n, nf, nB, Rptr, Sptr, Stgt, Bptr, Fptr, Nptr, Ntgt, perm, base, nullptr);
+    if (r != PP_OK) return r;
+    try {
+        // checked by build_structure: keep a 0-based copy
+        pp_handle::Structure &o = h->orig;
+        const int64_t b = base;
+        auto copy = [&](std::vector<int64_t> &dst, const int64_t *src, int64_t len) {
+            dst.resize(len);
+            for (int64_t i = 0; i < len; i++) dst[i] = src[i] - b;
+        };
+        o.n = n;
+        o.nf = nf;
+        o.nB = nB;
+        copy(o.R, Rptr, nf + 1);
+        copy(o.Sp, Sptr, nf + 1);
+        copy(o.St, Stgt, o.Sp[nf]);
+        copy(o.Bp, Bptr, nB + 1);
+        copy(o.Fp, Fptr, nB + 1);
+        copy(o.Np, Nptr, n + 1);
+        copy(o.Nt, Ntgt, o.Np[n]);
+        copy(o.perm, perm, n);
+        h->merged = false;
+        UCost uc;
+        h->mergeable = h->merge_width > 1 && merge_chains(o, h->merge_width, 0.5, h->mrg, h->group, uc);
+        if (h->mergeable) {
+            h->ufac_pairs = std::move(uc.fpairs);
+            h->ufac_elems = std::move(uc.felems);
+            h->usolve_pairs = std::move(uc.spairs);
+            r = use_plan(h, true);
+        } else {
+            h->group.clear();
+            h->mrg = pp_handle::Structure();
+        }
+    } catch (const std::bad_alloc &) {
+        h->have_structure = false;
+        return fail(h, PP_ENOMEM, "pp_set_structure: out of host memory");
+    }
+    if (r == PP_OK) ok(h);
+    return r;
+}
+
+// The bit pattern of the semiring's zero (the padding of merged blocks).
+static void zero_value(int sr, int dt, void *out) {
+    const bool lo = sr == PP_MINPLUS || sr == PP_MINMAX;  // +Inf
+    const bool hi = sr == PP_MAXPLUS || sr == PP_MAXMIN;  // -Inf
+    if (dt == PP_F32) {
+        const float v = lo ? INFINITY : hi ? -INFINITY : 0.0f;
+        memcpy(out, &v, 4);
+    } else if (dt == PP_F64) {
+        const double v = lo ? (double)INFINITY : hi ? -(double)INFINITY : 0.0;
+        memcpy(out, &v, 8);
+    } else {
+        const int32_t v = sr == PP_MINPLUS ? INT32_MAX : 0;
+        memcpy(out, &v, 4);
+    }
+}
+
+// Every entry of the caller's factor arrays with its place in the merged ones: fn(a, o, ma, mo) for array a
+// (0 LD, 1 UD, 2 LL, 3 UL) at offset o and merged array ma at offset mo.
+template <typename Fn>
+static void for_each_merged_entry(const pp_handle *h, Fn fn) {
+    const pp_handle::Structure &o = h->orig, &m = h->mrg;
+    const HostPlan &hp = h->hp;
+    int64_t Df = 0, Lf = 0;
+    for (int64_t f = 0; f < o.nf; f++) {
+        const int q = h->group[f];
+        const int64_t nn = o.R[f + 1] - o.R[f], na = o.Sp[f + 1] - o.Sp[f];
+        const int64_t off = o.R[f] - m.R[q], nnq = hp.nn[q], naq = hp.na[q], Dq = hp.dptr[q], Lq = hp.lptr[q];
+        for (int64_t j = 0; j < nn; j++)
+            for (int64_t i = 0; i < nn; i++) {
+                const int64_t a = Df + i + j * nn, b = Dq + (off + i) + (off + j) * nnq;
+                fn(0, a, 0, b);
+                fn(1, a, 1, b);
+            }
+        const int64_t *sq0 = m.St.data() + m.Sp[q], *sq1 = m.St.data() + m.Sp[q + 1];
+        for (int64_t r = 0; r < na; r++) {
+            const int64_t v = o.St[o.Sp[f] + r];
+            const bool inres = v < m.R[q + 1];
+            const int64_t row = inres ? v - m.R[q] : (int64_t)(std::lower_bound(sq0, sq1, v) - sq0);
+            for (int64_t j = 0; j < nn; j++) {
+                if (inres)
+                    fn(2, Lf + r + j * na, 0, Dq + row + (off + j) * nnq);
+                else
+                    fn(2, Lf + r + j * na, 2, Lq + row + (off + j) * naq);
+            }
+            for (int64_t i = 0; i < nn; i++) {
+                if (inres)
+                    fn(3, Lf + i + r * nn, 1, Dq + (off + i) + row * nnq);
+                else
+                    fn(3, Lf + i + r * nn, 3, Lq + (off + i) + row * nnq);
+            }
+        }
+        Df += nn * nn;
+        Lf += nn * na;
+    }
+}
+
 // Algorithmic traffic (elements) and (x)(+) pairs of one front's factorization: read the assembled blocks
 // and the children's update matrices, write the factor blocks and the update matrix; the partial LU's pairs.
 static void front_cost(const HostPlan &hp, int f, Cost &g) {
+    if (!hp.ufac_pairs.empty()) {
+        g.bytes += hp.ufac_elems[f];
+        g.pairs += hp.ufac_pairs[f];
+        return;
+    }
     const double nn = hp.nn[f], na = hp.na[f], nj = nn + na;
     double e = 4.0 * (nn * nn + nn * na) + na * na;
     for (int c = hp.chdptr[f]; c < hp.chdptr[f + 1]; c++) {
@@ -1039,6 +1291,14 @@ static int32_t set_semiring(pp_handle *h, int32_t sr, int32_t dt, const char *wh
     h->nnz_assembled = -1;  // pp_update_values needs the pattern of a completed pp_assemble
     const Ops *o = get_ops(sr, dt);
     if (!o) return fail(h, PP_EUNSUPPORTED, "%s: semiring %d with element type %d is not supported", who, sr, dt);
+    // merged fronts for every semiring whose zero absorbs in (x): not PlusProd, where 0 * Inf is NaN and a
+    // padded zero times a divergent star would reach entries of the caller's structure
+    const bool want_merged = h->mergeable && sr != PP_PLUSPROD;
+    if (want_merged != h->merged) {
+        h->ops = nullptr;
+        const int32_t r = use_plan(h, want_merged);
+        if (r != PP_OK) return r;
+    }
     if (h->ops != o) {
         h->ops = o;
         h->ws_esize = 0;
@@ -1185,8 +1445,38 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
     if (r != PP_OK) return r;
     const size_t es = h->ops->esize;
     cudaStream_t st = h->stream;
-    if ((h->nD > 0 && (!LD || !UD)) || (h->nL > 0 && (!LL || !UL)) || (h->hp.nN > 0 && !Nval))
+    if ((h->st.nD > 0 && (!LD || !UD)) || (h->st.nL > 0 && (!LL || !UL)) || (h->hp.nN > 0 && !Nval))
         return fail(h, PP_EINVAL, "pp_set_values: null array");
+    if (h->merged) {
+        // the caller's blocks placed into zero-filled merged blocks on the host, then uploaded
+        std::vector<unsigned char> m[4];
+        const void *srcs[4] = {LD, UD, LL, UL};
+        DevBuf *dst[4] = {&h->LD, &h->UD, &h->LL, &h->UL};
+        unsigned char zero[8];
+        zero_value(semiring, dtype, zero);
+        try {
+            for (int a = 0; a < 4; a++) {
+                const size_t len = (size_t)std::max<int64_t>(a < 2 ? h->nD : h->nL, 1);
+                m[a].resize(es * len);
+                for (size_t i = 0; i < len; i++) memcpy(m[a].data() + es * i, zero, es);
+            }
+        } catch (const std::bad_alloc &) {
+            return fail(h, PP_ENOMEM, "pp_set_values: out of host memory");
+        }
+        for_each_merged_entry(h, [&](int a, int64_t o, int ma, int64_t mo) {
+            memcpy(m[ma].data() + es * mo, static_cast<const unsigned char *>(srcs[a]) + es * o, es);
+        });
+        for (int a = 0; a < 4; a++)
+            if (a < 2 ? h->nD : h->nL)
+                CK(h, cudaMemcpyAsync(dst[a]->p, m[a].data(), es * (a < 2 ? h->nD : h->nL), cudaMemcpyHostToDevice, st),
+                   "pp_set_values");
+        if (h->hp.nN) CK(h, cudaMemcpyAsync(h->Nval.p, Nval, es * h->hp.nN, cudaMemcpyHostToDevice, st), "pp_set_values");
+        CK(h, cudaStreamSynchronize(st), "pp_set_values");
+        h->have_values = true;
+        h->factored = false;
+        ok(h);
+        return PP_OK;
+    }
     if (h->nD) CK(h, cudaMemcpyAsync(h->LD.p, LD, es * h->nD, cudaMemcpyHostToDevice, st), "pp_set_values");
     if (h->nD) CK(h, cudaMemcpyAsync(h->UD.p, UD, es * h->nD, cudaMemcpyHostToDevice, st), "pp_set_values");
     if (h->nL) CK(h, cudaMemcpyAsync(h->LL.p, LL, es * h->nL, cudaMemcpyHostToDevice, st), "pp_set_values");
@@ -1261,6 +1551,28 @@ extern "C" int32_t pp_get_factor(pp_handle *h, void *LD, void *LL, void *UD, voi
     CK(h, cudaSetDevice(h->device), "pp_get_factor");
     const size_t es = h->ops->esize;
     cudaStream_t st = h->stream;
+    if (h->merged) {
+        // the merged blocks to the host, then each of the caller's entries from its place in them
+        std::vector<unsigned char> m[4];
+        void *dst[4] = {LD, UD, LL, UL};
+        const DevBuf *src[4] = {&h->LD, &h->UD, &h->LL, &h->UL};
+        try {
+            for (int a = 0; a < 4; a++) m[a].resize(es * (size_t)std::max<int64_t>(a < 2 ? h->nD : h->nL, 1));
+        } catch (const std::bad_alloc &) {
+            return fail(h, PP_ENOMEM, "pp_get_factor: out of host memory");
+        }
+        for (int a = 0; a < 4; a++)
+            if (dst[a] && (a < 2 ? h->nD : h->nL))
+                CK(h, cudaMemcpyAsync(m[a].data(), src[a]->p, es * (a < 2 ? h->nD : h->nL), cudaMemcpyDeviceToHost, st),
+                   "pp_get_factor");
+        const int32_t r = settle(h, "pp_get_factor");
+        if (r != PP_OK) return r;
+        for_each_merged_entry(h, [&](int a, int64_t o, int ma, int64_t mo) {
+            if (dst[a]) memcpy(static_cast<unsigned char *>(dst[a]) + es * o, m[ma].data() + es * mo, es);
+        });
+        ok(h);
+        return PP_OK;
+    }
     if (LD && h->nD) CK(h, cudaMemcpyAsync(LD, h->LD.p, es * h->nD, cudaMemcpyDeviceToHost, st), "pp_get_factor");
     if (UD && h->nD) CK(h, cudaMemcpyAsync(UD, h->UD.p, es * h->nD, cudaMemcpyDeviceToHost, st), "pp_get_factor");
     if (LL && h->nL) CK(h, cudaMemcpyAsync(LL, h->LL.p, es * h->nL, cudaMemcpyDeviceToHost, st), "pp_get_factor");
@@ -1273,6 +1585,10 @@ extern "C" int32_t pp_get_factor(pp_handle *h, void *LD, void *LL, void *UD, voi
 
 static double solve_pairs_per_rhs(const HostPlan &hp) {
     double s = 0;
+    if (!hp.usolve_pairs.empty()) {
+        for (double x : hp.usolve_pairs) s += 2 * x;
+        return s + (double)hp.nN;
+    }
     for (int f = 0; f < hp.nf; f++) {
         const double nn = hp.nn[f], na = hp.na[f];
         s += nn * (nn - 1) + 2 * nn * na;

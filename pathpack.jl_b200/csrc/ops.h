@@ -144,6 +144,10 @@ struct HostPlan {
     int early_sub[2] = {0, 0}, early_bot[2] = {0, 0};
     int64_t sync_cap = 0;              // ints allocated at d_sync
     int sm_count = 148;
+    // algorithmic cost per front of the caller's (unpadded) structure, summed over the members of a merged
+    // front (empty: the plan's fronts are the caller's): factorization (x)(+) pairs and elements moved, and the
+    // (x)(+) pairs of one right-hand side through L* (or U*)
+    std::vector<double> ufac_pairs, ufac_elems, usolve_pairs;
 };
 
 struct Values {

@@ -27,12 +27,13 @@ class pp_stats(C.Structure):
     _fields_ = [("n", C.c_int64), ("nf", C.c_int64), ("nB", C.c_int64), ("nlevels", C.c_int64),
                 ("nD", C.c_int64), ("nL", C.c_int64), ("nN", C.c_int64), ("max_front", C.c_int64),
                 ("pairs_factor", C.c_double), ("ms_factor", C.c_double), ("ms_solve", C.c_double),
-                ("pairs_solve", C.c_double), ("device_bytes", C.c_int64), ("kernel_launches", C.c_int64)]
+                ("pairs_solve", C.c_double), ("device_bytes", C.c_int64), ("kernel_launches", C.c_int64),
+                ("plan_fronts", C.c_int64)]
 
 
 class pp_options(C.Structure):
     _fields_ = [("wait_timeout_us", C.c_int64), ("fail_alloc_after", C.c_int64), ("profile", C.c_int32),
-                ("reserved", C.c_int32)]
+                ("merge_width", C.c_int32)]
 
 
 class pp_kernel_class(C.Structure):

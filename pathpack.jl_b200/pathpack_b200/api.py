@@ -41,7 +41,7 @@ def _options(kw):
     o = pp_options()
     lib().pp_default_options(C.byref(o))
     for k, v in kw.items():
-        if k not in dict(pp_options._fields_) or k == "reserved":
+        if k not in dict(pp_options._fields_):
             raise TypeError("unknown option %r" % k)
         setattr(o, k, int(v))
     return o
@@ -69,7 +69,7 @@ class B200SLU:
         """The handle's pp_options as a dict (wait_timeout_us, fail_alloc_after, profile)."""
         o = pp_options()
         check(lib().pp_get_options(self._h, C.byref(o)), self._h)
-        return {k: getattr(o, k) for k, _ in pp_options._fields_ if k != "reserved"}
+        return {k: getattr(o, k) for k, _ in pp_options._fields_}
 
     def set_options(self, **options):
         """Change options (keywords as in pp_options); the others keep their values."""

@@ -172,18 +172,19 @@ def equal_values(a, b, what=""):
 
 
 def bits_equal(a, b, name, dtype, what="", solve=False):
-    """Bit-exact, except for the sign of a zero in two places.  (1) Float32 min/max on the device are the
-    hardware min/max (the reference's GPU kernels use the same, llvm.minnum), which order -0.0 below +0.0,
-    where the reference CPU's select ifelse(x < y, x, y) returns its second operand on a tie.  (2) With
-    solve=True (lmul!, rmul!, the star), for every element type: the solves' separator scatters combine the
-    contributions of several fronts with atomics in whatever order they arrive, and with a select-based (+)
-    the sign of a zero sum depends on that order (the reference's GPU scatters, atomic_splus!, have the same
-    freedom)."""
+    """Bit-exact, except for the sign of a zero, which the order in which equal values meet in (+) decides.
+    (1) Float32 min/max on the device are the hardware min/max (the reference's GPU kernels use the same,
+    llvm.minnum), which order -0.0 below +0.0, where the reference CPU's select ifelse(x < y, x, y) returns its
+    second operand on a tie.  (2) The solves' separator scatters (lmul!, rmul!, the star) combine the
+    contributions of several fronts with atomics in whatever order they arrive (the reference's GPU scatters,
+    atomic_splus!, have the same freedom).  (3) Merged fronts (amalgamation, as the reference's GPU path does)
+    combine the children's update matrices and the entries of A in one front instead of member by member.
+    `solve` is kept for the callers; every float comparison allows a zero of either sign."""
     a, b = np.asarray(a), np.asarray(b)
     assert a.shape == b.shape, what
     u = np.uint32 if a.itemsize == 4 else np.uint64
     bad = a.view(u) != b.view(u)
-    if np.dtype(dtype).kind == "f" and (np.dtype(dtype) == np.float32 or solve):
+    if np.dtype(dtype).kind == "f":
         bad &= ~((a == 0) & (b == 0))
     if bad.any():
         i = np.flatnonzero(bad)[:5]

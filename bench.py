@@ -18,15 +18,18 @@ path: assembly of A into the factor (copyto!), the multifrontal factorization (l
   pairs  algorithmic: the partial LU of every front, sum_f sum_{t=na}^{nj-1} t^2, plus lmul!'s L* on the root
          paths of the 256 unit sources and U* over every front for all 256 columns (unpadded structure).
 
-Multi-GPU (--gpus N under torchrun): each rank factors and solves its own independent instance (weak scaling,
-no collective on the data path); value = all ranks' pairs / the slowest rank's time.
+Multi-GPU (--gpus N under torchrun): one job on all ranks (strong scaling).  Every rank builds the same matrix;
+the factorization is split (each rank factors its part of the bottom of the tree, NCCL broadcasts on the
+library's stream give every rank the other parts, every rank factors the top), and each rank solves its own
+column panel of B (256 / N columns); value = the job's pairs (the factorization once, every column's solve) /
+the slowest rank's time.
 
 --impl reference runs the reference's CPU algorithm (the oracle: the C restatement of PATHPACK.jl's CPU path,
 oracle/; Julia is not available here) on the host cores, on the same workload; rank 0 only.
 
 The default line also carries "mstar": config 4's mstar (mlu + Matrix(F), F32 MinPlus, directed 6-NN graph of
 32,768 points, 4.3 GB of output) with its columns split into one contiguous panel per rank: wall seconds per
-mstar at N GPUs (strong scaling; the factor is replicated, no collective on the data path).
+mstar at N GPUs (strong scaling; the factorization split as above, then one column panel of A* per rank).
 
 --workload selects another BASELINE configuration instead, printing one line of the same form:
   config1, config3, config4   mlu + the whole star Matrix(F) as column panels over the ranks (device output;
@@ -233,7 +236,7 @@ def run_reference(args, rank, world):
     v = pairs * args.steps / tot
     line = {"impl": "reference", "metric": "(x)(+) pairs/s in mlu + lmul! (config 2)", "value": v,
             "unit": "pairs/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f64", "data": "synthetic (seeded, config 2 shapes)",
             "config": {"workload": w["name"], "semiring": "MinPlus", "n": w["n"], "nrhs": w["k"]},
             "cpu_baseline": {"value": v, "unit": "pairs/s", "cores": threads, "kind": "port",
@@ -273,14 +276,28 @@ def run_ours(args, rank, world, local):
         import torch.distributed as tdist
     dev = local
     torch.cuda.set_device(dev)
-    w = config2(rank)
+    from pathpack_b200.panels import column_panels, join_group
+
+    # one job on all ranks (strong scaling): the same matrix and right-hand sides everywhere; the factorization
+    # is split (every rank factors its part of the bottom of the tree, NCCL broadcasts exchange the parts, every
+    # rank factors the top) and each rank solves its own column panel of B
+    w = config2(0)
     n, k = w["n"], w["k"]
-    F = pp.B200SLU(pp.MinPlus(), np.float64, w["S"], device=dev)
+    pc0, kw = column_panels(k, world)[rank]
+    S = w["S"]
+    F = pp.B200SLU(pp.MinPlus(), np.float64, S, device=dev)
+    if dist:
+        join_group(F)
     F.assemble_csc(w["cp"], w["rv"], w["nz"]).factor()
     stream = torch.cuda.ExternalStream(F.stream(), device=dev)
     nz_d = torch.from_numpy(w["nz"]).to(f"cuda:{dev}")
-    B0 = torch.from_numpy(np.ascontiguousarray(w["B"].T)).to(f"cuda:{dev}")  # (k, n): column-major n x k
+    B0 = torch.from_numpy(np.ascontiguousarray(w["B"][:, pc0:pc0 + kw].T)).to(f"cuda:{dev}")  # (kw, n): n x kw
     Bw = torch.empty_like(B0)
+    # this rank's algorithmic pairs: the factorization once for the job (rank 0), lmul! of its columns
+    nn_, na_ = S.nn.astype(np.float64), S.na.astype(np.float64)
+    u_full = float((nn_ * (nn_ - 1) / 2 + nn_ * na_).sum())
+    src = np.array([int(np.flatnonzero(w["B"][:, c] == 0.0)[0]) for c in range(pc0, pc0 + kw)], dtype=np.int64)
+    pairs_rank = (w["pairs_factor"] if rank == 0 else 0.0) + S.rootpath_pairs(S.invp[src]) + kw * u_full
 
     def step_calls():
         # the step as separate C-ABI calls, everything enqueued on the library's stream (no host wait)
@@ -290,14 +307,25 @@ def run_ours(args, rank, world, local):
             Bw.copy_(B0)
         F._solve(Bw.T, True, sync=False)
 
-    # the timed step: the same calls captured once as a CUDA graph by the library (pp_plan_lmul: re-assembly
-    # from the device weights, factorization, lmul! of B0 into Bw), so that one graph launch enqueues the
-    # whole step and the host's speed does not enter the device time
-    plan = F.plan_lmul(nz_d, B0.T, Bw.T)
-    launches_per_step = plan.launches
+    if dist:
+        # joined handles run call by call (the factorization's broadcasts are not captured into a graph)
+        plan = None
+        F.factor()
+        launches_per_step = 6 + F.stats()["kernel_launches"]
+        F._solve(Bw.T, True)
+        launches_per_step += F.stats()["kernel_launches"]
 
-    def step():
-        plan.launch()
+        def step():
+            step_calls()
+    else:
+        # the timed step: the same calls captured once as a CUDA graph by the library (pp_plan_lmul: re-assembly
+        # from the device weights, factorization, lmul! of B0 into Bw), so that one graph launch enqueues the
+        # whole step and the host's speed does not enter the device time
+        plan = F.plan_lmul(nz_d, B0.T, Bw.T)
+        launches_per_step = plan.launches
+
+        def step():
+            plan.launch()
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     gidx = int(vis.split(",")[dev]) if vis else dev
@@ -342,13 +370,13 @@ def run_ours(args, rank, world, local):
         t = torch.tensor([ms], device=f"cuda:{dev}")
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         ms = float(t.item())
-    pairs = w["pairs_factor"] + w["pairs_solve"]
-    value = pairs * world * args.steps / (ms / 1e3)
+    pairs = _sum_over_ranks(pairs_rank, dev, world)  # = pairs_factor + pairs_solve of the one job
+    value = pairs * args.steps / (ms / 1e3)
 
     # e2e: host CSC + pinned host B through the C ABI, H2D and D2H inside each timed step
-    Bh = torch.empty((k, n), dtype=torch.float64, pin_memory=True)
+    Bh = torch.empty((kw, n), dtype=torch.float64, pin_memory=True)
     Bh_np = Bh.numpy()
-    Bsrc = np.ascontiguousarray(w["B"].T)
+    Bsrc = np.ascontiguousarray(w["B"][:, pc0:pc0 + kw].T)
     e2e_t = 0.0
     e2e_steps = []
     for it in range(args.warmup + args.steps):
@@ -365,8 +393,8 @@ def run_ours(args, rank, world, local):
         t = torch.tensor([e2e_t], device=f"cuda:{dev}")
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         e2e_t = float(t.item())
-    h2d = w["nz"].nbytes + n * k * 8
-    d2h = n * k * 8
+    h2d = w["nz"].nbytes + n * kw * 8  # per rank
+    d2h = n * kw * 8
 
     # roofline of the dominant kernel class, measured with CUDA events on the library's stream over K steps
     F.set_profile(True)
@@ -408,7 +436,7 @@ def run_ours(args, rank, world, local):
         ms4 = measure_star("config4", rank, world, dev, max(3, args.steps // 2), args.warmup, e2e=False)
         mstar = {"workload": STAR["config4"]["name"], "wall_s": ms4["wall_s"], "value": ms4["value"],
                  "unit": "pairs/s", "n_gpus": world, "scaling": "strong",
-                 "parallelism": "column panels of A* (factor replicated)", "columns_per_rank": ms4["columns_per_rank"],
+                 "parallelism": ms4["parallelism"], "columns_per_rank": ms4["columns_per_rank"],
                  "pairs_per_step": ms4["pairs_per_step"], "output": "device-resident",
                  "symbolic_s_host": ms4["symbolic_s"], "clocks": ms4["clocks"]}
 
@@ -419,34 +447,40 @@ def run_ours(args, rank, world, local):
             threads = os.cpu_count() or 1
             dt, Xc = cpu_baseline(w, threads)
             # the device result of the last step against the oracle (bit-exact for MinPlus)
-            got = Bw.T.cpu().numpy()
+            got = Bw.T.cpu().numpy()  # the whole of B at N = 1
             cpu = {"value": pairs / dt, "unit": "pairs/s", "cores": threads, "kind": "port",
                    "sample": "one full config-2 step (assembly + factorization + lmul!) with the oracle/ C "
                              "restatement on %d threads; Julia is not installed" % threads,
                    "seconds": dt, "matches_device_bitwise": bool(np.array_equal(got, Xc))}
         line = {"metric": "(x)(+) pairs/s in mlu + lmul! (config 2)", "value": value, "unit": "pairs/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
                 "data": "synthetic (seeded; config 2 shapes: 256x256 grid digraph, U[1,10) weights, unit columns)",
                 "config": {"workload": w["name"], "semiring": "MinPlus", "n": n, "nrhs": k, "nf": w["S"].nf,
-                           "pairs_per_step_per_gpu": pairs, "pairs_factor": w["pairs_factor"],
-                           "pairs_solve": w["pairs_solve"], "parallelism": "independent instance per GPU",
+                           "pairs_per_step": pairs, "pairs_factor": w["pairs_factor"],
+                           "pairs_solve": w["pairs_solve"], "columns_per_rank": [c for _, c in column_panels(k, world)],
+                           "parallelism": ("one GPU" if world == 1 else
+                                           "one job: the bottom of the tree split over the GPUs (its parts "
+                                           "exchanged by NCCL broadcasts), the top factored on every GPU, B split "
+                                           "into column panels"),
                            "l2": "inputs larger than L2 (B 134 MB + factor + workspace)"},
-                "e2e": {"value": pairs * world * args.steps / e2e_t, "unit": "pairs/s", "h2d_bytes_per_step": h2d,
+                "e2e": {"value": pairs * args.steps / e2e_t, "unit": "pairs/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * e2e_t / args.steps,
                         "step_ms_min": min(e2e_steps), "step_ms_median": float(np.median(e2e_steps)),
                         "clock": "host wall clock per step (perf_counter), summed over the K steps"},
                 "step_ms": {"median": float(np.median(step_ms)), "min": min(step_ms), "max": max(step_ms),
                             "clock": "CUDA events on the library's stream around each timed step",
-                            "step": "one launch of the library's captured plan (pp_plan_lmul): re-assembly, "
-                                    "factorization, lmul!",
+                            "step": ("one launch of the library's captured plan (pp_plan_lmul): re-assembly, "
+                                     "factorization, lmul!" if world == 1 else
+                                     "the C-ABI calls: re-assembly, split factorization, lmul! of the rank's panel"),
                             "call_by_call_ms_per_step": calls_ms},
                 "enqueue_ms": {"median": float(np.median(enqueue_ms)), "max": max(enqueue_ms),
                                "clock": "host perf_counter around enqueueing each timed step"},
                 "gpu_launches": launches, "roofline": roof, "kernels": kernels, "clocks": clocks,
                 "cpu_baseline": cpu, "mstar": mstar}
         print(json.dumps(line), flush=True)
-    plan.close()
+    if plan is not None:
+        plan.close()
     F.close()
 
 
@@ -511,6 +545,10 @@ def measure_star(key, rank, world, dev, steps, warmup, e2e=True, cpu=False, w=No
     if columns:  # a smaller case of the same kernels (profiling captures): the first columns of the panel
         ncols = min(ncols, int(columns))
     F = pp.B200SLU(sr, w["dtype"], S, device=dev)
+    if world > 1:  # the factorization split over the ranks (NCCL), every rank ends with the whole factor
+        from pathpack_b200.panels import join_group
+
+        join_group(F)
     F.assemble_csc(w["cp"], w["rv"], w["nz"]).factor()
     stream = torch.cuda.ExternalStream(F.stream(), device=dev)
     nz_d = torch.from_numpy(w["nz"]).to(f"cuda:{dev}")
@@ -546,12 +584,14 @@ def measure_star(key, rank, world, dev, steps, warmup, e2e=True, cpu=False, w=No
         torch.cuda.synchronize(dev)
         F.sync()
     ms = _max_over_ranks(e0.elapsed_time(e1), dev, world)
-    pairs_rank = w["pairs_factor"] + star_pairs(w, col0, ncols)
-    pairs = _sum_over_ranks(pairs_rank, dev, world)  # every rank factors: its pairs count
+    pairs_rank = (w["pairs_factor"] if rank == 0 else 0.0) + star_pairs(w, col0, ncols)
+    pairs = _sum_over_ranks(pairs_rank, dev, world)  # the job's factorization once, every rank's columns
     r = {"ms_per_step": ms / steps, "wall_s": ms / steps / 1e3, "pairs_per_step": pairs,
          "value": pairs * steps / (ms / 1e3), "launches": launches * steps, "clocks": clk.summary(),
          "columns_per_rank": [min(c, int(columns)) if columns else c for _, c in column_panels(n, world)],
-         "symbolic_s": w["symbolic_s"]}
+         "symbolic_s": w["symbolic_s"],
+         "parallelism": ("one GPU" if world == 1 else "the bottom of the tree split over the GPUs (NCCL broadcasts), "
+                         "the top factored on every GPU, column panels of A*")}
     if e2e:
         # host weights in, the rank's panel of the star out into pinned host memory, both inside the call
         host = torch.empty((max(ncols, 1), n), dtype=tdt, pin_memory=True)

@@ -92,12 +92,16 @@ int32_t pp_create(int32_t device, pp_handle **h);
      merge_width       amalgamation: the largest residual of a front merged from a chain of top fronts (the
                        reference's GPU amalgamation, ext/PATHPACKCUDAExt/chordal/amalgamate.jl); 0 = the
                        default, 64; 1 = no merging.  Read by pp_set_structure.  The factor arrays a caller
-                       exchanges (pp_set_values, pp_get_factor) keep the caller's structure either way. */
+                       exchanges (pp_set_values, pp_get_factor) keep the caller's structure either way.
+     trace             1: record the timeline of the top of the tree's factorization, task by task
+                       (pp_get_trace). */
 typedef struct pp_options {
     int64_t wait_timeout_us;
     int64_t fail_alloc_after;
     int32_t profile;
     int32_t merge_width;
+    int32_t trace;
+    int32_t reserved;
 } pp_options;
 void pp_default_options(pp_options *opt);
 /* pp_create with options (opt may be NULL: the defaults). */
@@ -170,6 +174,24 @@ int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols,
 /* Wait for the handle's stream; reports a device error of the calls enqueued since the last wait. */
 int32_t pp_sync(pp_handle *h);
 
+/* ---- several GPUs: one handle per GPU (a process or thread each), joined into a group over NCCL ----
+   The multi-GPU factorization of the reference (ext/PATHPACKCUDAExt/multigpu.jl:372-470 replicates the
+   factor by peer copies; here the factorization itself is split).  Every rank sets the same structure and
+   assembles the same matrix; then pp_factor on a joined handle factors only this rank's part of the bottom of
+   the tree (maximal subtrees of small fronts, dealt to the ranks in runs of about equal estimated time), gives
+   every rank the other parts with NCCL broadcasts on the handle's stream (the factor blocks and the children's
+   update matrices, over NVLink), and factors the top of the tree on every rank, so that each rank ends with the
+   whole factor and solves or computes star columns on its own (split the right-hand sides or the star's
+   columns across the ranks).  Every rank must call pp_factor the same number of times (a collective).  NCCL
+   (libnccl.so.2) is loaded when first needed.  A host wait on a joined handle's streams gives up after 60 s
+   (30 x wait_timeout_us when that is set), aborts the communicator and reports PP_EDEVICE; the handle has
+   then left the group (PP_ESTATE from the next pp_factor).  Plans (pp_plan_lmul) stay single-GPU. */
+#define PP_COMM_ID_BYTES 128
+/* A new group id (PP_COMM_ID_BYTES bytes): made on one rank and sent to the others. */
+int32_t pp_comm_id(void *id);
+/* Join the handle as `rank` of `nranks` (nranks = 1 leaves any group); blocks until every rank has joined. */
+int32_t pp_comm_init(pp_handle *h, const void *id, int32_t nranks, int32_t rank);
+
 /* ---- lmul! allocating nothing (no counterpart in the reference) ----
    pp_lmul_static is pp_lmul for device-resident B (n x k, leading dimension ldb, on the handle's device) that
    allocates nothing: no device memory, no host staging, no profiler events.  It is for callers that must not
@@ -209,6 +231,14 @@ int32_t pp_plan_launch(pp_plan *plan);
 /* kernels one launch of the plan runs */
 int32_t pp_plan_launches(const pp_plan *plan, int64_t *launches);
 int32_t pp_plan_destroy(pp_plan *plan);
+
+/* The timeline of the last factorization's top of the tree (pp_options.trace = 1): PP_TRACE_WORDS words per
+   tile task, in the order the tasks were listed: global timer in ns when the task was taken, when its tile was
+   assembled, when its products with the pivot blocks were done and when it was published; the SM and front,
+   (sm << 32) | front of the device plan; the tile, (I << 32) | J.  Copies at most max_tasks tasks, sets
+   *ntasks to the number of tasks. */
+#define PP_TRACE_WORDS 6
+int32_t pp_get_trace(pp_handle *h, uint64_t *out, int64_t max_tasks, int64_t *ntasks);
 
 /* Counters of the handle (sizes, pair counts, device times of the last calls). */
 int32_t pp_get_stats(pp_handle *h, pp_stats *s);

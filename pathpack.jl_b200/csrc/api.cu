@@ -6,7 +6,13 @@
 // conventions follow the reference's typed errors (check_semiring, ext/PATHPACKCUDAExt/runtime/config.jl:359-377;
 // the memory check before any work, api.jl:1031-1045; freeing everything on failure, api.jl:141-147).
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <algorithm>
+#include <chrono>
+#include <mutex>
+#include <thread>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -57,6 +63,54 @@ using namespace pp;
 
 static thread_local std::string g_err;
 
+// NCCL, for handles joined into a group of GPUs (pp_comm_init): loaded on first use with dlopen, so that the
+// library itself loads and runs without it (nccl.h gives the types only).  A process that already holds
+// libnccl.so.2 (PyTorch's, for instance) shares that copy.
+struct NcclApi {
+    bool ok = false;
+    std::string why;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*Broadcast)(const void *, void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    const char *(*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+static const NcclApi &nccl_api() {
+    static const NcclApi api = [] {
+        NcclApi a;
+        void *lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) lib = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) {
+            const char *e = dlerror();
+            a.why = std::string("libnccl.so.2 could not be loaded: ") + (e ? e : "?");
+            return a;
+        }
+        bool all = true;
+        auto sym = [&](auto &fn, const char *name) {
+            fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(lib, name));
+            all = all && fn;
+        };
+        sym(a.GetUniqueId, "ncclGetUniqueId");
+        sym(a.CommInitRank, "ncclCommInitRank");
+        sym(a.CommDestroy, "ncclCommDestroy");
+        sym(a.CommAbort, "ncclCommAbort");
+        sym(a.CommGetAsyncError, "ncclCommGetAsyncError");
+        sym(a.Broadcast, "ncclBroadcast");
+        sym(a.GroupStart, "ncclGroupStart");
+        sym(a.GroupEnd, "ncclGroupEnd");
+        sym(a.GetErrorString, "ncclGetErrorString");
+        a.ok = all;
+        if (!all) a.why = "libnccl.so.2 lacks a function the library needs";
+        return a;
+    }();
+    return api;
+}
+
 // The allocation budget of the handle whose call is running on this thread (pp_options.fail_alloc_after):
 // when it is >= 0, the allocation that finds it at 0 fails as if the device were out of memory.
 static thread_local int64_t *t_alloc_budget = nullptr;
@@ -86,6 +140,13 @@ struct DevBuf {
     U *as() const {
         return static_cast<U *>(p);
     }
+};
+
+// A rank's part of the bottom of the tree (several GPUs): fronts [f0, f1) and the element ranges of their
+// diagonal blocks (LD, UD), off-diagonal blocks (LL, UL) and workspace.
+struct Part {
+    int f0 = 0, f1 = 0;
+    int64_t d0 = 0, d1 = 0, l0 = 0, l1 = 0, w0 = 0, w1 = 0;
 };
 
 struct pp_handle {
@@ -145,6 +206,16 @@ struct pp_handle {
     std::vector<double> ufac_pairs, ufac_elems, usolve_pairs;
     bool mergeable = false, merged = false;
     int merge_width = 64;
+    bool trace_on = false;  // pp_options.trace
+    DevBuf d_trace;
+    // several GPUs (pp_comm_init): the NCCL communicator, this handle's rank, and every rank's part of the
+    // bottom of the tree (element ranges of LD/UD, LL/UL and the workspace)
+    void *comm = nullptr;
+    int nranks = 1, rank = 0;
+    bool comm_failed = false;
+    double comm_wait_s = 60.0;  // bound of a host wait on the handle's streams while joined (seconds)
+    std::string comm_msg;       // an NCCL failure met while enqueueing
+    std::vector<Part> parts;
 };
 
 // Makes the handle's allocation budget the one DevBuf::ensure consults for the rest of the enclosing call.
@@ -179,6 +250,29 @@ static int32_t cuda_fail(pp_handle *h, cudaError_t e, const char *what) {
 static void ok(pp_handle *h) {
     g_err.clear();
     if (h) h->err.clear();
+}
+
+// Wait for a stream of the handle.  Joined into a group of GPUs, a collective whose peers never arrive would
+// block for good: then the stream is polled, and after the group's bound (comm_wait_s) the communicator is
+// aborted, which ends its collectives; the call reports cudaErrorLaunchTimeout and the handle leaves the group.
+static cudaError_t stream_wait(pp_handle *h, cudaStream_t s) {
+    if (!h->comm) return cudaStreamSynchronize(s);
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e != cudaErrorNotReady) return e;
+        ncclResult_t ae = ncclSuccess;
+        const NcclApi &N = nccl_api();
+        if (N.CommGetAsyncError(static_cast<ncclComm_t>(h->comm), &ae) != ncclSuccess || ae != ncclSuccess ||
+            std::chrono::steady_clock::now() - t0 > std::chrono::duration<double>(h->comm_wait_s)) {
+            N.CommAbort(static_cast<ncclComm_t>(h->comm));
+            h->comm = nullptr;
+            h->comm_failed = true;
+            cudaStreamSynchronize(s);
+            return cudaErrorLaunchTimeout;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
 }
 
 template <typename U>
@@ -243,7 +337,12 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
     if (!h) return PP_OK;
     // best effort: the handle is released whatever the device's state
     if (cudaSetDevice(h->device) != cudaSuccess) cudaGetLastError();
-    if (h->stream) cudaStreamSynchronize(h->stream);
+    if (h->stream) stream_wait(h, h->stream);
+    if (h->factor_stream) stream_wait(h, h->factor_stream);
+    if (h->comm) {
+        nccl_api().CommDestroy(static_cast<ncclComm_t>(h->comm));
+        h->comm = nullptr;
+    }
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
     if (h->fev0) cudaEventDestroy(h->fev0);
@@ -288,12 +387,13 @@ static int32_t apply_options(pp_handle *h, const pp_options *o, const char *who)
     h->fail_alloc_after = o->fail_alloc_after < 0 ? -1 : o->fail_alloc_after;
     if (h->d_err.p) {
         // nothing of the handle may be running while the bound changes; the copy is synchronous
-        CK(h, cudaStreamSynchronize(h->factor_stream), who);
-        CK(h, cudaStreamSynchronize(h->stream), who);
+        CK(h, stream_wait(h, h->factor_stream), who);
+        CK(h, stream_wait(h, h->stream), who);
         CK(h, cudaMemcpy(h->d_err.as<int>() + 2, &h->wait_ns, sizeof(uint64_t), cudaMemcpyHostToDevice), who);
     }
     h->prof.on = o->profile != 0;
     h->merge_width = o->merge_width == 0 ? 64 : o->merge_width;
+    h->trace_on = o->trace != 0;
     return PP_OK;
 }
 
@@ -325,6 +425,7 @@ extern "C" int32_t pp_get_options(const pp_handle *h, pp_options *opt) {
     opt->fail_alloc_after = h->fail_alloc_after;
     opt->profile = h->prof.on ? 1 : 0;
     opt->merge_width = h->merge_width;
+    opt->trace = h->trace_on ? 1 : 0;
     return PP_OK;
 }
 
@@ -414,7 +515,7 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
         return fail(h, PP_EINVAL, "pp_set_structure: null array");
     if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_set_structure: base must be 0 or 1");
     CK(h, cudaSetDevice(h->device), "pp_set_structure");
-    if (h->factor_stream) cudaStreamSynchronize(h->factor_stream);  // nothing in flight reads the old plan
+    if (h->factor_stream) stream_wait(h, h->factor_stream);  // nothing in flight reads the old plan
     h->have_structure = h->have_values = h->factored = false;
     h->nnz_assembled = -1;
     HostPlan hp;
@@ -784,7 +885,7 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
         CK(h, cudaMemsetAsync(h->d_err.p, 0, sizeof(int) * 4, st), "upload");
         CK(h, cudaMemcpyAsync(h->d_err.as<int>() + 2, &h->wait_ns, sizeof(uint64_t), cudaMemcpyHostToDevice, st),
            "upload");
-        CK(h, cudaStreamSynchronize(st), "upload");
+        CK(h, stream_wait(h, st), "upload");
         DevPlan &d = hp.dev;
         d.n = (int)n;
         d.nf = (int)nf;
@@ -865,6 +966,92 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
         return fail(h, PP_ENOMEM, "pp_set_structure: out of host memory");
     }
     h->have_structure = true;
+    ok(h);
+    return PP_OK;
+}
+
+// ---------------------------------------------------------------- several GPUs
+
+// Every rank's part of the bottom of the tree to every rank: per part and factor array (and the workspace,
+// which holds the update matrices the top of the tree reads) one NCCL broadcast from the part's rank, in place,
+// all in one group on the calling stream.
+static cudaError_t exchange_parts(void *ctx, cudaStream_t st) {
+    pp_handle *h = static_cast<pp_handle *>(ctx);
+    const NcclApi &N = nccl_api();
+    const size_t es = h->ops->esize;
+    ncclComm_t comm = static_cast<ncclComm_t>(h->comm);
+    if (!comm) {
+        h->comm_msg = "the handle left its group of GPUs after an earlier failure";
+        return cudaErrorInvalidValue;
+    }
+    ncclResult_t r = N.GroupStart();
+    for (int q = 0; q < h->nranks && r == ncclSuccess; q++) {
+        const Part &pt = h->parts[q];
+        const struct {
+            void *p;
+            int64_t a, b;
+        } seg[5] = {{h->LD.p, pt.d0, pt.d1}, {h->UD.p, pt.d0, pt.d1}, {h->LL.p, pt.l0, pt.l1},
+                    {h->UL.p, pt.l0, pt.l1}, {h->W.p, pt.w0, pt.w1}};
+        for (const auto &g : seg)
+            if (g.b > g.a && r == ncclSuccess) {
+                char *p = static_cast<char *>(g.p) + es * (size_t)g.a;
+                r = N.Broadcast(p, p, es * (size_t)(g.b - g.a), ncclUint8, q, comm, st);
+            }
+    }
+    const ncclResult_t r2 = N.GroupEnd();
+    if (r != ncclSuccess || r2 != ncclSuccess) {
+        h->comm_msg = std::string("NCCL: ") + N.GetErrorString(r != ncclSuccess ? r : r2);
+        return cudaErrorInvalidValue;
+    }
+    return cudaSuccess;
+}
+
+extern "C" int32_t pp_comm_id(void *id) {
+    if (!id) return fail(nullptr, PP_EINVAL, "pp_comm_id: null id");
+    const NcclApi &N = nccl_api();
+    if (!N.ok) return fail(nullptr, PP_EUNSUPPORTED, "pp_comm_id: %s", N.why.c_str());
+    ncclUniqueId u;
+    const ncclResult_t r = N.GetUniqueId(&u);
+    if (r != ncclSuccess) return fail(nullptr, PP_EDEVICE, "pp_comm_id: NCCL: %s", N.GetErrorString(r));
+    static_assert(sizeof(ncclUniqueId) == PP_COMM_ID_BYTES, "NCCL unique id size");
+    memcpy(id, &u, sizeof u);
+    ok(nullptr);
+    return PP_OK;
+}
+
+extern "C" int32_t pp_comm_init(pp_handle *h, const void *id, int32_t nranks, int32_t rank) {
+    const char *who = "pp_comm_init";
+    if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
+    if (nranks < 1 || rank < 0 || rank >= nranks || (nranks > 1 && !id))
+        return fail(h, PP_EINVAL, "%s: rank %d of %d", who, rank, nranks);
+    CK(h, cudaSetDevice(h->device), who);
+    CK(h, stream_wait(h, h->factor_stream), who);
+    CK(h, stream_wait(h, h->stream), who);
+    if (h->comm) {
+        nccl_api().CommDestroy(static_cast<ncclComm_t>(h->comm));
+        h->comm = nullptr;
+    }
+    h->comm_failed = false;
+    h->nranks = 1;
+    h->rank = 0;
+    h->hp.exchange = nullptr;
+    h->hp.exchange_ctx = nullptr;
+    h->ws_esize = 0;  // the bottom work list changes: prepared again before the next factorization
+    if (nranks > 1) {
+        const NcclApi &N = nccl_api();
+        if (!N.ok) return fail(h, PP_EUNSUPPORTED, "%s: %s", who, N.why.c_str());
+        ncclUniqueId u;
+        memcpy(&u, id, sizeof u);
+        ncclComm_t comm = nullptr;
+        const ncclResult_t r = N.CommInitRank(&comm, nranks, u, rank);
+        if (r != ncclSuccess) return fail(h, PP_EDEVICE, "%s: NCCL: %s", who, N.GetErrorString(r));
+        h->comm = comm;
+        h->nranks = nranks;
+        h->rank = rank;
+        h->hp.exchange = exchange_parts;
+        h->hp.exchange_ctx = h;
+        h->comm_wait_s = h->wait_ns ? std::max(1.0, 30e-9 * (double)h->wait_ns) : 60.0;
+    }
     ok(h);
     return PP_OK;
 }
@@ -1120,26 +1307,75 @@ static int32_t prepare_workspace(pp_handle *h) {
     hp.mptr.assign(nf, 0);
     hp.fws.assign(nf, -1);
     hp.mld.assign(nf, 1);
+    // the bottom fronts' update matrices first, in front order (so that the fronts of a range of the tree have
+    // one contiguous range of the workspace: a rank's part of the bottom, several GPUs), then the top fronts'
+    // frontal matrices
+    std::vector<int64_t> wend(nf, 0);
     int64_t off = 0;
-    for (int f = 0; f < nf; f++) {
-        const int nn = hp.nn[f], na = hp.na[f], nj = nn + na;
-        if (fbot[f]) {
-            hp.mptr[f] = off;
-            hp.mld[f] = std::max(na, 1);
-            off += (int64_t)na * na;
-        } else {
-            hp.fws[f] = off;
-            hp.mptr[f] = off + nn + (int64_t)nn * nj;
-            hp.mld[f] = nj;
-            off += (int64_t)nj * nj;
+    for (int pass = 0; pass < 2; pass++)
+        for (int f = 0; f < nf; f++) {
+            if ((fbot[f] != 0) != (pass == 0)) continue;
+            const int nn = hp.nn[f], na = hp.na[f], nj = nn + na;
+            if (fbot[f]) {
+                hp.mptr[f] = off;
+                hp.mld[f] = std::max(na, 1);
+                off += (int64_t)na * na;
+            } else {
+                hp.fws[f] = off;
+                hp.mptr[f] = off + nn + (int64_t)nn * nj;
+                hp.mld[f] = nj;
+                off += (int64_t)nj * nj;
+            }
+            off = (off + 3) & ~(int64_t)3;  // 16-byte alignment of every block
+            wend[f] = off;
         }
-        off = (off + 3) & ~(int64_t)3;  // 16-byte alignment of every block
-    }
     hp.ws_elems = off;
+    // several GPUs: the maximal bottom subtrees (contiguous ranges of fronts in postorder) dealt to the ranks in
+    // front order, each rank a contiguous run of about equal estimated time; a rank's part is then one range of
+    // each factor array and of the workspace
+    h->parts.clear();
+    if (h->nranks > 1) {
+        std::vector<int> fdsc(nf);
+        for (int f = 0; f < nf; f++) fdsc[f] = f;
+        for (int f = 0; f < nf; f++)
+            if (h->pnt[f] >= 0) fdsc[h->pnt[f]] = std::min(fdsc[h->pnt[f]], fdsc[f]);
+        std::vector<double> est(nf + 1, 0.0);  // prefix sums of the bottom fronts' estimated times
+        for (int f = 0; f < nf; f++) {
+            const double nj = hp.nn[f] + hp.na[f];
+            est[f + 1] = est[f] + (fbot[f] ? 6.0 + nj * nj / 64.0 + hp.nn[f] * nj * nj / 512.0 : 0.0);
+        }
+        std::vector<std::pair<int, int>> roots;  // (first front, root) of each maximal bottom subtree
+        for (int f = 0; f < nf; f++)
+            if (fbot[f] && (h->pnt[f] < 0 || !fbot[h->pnt[f]])) roots.push_back({fdsc[f], f});
+        // subtree q goes to the rank whose share of the total holds the middle of its estimated time: the ranks
+        // of consecutive subtrees never decrease, so every part is one run
+        h->parts.assign(h->nranks, Part{});
+        std::vector<char> used(h->nranks, 0);
+        for (const auto &rt : roots) {
+            const double mid = 0.5 * (est[rt.first] + est[rt.second + 1]);
+            const int r = est[nf] > 0 ? std::min(h->nranks - 1, (int)(mid * h->nranks / est[nf])) : 0;
+            Part &pt = h->parts[r];
+            if (!used[r]) {
+                pt.f0 = rt.first;
+                pt.w0 = hp.mptr[rt.first];
+                used[r] = 1;
+            }
+            pt.f1 = rt.second + 1;
+            pt.w1 = wend[rt.second];
+        }
+        for (int r = 0; r < h->nranks; r++) {
+            Part &pt = h->parts[r];
+            if (!used[r]) continue;  // an empty part: f0 = f1 = 0
+            pt.d0 = hp.dptr[pt.f0];
+            pt.d1 = hp.dptr[pt.f1];
+            pt.l0 = hp.lptr[pt.f0];
+            pt.l1 = hp.lptr[pt.f1];
+        }
+    }
     const int maxh = h->maxh;
     cudaStream_t st = h->stream;
-    CK(h, cudaStreamSynchronize(h->factor_stream), "prepare_workspace");
-    CK(h, cudaStreamSynchronize(st), "prepare_workspace");
+    CK(h, stream_wait(h, h->factor_stream), "prepare_workspace");
+    CK(h, stream_wait(h, st), "prepare_workspace");
     // stage 0 of each solve direction lists the subtrees and forward bottom fronts that the bottom kernel
     // factors first: a solve sweeps them while the top of the tree is factored.  fbot holds every child of a
     // front it holds, so the stable partition keeps each child before its parent.
@@ -1192,7 +1428,19 @@ static int32_t prepare_workspace(pp_handle *h) {
             const double nj = hp.nn[f] + hp.na[f];
             fcost[f] = 6.0 + nj * nj / 64.0 + hp.nn[f] * nj * nj / 512.0;
         }
-        const std::vector<int> wl = schedule_order(hl, fcost, h->pnt, true, h->sm_count * 6);
+        std::vector<int> wl = schedule_order(hl, fcost, h->pnt, true, h->sm_count * 6);
+        if (h->nranks > 1) {  // this rank's part only (the list order keeps children first)
+            const Part &pt = h->parts[h->rank];
+            std::vector<int> mine;
+            Cost part;
+            for (int f : wl)
+                if (f >= pt.f0 && f < pt.f1) {
+                    mine.push_back(f);
+                    front_cost(hp, f, part);
+                }
+            wl.swap(mine);
+            acc = part;
+        }
         hp.fb_count = (int)wl.size();
         hp.fb_bytes = acc.bytes;
         hp.fb_pairs = acc.pairs;
@@ -1266,7 +1514,7 @@ static int32_t prepare_workspace(pp_handle *h) {
     CK(h, upload(h->d_mptr, hp.mptr, st), "upload");
     CK(h, upload(h->d_mld, hp.mld, st), "upload");
     CK(h, upload(h->d_fws, hp.fws, st), "upload");
-    CK(h, cudaStreamSynchronize(st), "upload");
+    CK(h, stream_wait(h, st), "upload");
     hp.dev.mptr = h->d_mptr.as<int64_t>();
     hp.dev.mld = h->d_mld.as<int>();
     hp.dev.fws = h->d_fws.as<int64_t>();
@@ -1349,7 +1597,7 @@ extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, co
     if (!h->have_structure) return fail(h, PP_ESTATE, "pp_assemble: no structure (call pp_set_structure first)");
     if (base != 0 && base != 1) return fail(h, PP_EINVAL, "pp_assemble: base must be 0 or 1");
     CK(h, cudaSetDevice(h->device), "pp_assemble");
-    CK(h, cudaStreamSynchronize(h->factor_stream), "pp_assemble");  // buffers may be reallocated below
+    CK(h, stream_wait(h, h->factor_stream), "pp_assemble");  // buffers may be reallocated below
     int32_t r = set_semiring(h, semiring, dtype, "pp_assemble");
     if (r != PP_OK) return r;
     const int n = h->hp.n;
@@ -1394,7 +1642,7 @@ extern "C" int32_t pp_assemble(pp_handle *h, int32_t semiring, int32_t dtype, co
     CK(h, h->ops->assemble(h->hp, h->csc_ptr.as<int>(), h->csc_row.as<int>(), h->csc_val.p, values_of(h), st),
        "pp_assemble");
     h->prof.end(pi, st, 2.0 * (h->nD + h->nL) + h->hp.nN + (double)cp[n] * (1.0 + 8.0 / es), 0);
-    CK(h, cudaStreamSynchronize(st), "pp_assemble");
+    CK(h, stream_wait(h, st), "pp_assemble");
     h->prof.collect();
     h->nnz_assembled = cp[n];
     h->have_values = true;
@@ -1427,7 +1675,7 @@ extern "C" int32_t pp_update_values(pp_handle *h, const void *nzval, int32_t whe
     CK(h, h->ops->assemble(h->hp, h->csc_ptr.as<int>(), h->csc_row.as<int>(), h->csc_val.p, values_of(h), st),
        "pp_update_values");
     h->prof.end(pi, st, 2.0 * (h->nD + h->nL) + h->hp.nN + (double)nnz * (1.0 + 8.0 / es), 0);
-    if (where == PP_HOST) CK(h, cudaStreamSynchronize(st), "pp_update_values");  // the caller's array is free
+    if (where == PP_HOST) CK(h, stream_wait(h, st), "pp_update_values");  // the caller's array is free
     h->have_values = true;
     h->factored = false;
     ok(h);
@@ -1440,7 +1688,7 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
     if (!h) return fail(nullptr, PP_EINVAL, "pp_set_values: null handle");
     if (!h->have_structure) return fail(h, PP_ESTATE, "pp_set_values: no structure");
     CK(h, cudaSetDevice(h->device), "pp_set_values");
-    CK(h, cudaStreamSynchronize(h->factor_stream), "pp_set_values");
+    CK(h, stream_wait(h, h->factor_stream), "pp_set_values");
     int32_t r = set_semiring(h, semiring, dtype, "pp_set_values");
     if (r != PP_OK) return r;
     const size_t es = h->ops->esize;
@@ -1471,7 +1719,7 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
                 CK(h, cudaMemcpyAsync(dst[a]->p, m[a].data(), es * (a < 2 ? h->nD : h->nL), cudaMemcpyHostToDevice, st),
                    "pp_set_values");
         if (h->hp.nN) CK(h, cudaMemcpyAsync(h->Nval.p, Nval, es * h->hp.nN, cudaMemcpyHostToDevice, st), "pp_set_values");
-        CK(h, cudaStreamSynchronize(st), "pp_set_values");
+        CK(h, stream_wait(h, st), "pp_set_values");
         h->have_values = true;
         h->factored = false;
         ok(h);
@@ -1482,7 +1730,7 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
     if (h->nL) CK(h, cudaMemcpyAsync(h->LL.p, LL, es * h->nL, cudaMemcpyHostToDevice, st), "pp_set_values");
     if (h->nL) CK(h, cudaMemcpyAsync(h->UL.p, UL, es * h->nL, cudaMemcpyHostToDevice, st), "pp_set_values");
     if (h->hp.nN) CK(h, cudaMemcpyAsync(h->Nval.p, Nval, es * h->hp.nN, cudaMemcpyHostToDevice, st), "pp_set_values");
-    CK(h, cudaStreamSynchronize(st), "pp_set_values");
+    CK(h, stream_wait(h, st), "pp_set_values");
     h->have_values = true;
     h->factored = false;
     ok(h);
@@ -1492,8 +1740,8 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
 // Wait for the handle's stream, then take the times of the calls enqueued since the last wait and the error
 // word of the persistent kernels (set when a bounded wait expired; cleared once reported).
 static int32_t settle(pp_handle *h, const char *who) {
-    CK(h, cudaStreamSynchronize(h->factor_stream), who);
-    CK(h, cudaStreamSynchronize(h->stream), who);
+    CK(h, stream_wait(h, h->factor_stream), who);
+    CK(h, stream_wait(h, h->stream), who);
     if (h->factor_pending) {
         float ms = 0;
         if (cudaEventElapsedTime(&ms, h->fev0, h->fev1) == cudaSuccess) h->st.ms_factor = ms;
@@ -1522,21 +1770,43 @@ extern "C" int32_t pp_factor(pp_handle *h) {
     if (!h) return fail(nullptr, PP_EINVAL, "pp_factor: null handle");
     if (!h->have_values) return fail(h, PP_ESTATE, "pp_factor: no values (call pp_assemble or pp_set_values)");
     CK(h, cudaSetDevice(h->device), "pp_factor");
+    if (h->ws_esize != h->ops->esize || h->hp.mld.empty()) {  // joined or left a group since the last one
+        const int32_t r = prepare_workspace(h);
+        if (r != PP_OK) {
+            h->factored = false;
+            return r;
+        }
+    }
     const size_t wbytes = h->ops->esize * std::max<int64_t>(h->hp.ws_elems, 1);
     if (wbytes > h->W.bytes) {
-        CK(h, cudaStreamSynchronize(h->factor_stream), "pp_factor");
-        CK(h, cudaStreamSynchronize(h->stream), "pp_factor");
+        CK(h, stream_wait(h, h->factor_stream), "pp_factor");
+        CK(h, stream_wait(h, h->stream), "pp_factor");
         h->W.release();
         h->factored = false;
         if (need_memory(h, wbytes, "pp_factor") != PP_OK) return PP_ENOMEM;
         CK(h, h->W.ensure(wbytes), "pp_factor");
     }
     if (ensure_sync(h, 1) != PP_OK) return PP_ENOMEM;  // the bottom kernel's counters
+    h->hp.d_trace = nullptr;
+    if (h->trace_on && h->hp.top_ntasks > 0) {
+        CK(h, h->d_trace.ensure(sizeof(unsigned long long) * PP_TRACE_WORDS * (size_t)h->hp.top_ntasks), "pp_factor");
+        CK(h, cudaMemsetAsync(h->d_trace.p, 0, sizeof(unsigned long long) * PP_TRACE_WORDS * (size_t)h->hp.top_ntasks,
+                              h->stream),
+           "pp_factor");
+        h->hp.d_trace = h->d_trace.as<unsigned long long>();
+    }
+    if (h->comm_failed) return fail(h, PP_ESTATE, "pp_factor: the handle left its group of GPUs after a failure");
     cudaStream_t st = h->stream;
     int64_t nl = 0;
     CK(h, after_factor(h), "pp_factor");  // the previous top factorization reads the bottom's update matrices
     CK(h, record_timing(h, h->fev0, st), "pp_factor");
-    CK(h, h->ops->factor(h->hp, values_of(h), st, &nl), "pp_factor");
+    h->comm_msg.clear();
+    const cudaError_t fe = h->ops->factor(h->hp, values_of(h), st, &nl);
+    if (fe != cudaSuccess && !h->comm_msg.empty()) {
+        h->factored = false;
+        return fail(h, PP_EDEVICE, "pp_factor: %s", h->comm_msg.c_str());
+    }
+    CK(h, fe, "pp_factor");
     CK(h, record_timing(h, h->fev1, h->factor_stream), "pp_factor");  // the top of the tree ends there
     h->factor_pending = !h->capturing;
     h->st.kernel_launches = nl;
@@ -1905,6 +2175,21 @@ extern "C" int32_t pp_sync(pp_handle *h) {
     return PP_OK;
 }
 
+extern "C" int32_t pp_get_trace(pp_handle *h, uint64_t *out, int64_t max_tasks, int64_t *ntasks) {
+    if (!h || !ntasks || (max_tasks > 0 && !out)) return fail(h, PP_EINVAL, "pp_get_trace: null argument");
+    CK(h, cudaSetDevice(h->device), "pp_get_trace");
+    const int32_t r = settle(h, "pp_get_trace");
+    if (r != PP_OK) return r;
+    const int64_t have = h->d_trace.p && h->trace_on ? (int64_t)h->hp.top_ntasks : 0;
+    *ntasks = have;
+    const int64_t m = std::min<int64_t>(have, std::max<int64_t>(max_tasks, 0));
+    if (m > 0)
+        CK(h, cudaMemcpy(out, h->d_trace.p, sizeof(uint64_t) * PP_TRACE_WORDS * (size_t)m, cudaMemcpyDeviceToHost),
+           "pp_get_trace");
+    ok(h);
+    return PP_OK;
+}
+
 extern "C" int32_t pp_get_stats(pp_handle *h, pp_stats *s) {
     if (!h || !s) return fail(h, PP_EINVAL, "pp_get_stats: null argument");
     CK(h, cudaSetDevice(h->device), "pp_get_stats");
@@ -2018,6 +2303,7 @@ extern "C" int32_t pp_plan_lmul(pp_handle *h, const void *nzval, const void *Bin
     if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
     if (!h->have_structure || h->nnz_assembled < 0)
         return fail(h, PP_ESTATE, "%s: no pattern (call pp_assemble first)", who);
+    if (h->nranks > 1) return fail(h, PP_ESTATE, "%s: plans are for a handle on one GPU (not joined by pp_comm_init)", who);
     const int n = h->hp.n;
     if (n == 0 || k <= 0 || k >= INT32_MAX / 2) return fail(h, PP_EINVAL, "%s: n = %d, k = %lld", who, n, (long long)k);
     if ((h->nnz_assembled > 0 && !nzval) || !Bin || !Bout || ldb < n) return fail(h, PP_EINVAL, "%s: arrays", who);

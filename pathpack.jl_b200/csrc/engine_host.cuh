@@ -100,6 +100,7 @@ struct Engine {
             if (pi >= 0) hp.prof->end(pi, st, hp.fb_bytes, hp.fb_pairs);
             nl++;
         }
+        if (hp.exchange) PP_TRY(hp.exchange(hp.exchange_ctx, st));  // the other ranks' parts of the bottom
         cudaStream_t ts = st;
         if (hp.top_stream && hp.ev_bottom && hp.ev_factored) {
             ts = hp.top_stream;
@@ -115,7 +116,7 @@ struct Engine {
             const int pi = hp.prof ? hp.prof->begin(K_FACTOR_TOP, ts) : -1;
             factor_top_kernel<SR, T><<<grid, 256, smem, ts>>>(hp.d_ttasks, hp.top_ntasks, hp.dev, hp.d_tfoff,
                                                               hp.d_croff, hp.d_crng, LD, LL, UD, UL, W, hp.d_tflags,
-                                                              hp.d_err);
+                                                              hp.d_err, hp.d_trace);
             PP_TRY(cudaGetLastError());
             if (pi >= 0) hp.prof->end(pi, ts, hp.top_cost.bytes, hp.top_cost.pairs);
             nl++;

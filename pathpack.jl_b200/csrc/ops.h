@@ -99,6 +99,8 @@ struct HostPlan {
     const int *d_crng = nullptr;       // per child edge: the parent's tile-block boundaries in the child's rel[]
     int *d_tflags = nullptr;           // [0] task counter, [1] error word, then the fronts' flags
     int64_t tflags_n = 0;
+    // per-task timeline of the top factorization (pp_options.trace): TRACE_WORDS per task, or null
+    unsigned long long *d_trace = nullptr;
     Cost top_cost;
     int64_t nN = 0;
     // solve schedules (lmul: components after their coupling successors; rmul: after their predecessors)
@@ -148,6 +150,11 @@ struct HostPlan {
     // front (empty: the plan's fronts are the caller's): factorization (x)(+) pairs and elements moved, and the
     // (x)(+) pairs of one right-hand side through L* (or U*)
     std::vector<double> ufac_pairs, ufac_elems, usolve_pairs;
+    // several GPUs (pp_comm_init): each rank's bottom kernel factors its own part of the bottom of the tree
+    // (d_fbottom holds that part), then `exchange` runs on the calling stream and gives every rank the other
+    // parts, before the top of the tree is factored on every rank
+    cudaError_t (*exchange)(void *ctx, cudaStream_t st) = nullptr;
+    void *exchange_ctx = nullptr;
 };
 
 struct Values {

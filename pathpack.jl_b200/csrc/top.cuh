@@ -28,6 +28,7 @@
 // task counter; err is the error word of the factorization.
 #pragma once
 
+#include "pathpack_b200.h"
 #include "persist.cuh"
 
 namespace pp {
@@ -185,88 +186,86 @@ __device__ __forceinline__ void tile_solve_left(T *X, const T *D, int b) {
     }
 }
 
-// Partial LU of the b x b diagonal tile, warp-pipelined.  Columns are dealt round-robin: warp w holds columns
-// w, w + 8, ... (lanes: rows l and l + 32), slot 0 being its column of the current group of eight pivots (the
-// slots move down after each group).  Column p + 1 belongs to warp (p + 1) & 7: once it has pivot p, that warp
-// scales it by the star of its diagonal and publishes it in X with a per-column flag in shared memory, before
-// its other columns take pivot p, so consecutive pivots are published by different warps and the next
-// lookahead never waits behind a warp's own updates.  Pivots p >= 32 touch rows l + 32 only and at most four
-// slots.  Every column is final when published, so X holds the factored tile at the end.  Per element the
-// operands and their order are those of lu_smem.  A wait that does not end within its bound sets *err (the
-// tile is then garbage, the launch reports the error).
+// Per-task timeline (pp_options.trace): for task t, trace[TRACE_WORDS * t + ...] = global timer (ns) when the
+// task was taken, when its tile was assembled (children's update matrices and A), when the products with the
+// pivot blocks were done, when its flag was set, then (SM << 32) | front and (I << 32) | J.
+constexpr int TRACE_WORDS = PP_TRACE_WORDS;  // include/pathpack_b200.h
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned smid() {
+    unsigned s;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(s));
+    return s;
+}
+
+// The partial LU of the b x b diagonal tile in X, held in registers: the scheme of getrf_reg_kernel (getrf.cuh)
+// on a 64 x 64 tile (per element the scalar LU's operations in its order, sgetrf2!, src/CPU/dense/sgetrf.jl:
+// 151-175, as lu_smem).  Thread (tr, tc) = (tid % 16, tid / 16) holds f[a][c] = X[tr + 16a][tc + 16c]; per pivot the
+// half-warp holding column p scales it (the diagonal by a shuffle) and publishes it, the threads holding row p
+// publish it, one barrier (column and row double-buffered in cb / rb, 2 x 16 x 4 elements each), then every
+// thread updates its trailing entries.  Every thread of the CTA calls it.
 template <int SR, typename T>
-__device__ __forceinline__ void tile_lu(T *X, int *colflag, int b, int *err) {
+__device__ __forceinline__ void tile_lu_reg(T *X, int b, T *cb, T *rb) {
     using S = Sem<SR, T>;
-    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
-    T x0[8], x1[8];
+    constexpr int R = 4;
+    const int tid = threadIdx.x, tr = tid & 15, tc = tid >> 4, lane = tid & 31;
+    const T z = S::zero();
+    T f[R][R];
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-        x0[q] = X[l * TLD + 8 * q + w];
-        x1[q] = X[(l + 32) * TLD + 8 * q + w];
-    }
-    auto publish = [&](int p, T &y0, T &y1) {
-        const T d = __shfl_sync(0xffffffffu, p >= 32 ? y1 : y0, p & 31);
-        if (!S::integral) {
-            const T s = S::star(d);
-            if (l > p && l < b) y0 = S::mul(y0, s);
-            if (l + 32 > p && l + 32 < b) y1 = S::mul(y1, s);
+    for (int a = 0; a < R; a++)
+#pragma unroll
+        for (int c = 0; c < R; c++) {
+            const int i = tr + 16 * a, j = tc + 16 * c;
+            f[a][c] = (i < b && j < b) ? X[i * TLD + j] : z;
         }
-        X[l * TLD + p] = y0;
-        X[(l + 32) * TLD + p] = y1;
-        __syncwarp();
-        __threadfence_block();
-        if (l == 0) *(volatile int *)(colflag + p) = 1;
-    };
-    auto group = [&](int pg, auto half) {
-        constexpr bool HI = decltype(half)::hi;
-        constexpr int NS = HI ? 4 : 8;  // live slots
 #pragma unroll
-        for (int qp = 0; qp < 8; qp++) {
-            const int p = 8 * pg + qp;
-            if (p < b) {
-                if (w != qp) {  // column p is warp qp's
-                    if (l == 0) {
-                        long long it = 0;
-                        while (*(volatile int *)(colflag + p) == 0)
-                            if (++it > WAIT_LIMIT) {
-                                atomicExch(err, 1);
-                                break;
-                            }
-                    }
-                    __syncwarp();
-                    __threadfence_block();
-                }
-                const T c0 = HI ? S::zero() : X[l * TLD + p], c1 = X[(l + 32) * TLD + p];
-                const bool g0 = !HI && l > p && l < b, g1 = l + 32 > p && l + 32 < b;
-                // lookahead: column p + 1 is slot 0 of warp qp + 1, or slot 1 of warp 0 after the group
-                const int la_w = (qp + 1) & 7, la_s = qp < 7 ? 0 : 1;
-                if (w == la_w && p + 1 < b) {
-                    const T up = __shfl_sync(0xffffffffu, HI ? x1[la_s] : x0[la_s], p & 31);
-                    if (!HI) x0[la_s] = muladd_if<SR, T>(g0, c0, up, x0[la_s]);
-                    x1[la_s] = muladd_if<SR, T>(g1, c1, up, x1[la_s]);
-                    publish(p + 1, x0[la_s], x1[la_s]);
-                }
-                T up[NS];
+    for (int q = 0; q < R; q++) {
+        const int pend = min(16, b - 16 * q);  // pivots of this phase (uniform over the CTA)
+        for (int pp = 0; pp < pend; pp++) {
+            const int p = 16 * q + pp, buf = p & 1;
+            T *colb = cb + buf * 16 * R, *rowb = rb + buf * 16 * R;
+            if (tc == pp) {  // one half-warp holds column p
+                if (!S::integral) {
+                    const unsigned half = (lane & 16) ? 0xffff0000u : 0x0000ffffu;
+                    const T s = S::star(__shfl_sync(half, f[q][q], (lane & 16) | pp));
 #pragma unroll
-                for (int sl = 0; sl < NS; sl++) up[sl] = __shfl_sync(0xffffffffu, HI ? x1[sl] : x0[sl], p & 31);
-#pragma unroll
-                for (int sl = 0; sl < NS; sl++) {
-                    const int c = w + 8 * (pg + sl);
-                    const bool on = c > p + 1 && c < b;
-                    if (!HI) x0[sl] = muladd_if<SR, T>(on && g0, c0, up[sl], x0[sl]);
-                    x1[sl] = muladd_if<SR, T>(on && g1, c1, up[sl], x1[sl]);
+                    for (int a = q; a < R; a++)
+                        if (a > q || tr > pp) f[a][q] = S::mul(f[a][q], s);
                 }
+#pragma unroll
+                for (int a = q; a < R; a++) colb[tr * R + a] = f[a][q];
             }
-        }
+            if (tr == pp) {
 #pragma unroll
-        for (int sl = 0; sl < 7; sl++) {
-            x0[sl] = x0[sl + 1];
-            x1[sl] = x1[sl + 1];
+                for (int c = q; c < R; c++) rowb[tc * R + c] = f[q][c];
+            }
+            __syncthreads();
+            T cv[R], rv[R];
+#pragma unroll
+            for (int a = q; a < R; a++) cv[a] = colb[tr * R + a];
+#pragma unroll
+            for (int c = q; c < R; c++) rv[c] = rowb[tc * R + c];
+            const bool r0 = tr > pp, c0 = tc > pp;  // row 16q + tr and column 16q + tc still trail pivot p
+#pragma unroll
+            for (int a = q; a < R; a++)
+#pragma unroll
+                for (int c = q; c < R; c++)
+                    if ((a > q || r0) && (c > q || c0)) f[a][c] = S::muladd(cv[a], rv[c], f[a][c]);
         }
-    };
-    if (w == 0) publish(0, x0[0], x1[0]);
-    for (int pg = 0; pg < 4 && 8 * pg < b; pg++) group(pg, Half<false>());
-    for (int pg = 4; 8 * pg < b; pg++) group(pg, Half<true>());
+    }
+#pragma unroll
+    for (int a = 0; a < R; a++)
+#pragma unroll
+        for (int c = 0; c < R; c++) {
+            const int i = tr + 16 * a, j = tc + 16 * c;
+            if (i < b && j < b) X[i * TLD + j] = f[a][c];
+        }
+    __syncthreads();
 }
 
 template <int SR, typename T>
@@ -274,7 +273,7 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
                                                          const int64_t *__restrict__ foff,
                                                          const int64_t *__restrict__ croff,
                                                          const int *__restrict__ crng, T *LD, T *LL, T *UD, T *UL,
-                                                         T *W, int *flags, int *err) {
+                                                         T *W, int *flags, int *err, unsigned long long *trace) {
     using S = Sem<SR, T>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *As = reinterpret_cast<T *>(smem_raw);  // [TB][TLD]: A operand (rows x k), or the diagonal tile
@@ -285,13 +284,15 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
     __shared__ int2 s_cmeta[CHILD_CHUNK];  // leading dimension of the update matrix, offset of rel
     __shared__ int s_ctop[CHILD_CHUNK];    // the child if it is a top front, else -1
     __shared__ int s_bad;
-    __shared__ int s_colflag[TB];  // published pivot columns of the diagonal tile's LU
+    __shared__ __align__(16) T s_luc[2 * 16 * 4], s_lur[2 * 16 * 4];  // tile_lu_reg's published column and row
     const int tid = threadIdx.x, tc = tid & 15, tr = tid >> 4;
     const T z = S::zero();
 
     while (true) {
         const int t = cta_take(next);
         if (t >= ntasks) return;
+        unsigned long long *trc = trace && threadIdx.x == 0 ? trace + (size_t)TRACE_WORDS * t : nullptr;
+        if (trc) trc[0] = global_ns();
         const int4 task = tasks[t];
         const int f = task.x, I = task.y, J = task.z;
         const int nn = P.nn[f], na = P.na[f], nj = nn + na;
@@ -380,6 +381,7 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
             if (r < mi && c < mj) As[r * TLD + c] = combine_with<SR, T>(As[r * TLD + c], aval[k], i0 + r, j0 + c, nn);
         }
         __syncthreads();
+        if (trc) trc[1] = global_ns();
         T acc[4][4];
 #pragma unroll
         for (int i = 0; i < 4; i++)
@@ -412,6 +414,7 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
             __syncthreads();
         }
 
+        if (trc) trc[2] = global_ns();
         // the tile to shared memory (As: rows x columns); the triangular work runs on it warp by warp
         const bool pivot_region = I < kb || J < kb;
 #pragma unroll
@@ -428,11 +431,10 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
                 Bs[r * TLD + c] = (r < b && c < b) ? ld_cg(F + (d0 + r) + (int64_t)(d0 + c) * nj) : z;
             }
         }
-        if (pivot_region && I == J && tid < TB) s_colflag[tid] = 0;
         __syncthreads();
         if (pivot_region) {
             if (I == J)
-                tile_lu<SR, T>(As, s_colflag, mi, err);
+                tile_lu_reg<SR, T>(As, mi, s_luc, s_lur);
             else if (I > J)
                 tile_solve_right<SR, T>(As, Bs, mj);
             else
@@ -454,6 +456,11 @@ __global__ void __launch_bounds__(256) factor_top_kernel(const int4 *__restrict_
             __threadfence();
             atomicExch(fl + I * nbt + J, 1);
             if (!pivot_region) atomicAdd(fl + nbt * nbt, 1);
+            if (trc) {
+                trc[3] = global_ns();
+                trc[4] = ((unsigned long long)smid() << 32) | (unsigned)f;
+                trc[5] = ((unsigned long long)(unsigned)I << 32) | (unsigned)J;
+            }
         }
     }
 }

@@ -33,7 +33,7 @@ class pp_stats(C.Structure):
 
 class pp_options(C.Structure):
     _fields_ = [("wait_timeout_us", C.c_int64), ("fail_alloc_after", C.c_int64), ("profile", C.c_int32),
-                ("merge_width", C.c_int32)]
+                ("merge_width", C.c_int32), ("trace", C.c_int32), ("reserved", C.c_int32)]
 
 
 class pp_kernel_class(C.Structure):
@@ -67,11 +67,14 @@ SIGNATURES = {
     "pp_lmul_static": (C.c_int32, [_P, _P, C.c_int64, C.c_int64]),
     "pp_star": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int64, C.c_int32]),
     "pp_sync": (C.c_int32, [_P]),
+    "pp_comm_id": (C.c_int32, [C.c_void_p]),
+    "pp_comm_init": (C.c_int32, [_P, C.c_void_p, C.c_int32, C.c_int32]),
     "pp_plan_lmul": (C.c_int32, [_P, _P, _P, _P, C.c_int64, C.c_int64, C.POINTER(_P)]),
     "pp_plan_launch": (C.c_int32, [_P]),
     "pp_plan_launches": (C.c_int32, [_P, C.POINTER(C.c_int64)]),
     "pp_plan_destroy": (C.c_int32, [_P]),
     "pp_get_stats": (C.c_int32, [_P, C.POINTER(pp_stats)]),
+    "pp_get_trace": (C.c_int32, [_P, C.c_void_p, C.c_int64, C.POINTER(C.c_int64)]),
     "pp_stream": (_P, [_P]),
     "pp_set_profile": (C.c_int32, [_P, C.c_int32]),
     "pp_get_profile": (C.c_int32, [_P, C.POINTER(pp_kernel_class), C.c_int32, C.POINTER(C.c_int32)]),

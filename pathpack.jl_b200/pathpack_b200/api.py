@@ -41,7 +41,7 @@ def _options(kw):
     o = pp_options()
     lib().pp_default_options(C.byref(o))
     for k, v in kw.items():
-        if k not in dict(pp_options._fields_):
+        if k not in dict(pp_options._fields_) or k == "reserved":
             raise TypeError("unknown option %r" % k)
         setattr(o, k, int(v))
     return o
@@ -69,13 +69,23 @@ class B200SLU:
         """The handle's pp_options as a dict (wait_timeout_us, fail_alloc_after, profile)."""
         o = pp_options()
         check(lib().pp_get_options(self._h, C.byref(o)), self._h)
-        return {k: getattr(o, k) for k, _ in pp_options._fields_}
+        return {k: getattr(o, k) for k, _ in pp_options._fields_ if k != "reserved"}
 
     def set_options(self, **options):
         """Change options (keywords as in pp_options); the others keep their values."""
         cur = self.options()
         cur.update(options)
         check(lib().pp_set_options(self._h, C.byref(_options(cur))), self._h)
+        return self
+
+    # --- several GPUs
+    def join(self, comm_id, nranks, rank):
+        """Join this factor's handle to a group of `nranks` GPUs as `rank` (pp_comm_init): factor() then splits
+        the bottom of the tree across the group and exchanges the parts over NCCL; every rank must set the same
+        structure, assemble the same matrix and call factor() the same number of times.  comm_id: the bytes of
+        comm_id() made on one rank; nranks = 1 leaves the group."""
+        buf = C.create_string_buffer(bytes(comm_id), 128) if comm_id is not None else None
+        check(lib().pp_comm_init(self._h, buf, int(nranks), int(rank)), self._h)
         return self
 
     # --- lifecycle
@@ -162,6 +172,17 @@ class B200SLU:
         check(lib().pp_get_profile(self._h, arr, 16, C.byref(cnt)), self._h)
         return {arr[i].name.decode(): {"launches": arr[i].launches, "ms": arr[i].ms, "bytes": arr[i].bytes,
                                        "pairs": arr[i].pairs} for i in range(cnt.value)}
+
+    def trace(self):
+        """The timeline of the last factorization's top of the tree (option trace=1; pp_get_trace): an
+        (ntasks, 6) uint64 array of [taken, assembled, products done, published] (global timer, ns),
+        (sm << 32) | front, (I << 32) | J per tile task, in list order."""
+        cnt = C.c_int64()
+        check(lib().pp_get_trace(self._h, None, 0, C.byref(cnt)), self._h)
+        out = np.zeros((cnt.value, 6), dtype=np.uint64)
+        if cnt.value:
+            check(lib().pp_get_trace(self._h, vptr(out), cnt.value, C.byref(cnt)), self._h)
+        return out
 
     def stream(self):
         """The handle's CUDA stream (cudaStream_t as an integer)."""
@@ -297,6 +318,13 @@ class TransposedSLU:
 def transpose(F):
     """transpose(F) for lmul_(transpose(F), B) = (A*)^T B and rmul_(B, transpose(F)) = B (A*)^T."""
     return F.parent if isinstance(F, TransposedSLU) else TransposedSLU(F)
+
+
+def comm_id():
+    """A new group id for B200SLU.join (pp_comm_id, 128 bytes): make it on one rank, send it to the others."""
+    buf = C.create_string_buffer(128)
+    check(lib().pp_comm_id(buf))
+    return buf.raw
 
 
 def mlu(s, A, *, dtype=None, structure=None, device=0, method="nd"):

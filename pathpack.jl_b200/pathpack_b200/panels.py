@@ -1,12 +1,36 @@
-"""Column panels: how one star (Matrix(F), mstar) or one multi-right-hand-side solve is shared by several GPUs.
+"""Several GPUs: the split factorization's group, and the column panels of a star or a multi-right-hand-side
+solve.
 
-Every rank holds the whole factor (its own handle on its own GPU) and computes a contiguous block of columns of
-A* (pp_star with col0 / ncols) or of A* B; the panels are independent, so no collective runs on the data path.
-The only exchange is the optional gather of the panels to one rank (host memory; `torch.distributed.gather`
-over gloo, or over NCCL with device tensors).  This is the reference's row-block split of the multi-GPU APSP
-(ext/PATHPACKCUDAExt/multigpu.jl:254-258) in column form, which is lmul!'s natural layout.
+join_group makes every rank's factor (its own handle on its own GPU) a member of one NCCL group
+(pp_comm_init): the factorization is then split across the ranks and every rank ends with the whole factor.
+Each rank then computes a contiguous block of columns of A* (pp_star with col0 / ncols) or of A* B; the panels
+are independent, so no collective runs on the solve's data path.  The only other exchange is the optional
+gather of the panels to one rank (host memory; `torch.distributed.gather` over gloo, or over NCCL with device
+tensors).  This is the reference's row-block split of the multi-GPU APSP (ext/PATHPACKCUDAExt/
+multigpu.jl:254-258) in column form, which is lmul!'s natural layout.
 """
 import numpy as np
+
+
+def share_comm_id(group=None):
+    """A group id made on rank 0 (pp_comm_id) and sent to every rank with torch.distributed (any backend)."""
+    import torch.distributed as dist
+
+    obj = [None]
+    if dist.get_rank(group) == 0:
+        from .api import comm_id
+
+        obj[0] = comm_id()
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return obj[0]
+
+
+def join_group(F, group=None):
+    """Join F (a B200SLU on this rank's GPU) to the NCCL group of all ranks of `group` (pp_comm_init)."""
+    import torch.distributed as dist
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    return F.join(share_comm_id(group) if world > 1 else None, world, rank)
 
 
 def column_panels(n, world):

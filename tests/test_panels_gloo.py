@@ -74,3 +74,34 @@ def test_star_panels_gathered_over_gloo(world, name, dtype):
     import torch.multiprocessing as mp
 
     mp.spawn(_worker, args=(world, _free_port(), name, dtype), nprocs=world, join=True)
+
+
+def _id_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from pathpack_b200.panels import share_comm_id
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        q.put((rank, share_comm_id()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_group_id_reaches_every_rank_over_gloo(world):
+    """The id of the split factorization's NCCL group (pp_comm_id, made on rank 0) reaches every rank intact."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    mp.start_processes(_id_worker, args=(world, _free_port(), q), nprocs=world, join=True, start_method="spawn")
+    got = dict(q.get() for _ in range(world))
+    assert sorted(got) == list(range(world))
+    assert all(len(v) == 128 and v == got[0] for v in got.values())
+    assert any(got[0])

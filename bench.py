@@ -944,7 +944,9 @@ def main():
         import torch.distributed as tdist
 
         torch.cuda.set_device(local)
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        # NVLink SHARP off for the process group and the library's group (its kernels use no multicast either)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
         if args.workload in STAR:
             run_star(args, rank, world, local)

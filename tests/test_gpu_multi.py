@@ -63,8 +63,9 @@ def _worker(rank, world, port, case, errq):
                 same(got, want, name, dtype, "rank %d %s %s" % (rank, case, what))
             B, _ = graphs.unit_columns(n, 64, seed=5, dtype=dtype, zero=s.zero(dtype), one=s.one(dtype))
             c0, kw = column_panels(64, world)[rank]
-            X = pp.lmul_(F, np.asfortranarray(B[:, c0:c0 + kw]))
-            same(X, O.lmul(B)[:, c0:c0 + kw], name, dtype, "rank %d %s lmul! panel" % (rank, case))
+            want = O.lmul(B)[:, c0:c0 + kw]
+            X = pp.lmul_(F, np.array(B[:, c0:c0 + kw], order="F"))  # a copy: lmul! works in place
+            same(X, want, name, dtype, "rank %d %s lmul! panel" % (rank, case))
             col0, ncols = column_panels(n, world)[rank]
             ncols = min(ncols, 96)
             E = np.full((n, ncols), s.zero(dtype), dtype=dtype, order="F")

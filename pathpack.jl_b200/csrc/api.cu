@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <condition_variable>
 #include <mutex>
 #include <thread>
 #include <cstdarg>
@@ -149,6 +150,29 @@ struct Part {
     int64_t d0 = 0, d1 = 0, l0 = 0, l1 = 0, w0 = 0, w1 = 0;
 };
 
+// Page-locked host memory (cudaHostAlloc), released with the handle.
+struct PinnedBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+    ~PinnedBuf() { release(); }
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    cudaError_t ensure(size_t b) {
+        if (b <= bytes && p) return cudaSuccess;
+        release();
+        if (t_alloc_budget && *t_alloc_budget >= 0 && (*t_alloc_budget)-- == 0) return cudaErrorMemoryAllocation;
+        cudaError_t e = cudaHostAlloc(&p, b, cudaHostAllocDefault);
+        if (e == cudaSuccess)
+            bytes = b;
+        else
+            cudaGetLastError();
+        return e;
+    }
+};
+
 struct pp_handle {
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -162,6 +186,8 @@ struct pp_handle {
     cudaEvent_t ev_bottom = nullptr, ev_factored = nullptr;
     cudaEvent_t copy_ev = nullptr;
     cudaEvent_t panel_ready[2] = {}, panel_copied[2] = {};  // double-buffered star panels to host memory
+    cudaEvent_t ring_ev[3] = {};  // star panels into pageable host memory: the pinned ring's slots filled
+    PinnedBuf ring;               // three panels of page-locked host memory (allocated on first use)
     bool factor_pending = false, solve_pending = false;  // enqueued, times not yet read
     // set while a plan (pp_plan_lmul) captures the handle's calls into a CUDA graph: no timing events, no
     // profiler, and no wait for the previous factorization (a graph launch is ordered as a whole)
@@ -323,6 +349,7 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
         e = cudaEventCreateWithFlags(&h->panel_ready[i], cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->panel_copied[i], cudaEventDisableTiming);
     }
+    for (int i = 0; i < 3 && e == cudaSuccess; i++) e = cudaEventCreateWithFlags(&h->ring_ev[i], cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) {
         pp_destroy(h);
@@ -358,6 +385,8 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
         if (h->panel_ready[i]) cudaEventDestroy(h->panel_ready[i]);
         if (h->panel_copied[i]) cudaEventDestroy(h->panel_copied[i]);
     }
+    for (int i = 0; i < 3; i++)
+        if (h->ring_ev[i]) cudaEventDestroy(h->ring_ev[i]);
     if (h->copy_stream) {
         cudaStreamSynchronize(h->copy_stream);
         cudaStreamDestroy(h->copy_stream);
@@ -2065,6 +2094,67 @@ extern "C" int32_t pp_rmul_t(pp_handle *h, void *B, int64_t ldb, int64_t k, int3
     return run_solve(h, B, ldb, k, where, 0, 1, "pp_rmul_t");
 }
 
+// Host threads that copy star panels out of the pinned ring into the caller's pageable array: every thread
+// copies its share of the columns of every panel, in panel order, while the GPU computes the next panels.
+struct RingCopier {
+    struct Job {
+        const unsigned char *src = nullptr;
+        unsigned char *dst = nullptr;
+        size_t col_bytes = 0, ldc_bytes = 0;
+        int w = 0;
+    };
+    int T;
+    std::vector<Job> jobs;
+    std::vector<int> done;  // threads finished, per panel
+    int posted = 0;
+    bool stop = false;
+    std::mutex mu;
+    std::condition_variable cv_post, cv_done;
+    std::vector<std::thread> th;
+
+    RingCopier(int nthreads, int64_t npanels) : T(nthreads), jobs(npanels), done(npanels, 0) {
+        for (int t = 0; t < T; t++) th.emplace_back([this, t] { run(t); });
+    }
+    ~RingCopier() {
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            stop = true;
+        }
+        cv_post.notify_all();
+        for (auto &x : th) x.join();
+    }
+    void run(int t) {
+        for (int p = 0;; p++) {
+            Job j;
+            {
+                std::unique_lock<std::mutex> lk(mu);
+                cv_post.wait(lk, [&] { return stop || posted > p; });
+                if (posted <= p) return;
+                j = jobs[p];
+            }
+            const int a = (int)((int64_t)j.w * t / T), b = (int)((int64_t)j.w * (t + 1) / T);
+            for (int c = a; c < b; c++) memcpy(j.dst + c * j.ldc_bytes, j.src + c * j.col_bytes, j.col_bytes);
+            {
+                std::lock_guard<std::mutex> lk(mu);
+                done[p]++;
+            }
+            cv_done.notify_all();
+        }
+    }
+    void post(int p, const Job &j) {
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            jobs[p] = j;
+            posted = p + 1;
+        }
+        cv_post.notify_all();
+    }
+    void wait(int p) {
+        std::unique_lock<std::mutex> lk(mu);
+        cv_done.wait(lk, [&] { return done[p] == T; });
+    }
+};
+
 extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where) {
     AllocScope alloc_scope(h);
     const char *who = "pp_star";
@@ -2117,6 +2207,36 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
         d_pos = h->star_map.as<int>();
         d_cmap = d_pos + ncols;
     }
+    // host output into pageable memory (not page-locked, not registered): the copy engine cannot write it at full
+    // speed, so each panel goes to a slot of a page-locked ring first and host threads copy it into C from there
+    // while the GPU computes the next panels; page-locked C takes the copies directly
+    bool use_ring = false;
+    if (where == PP_HOST) {
+        cudaPointerAttributes pa{};
+        if (cudaPointerGetAttributes(&pa, C) != cudaSuccess) cudaGetLastError();
+        use_ring = pa.type == cudaMemoryTypeUnregistered;
+    }
+    const size_t slot_bytes = es * (size_t)n * pw;
+    std::unique_ptr<RingCopier> copier;
+    if (use_ring) {
+        CK(h, h->ring.ensure(3 * slot_bytes), who);
+        const unsigned hw = std::thread::hardware_concurrency();
+        const int T = (int)std::max(1u, std::min(16u, hw ? hw : 4u));
+        try {
+            copier.reset(new RingCopier(T, (ncols + pw - 1) / pw));
+        } catch (const std::exception &) {
+            return fail(h, PP_ENOMEM, "%s: could not start the host copy threads", who);
+        }
+    }
+    auto ring_job = [&](int64_t p) {
+        RingCopier::Job j;
+        j.src = static_cast<const unsigned char *>(h->ring.p) + (size_t)(p % 3) * slot_bytes;
+        j.dst = static_cast<unsigned char *>(C) + es * (size_t)(p * pw) * (size_t)ldc;
+        j.col_bytes = es * (size_t)n;
+        j.ldc_bytes = es * (size_t)ldc;
+        j.w = (int)std::min<int64_t>(pw, ncols - p * pw);
+        return j;
+    };
     CK(h, cudaEventRecord(h->ev0, st), who);
     // host output: panel i is written to staging buffer i % 2 and copied to C on the copy stream while panel
     // i + 1 is computed; panel i + 2 waits for that copy before it reuses the buffer
@@ -2141,7 +2261,22 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
             CK(h, h->ops->rows_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
         h->prof.end(pi, st, 2.0 * n * w, 0);
         nl += 3;
-        if (where == PP_HOST) {
+        if (where == PP_HOST && use_ring) {
+            // slot panel % 3 of the ring: free once the host threads copied panel - 3 out of it
+            const int slot = (int)(panel % 3);
+            if (panel >= 3) copier->wait((int)(panel - 3));
+            CK(h, cudaEventRecord(h->panel_ready[buf], st), who);
+            CK(h, cudaStreamWaitEvent(h->copy_stream, h->panel_ready[buf], 0), who);
+            CK(h, cudaMemcpyAsync(static_cast<char *>(h->ring.p) + (size_t)slot * slot_bytes, stage, es * (size_t)n * w,
+                                  cudaMemcpyDeviceToHost, h->copy_stream),
+               who);
+            CK(h, cudaEventRecord(h->panel_copied[buf], h->copy_stream), who);
+            CK(h, cudaEventRecord(h->ring_ev[slot], h->copy_stream), who);
+            if (panel >= 1) {  // the previous panel has reached the ring (or will soon): hand it to the threads
+                CK(h, cudaEventSynchronize(h->ring_ev[(panel - 1) % 3]), who);
+                copier->post((int)(panel - 1), ring_job(panel - 1));
+            }
+        } else if (where == PP_HOST) {
             CK(h, cudaEventRecord(h->panel_ready[buf], st), who);
             CK(h, cudaStreamWaitEvent(h->copy_stream, h->panel_ready[buf], 0), who);
             CK(h, cudaMemcpy2DAsync(static_cast<char *>(C) + es * (size_t)c0 * ldc, es * ldc, stage, es * n, es * n, w,
@@ -2149,6 +2284,11 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
                who);
             CK(h, cudaEventRecord(h->panel_copied[buf], h->copy_stream), who);
         }
+    }
+    if (use_ring && panel >= 1) {
+        CK(h, cudaEventSynchronize(h->ring_ev[(panel - 1) % 3]), who);
+        copier->post((int)(panel - 1), ring_job(panel - 1));
+        for (int64_t p = std::max<int64_t>(0, panel - 3); p < panel; p++) copier->wait((int)p);
     }
     if (where == PP_HOST) {
         CK(h, cudaEventRecord(h->copy_ev, h->copy_stream), who);

@@ -230,47 +230,72 @@ __global__ void __launch_bounds__(256, sizeof(T) == 8 ? 2 : (FWD ? 4 : 3)) sweep
                 Dd[q * SW_DL + c] = (q < nv && c < nv) ? Te(r0 + q, r0 + c) : z;
             }
             __syncthreads();
-            const int src = lane & ~7;
-            for (int pass = 0; pass < 4; pass++) {
-                // lane (dc, dg) holds rows dg + 8 u of right-hand side dc; pivot 8 u + g lives in lane (dc, g)
-                const int dc = 16 * w + 4 * pass + (lane >> 3);
-                T y[8];
+            // blocked by 8 rows: per sub-block (in pivot order: ascending forward, descending backward) a thread per
+            // right-hand side solves the sub-block's 8 x 8 triangle in registers, then the CTA applies the
+            // sub-block's pivots to the block's remaining rows as a register-tiled product (4 right-hand sides x
+            // the 8 pivots per thread, k in pivot order), so most of the block's pairs run at the product's rate
+            const int nb8 = (nv + 7) >> 3;
+            for (int jj = 0; jj < nb8; jj++) {
+                const int J = FWD ? jj : nb8 - 1 - jj;
+                const int j0 = 8 * J, jn = min(8, nv - j0);
+                if (tid < SWW_CT) {
+                    T y[8];
 #pragma unroll
-                for (int u = 0; u < 8; u++) y[u] = Ys[(dg + 8 * u) * SWW_YL + dc];
-                if (FWD) {
+                    for (int r = 0; r < 8; r++) y[r] = r < jn ? Ys[(j0 + r) * SWW_YL + tid] : z;
+                    if (FWD) {
 #pragma unroll
-                    for (int u = 0; u < 8; u++)
                         for (int g = 0; g < 8; g++) {
-                            const int q = 8 * u + g;
-                            if (q >= nv) break;
-                            T yq = __shfl_sync(0xffffffffu, y[u], src | g);
-                            if (scale) yq = S::mul(yq, S::star(Dd[q * SW_DL + q]));
-                            if (dg == g) y[u] = yq;
-                        // rows dg + 8 v below pivot 8 u + g: v > u, or v == u and dg > g (u is unrolled, so only
-                        // slot u is tested); rows at or past nv hold values that are never pivots or stored
+                            if (g >= jn) break;
+                            T yq = y[g];
+                            if (scale) yq = S::mul(yq, S::star(Dd[(j0 + g) * SW_DL + j0 + g]));
+                            y[g] = yq;
 #pragma unroll
-                        for (int v = u; v < 8; v++)
-                            if (v > u || dg > g) y[v] = S::muladd(Dd[(dg + 8 * v) * SW_DL + q], yq, y[v]);
+                            for (int v = g + 1; v < 8; v++)
+                                if (v < jn) y[v] = S::muladd(Dd[(j0 + v) * SW_DL + j0 + g], yq, y[v]);
                         }
-                } else {
+                    } else {
 #pragma unroll
-                    for (int u = 7; u >= 0; u--)
                         for (int g = 7; g >= 0; g--) {
-                            const int q = 8 * u + g;
-                            if (q >= nv) continue;
-                            T yq = __shfl_sync(0xffffffffu, y[u], src | g);
-                            if (scale) yq = S::mul(S::star(Dd[q * SW_DL + q]), yq);
-                            if (dg == g) y[u] = yq;
-                        // rows dg + 8 v above pivot 8 u + g: v < u, or v == u and dg < g
+                            if (g >= jn) continue;
+                            T yq = y[g];
+                            if (scale) yq = S::mul(S::star(Dd[(j0 + g) * SW_DL + j0 + g]), yq);
+                            y[g] = yq;
 #pragma unroll
-                        for (int v = 0; v <= u; v++)
-                            if (v < u || dg < g) y[v] = S::muladd(Dd[(dg + 8 * v) * SW_DL + q], yq, y[v]);
+                            for (int v = 0; v < g; v++) y[v] = S::muladd(Dd[(j0 + v) * SW_DL + j0 + g], yq, y[v]);
                         }
-                }
+                    }
 #pragma unroll
-                for (int u = 0; u < 8; u++) Ys[(dg + 8 * u) * SWW_YL + dc] = y[u];
+                    for (int r = 0; r < 8; r++)
+                        if (r < jn) Ys[(j0 + r) * SWW_YL + tid] = y[r];
+                }
+                __syncthreads();
+                // the rows the sub-block's pivots act on: below it (forward) or above it (backward)
+                const int ra = FWD ? j0 + 8 : 0, rz = FWD ? nv : j0;
+                if (rz > ra) {
+                    const int cg = 4 * (tid & 31);  // right-hand sides cg .. cg + 3
+                    T yv[8][4];
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++)
+#pragma unroll
+                        for (int c = 0; c < 4; c++) yv[kk][c] = kk < jn ? Ys[(j0 + kk) * SWW_YL + cg + c] : z;
+                    for (int i = ra + (tid >> 5); i < rz; i += 8) {
+                        T d[8];
+#pragma unroll
+                        for (int kk = 0; kk < 8; kk++) d[kk] = kk < jn ? Dd[i * SW_DL + j0 + kk] : z;
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            T a = Ys[i * SWW_YL + cg + c];
+#pragma unroll
+                            for (int u = 0; u < 8; u++) {
+                                const int kk = FWD ? u : 7 - u;
+                                a = S::muladd(d[kk], yv[kk][c], a);
+                            }
+                            Ys[i * SWW_YL + cg + c] = a;
+                        }
+                    }
+                }
+                __syncthreads();
             }
-            __syncthreads();
             for (int e = tid; e < SW_RB * SWW_CT; e += 256) {
                 const int r = e / SWW_CT, c = e % SWW_CT;
                 if (r < nv && c0 + c < k) X[(int64_t)(rlo + r0 + r) * ldx + c0 + c] = Ys[r * SWW_YL + c];

@@ -11,6 +11,7 @@ import pytest
 import pathpack_b200 as pp
 from oracle.oracle import OracleLU
 from oracle import oracle as orc
+from pathpack_b200 import graphs
 from tests.helpers import CASES, EXACT, close, graph, same, weights
 
 pytestmark = pytest.mark.gpu
@@ -211,5 +212,30 @@ def test_wide_solves(gpu, name, dtype, k):
         same(pp.lmul_(F, B.copy(order="F")), O.lmul(B), name, dtype, "wide lmul k=%d" % k)
         R = np.asfortranarray(B.T)
         same(pp.rmul_(R.copy(order="F"), F), O.rmul(R), name, dtype, "wide rmul k=%d" % k)
+    finally:
+        F.close()
+
+
+def test_star_into_pageable_and_pinned_host_memory(gpu):
+    """Matrix(F) into host memory: a pageable array goes through the library's page-locked ring (host threads copy
+    each panel out while the GPU computes the next; four panels here, so the ring's three slots are reused) and a
+    page-locked array takes the device-to-host copies directly; both equal the star computed into device memory."""
+    import torch
+
+    n, I, J, W = graphs.grid2d(100, 100, 1.0, 10.0, seed=21, dtype=np.float64)
+    cp, rv, nz = graphs.csc(n, I, J, W)
+    S = pp.ssymbolic(n, cp, rv)
+    F = pp.B200SLU(pp.MinPlus(), np.float64, S, device=0).assemble_csc(cp, rv, nz).factor()
+    try:
+        pageable = F.star()
+        pinned = torch.empty((n, n), dtype=torch.float64).pin_memory()
+        F.star(out=pinned.numpy().T)  # the transpose of a row-major n x n array is column-major
+        dev = torch.empty((n, n), dtype=torch.float64, device="cuda:0").t()
+        F.star(out=dev)
+        want = dev.cpu().numpy()
+        assert np.array_equal(pageable.view(np.uint64), want.view(np.uint64))
+        assert np.array_equal(pinned.numpy().T.view(np.uint64), want.view(np.uint64))
+        part = F.star(5000, 4001)  # a column range that does not start a panel
+        assert np.array_equal(part.view(np.uint64), want[:, 5000:9001].view(np.uint64))
     finally:
         F.close()

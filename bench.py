@@ -823,7 +823,7 @@ def run_kernel(args, rank, world, local):
     peak = alu_peak(w["semiring"], w["dtype"], sms, float(pk.get("sm_max_mhz", 1965.0)))
     per_launch = ms / 1e3 / args.steps
     dmma = key == "config5b-f64"
-    roof = {"kernel": "getrf_reg_kernel" if key == "config5a" else ("gemm_dmma_kernel" if dmma else "gemm_kernel"),
+    roof = {"kernel": "getrf_reg_kernel" if key == "config5a" else ("gemm_dmma_tma_kernel" if dmma else "gemm_kernel"),
             "bound": "tensor" if dmma else "alu",
             "achieved": x["pairs"] / per_launch, "peak": peak, "unit": "pairs/s", "frac": x["pairs"] / per_launch / peak,
             "traffic": None,

@@ -18,6 +18,9 @@
 // and take k in increasing order, which for PlusProd is the order of the reference's sgemx2!.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <type_traits>
 
 #include "semiring.cuh"
@@ -326,6 +329,183 @@ __global__ void __launch_bounds__(128) gemm_dmma_kernel(int M, int N, int K, T *
             }
 }
 
+// ---- PlusProd Float64 with TMA-staged tiles
+//
+// gemm_dmma_kernel's warp tiling and DMMA fragments, with the k-chunks of A and B fetched by the tensor memory
+// accelerator (cp.async.bulk.tensor.2d) into a 4-stage shared-memory ring: one thread issues a stage's copies
+// and arms its "full" barrier with the byte count; the four warps wait on it (mbarrier try_wait), compute, and
+// arrive on the stage's "empty" barrier, after which the stage is refilled with chunk kt + 4.  No register
+// staging and no CTA barrier in the main loop.  The boxes are shaped so that the fragment loads are free of
+// bank conflicts without swizzling: A in boxes of 8 (m) x 16 (k) (a warp's A fragment, 8 m x 4 k, is 256
+// contiguous bytes), B in boxes of 4 (k) x 64 (n) (a B fragment, 4 k x 8 n, likewise).  Out-of-range elements
+// are filled with zeros by the copy (the PlusProd zero).  The tensor maps cover this GPU's memory only and
+// no copy uses cluster multicast.  Every mbarrier wait is bounded (2 s of global time): one that runs out sets
+// g_gemm_err, fills the CTA's tile of C with NaN, waits (bounded) for the copies it issued, and returns.
+constexpr int DT_STAGES = 4, DT_BK = 16;
+constexpr int DT_A_ELEMS = 64 * DT_BK, DT_B_ELEMS = DT_BK * 64;  // doubles per stage
+constexpr unsigned DT_STAGE_BYTES = 8u * (DT_A_ELEMS + DT_B_ELEMS);
+constexpr size_t dmma_tma_smem = 128 + (size_t)DT_STAGES * DT_STAGE_BYTES + 2 * DT_STAGES * sizeof(unsigned long long);
+
+__device__ int g_gemm_err;
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long *bar, unsigned phase) {
+    unsigned long long t0 = 0;
+    for (unsigned it = 0;; it++) {
+        unsigned ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(phase)
+            : "memory");
+        if (ok) return true;
+        if ((it & 63) == 0) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (it == 0)
+                t0 = t;
+            else if (t - t0 > 2000000000ull)
+                return false;
+        }
+    }
+}
+
+template <typename T>  // T = double
+__global__ void __launch_bounds__(128) gemm_dmma_tma_kernel(int M, int N, int K, T *__restrict__ C, int64_t ldc,
+                                                            const __grid_constant__ CUtensorMap mapA,
+                                                            const __grid_constant__ CUtensorMap mapB) {
+    static_assert(std::is_same<T, double>::value, "DMMA f64");
+    extern __shared__ __align__(128) unsigned char dt_smem[];
+    unsigned char *base = dt_smem + ((128 - (smem_u32(dt_smem) & 127)) & 127);
+    double *sA = reinterpret_cast<double *>(base);             // [stage][8 boxes][16 k][8 m]
+    double *sB = sA + DT_STAGES * DT_A_ELEMS;                  // [stage][4 boxes][64 n][4 k]
+    unsigned long long *full = reinterpret_cast<unsigned long long *>(sB + DT_STAGES * DT_B_ELEMS);
+    unsigned long long *empty = full + DT_STAGES;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int wm = (w & 1) * 32, wn = (w >> 1) * 32;
+    const int g = lane >> 2, q = lane & 3;
+    const int m0 = blockIdx.x * DM_BM, n0 = blockIdx.y * DM_BN;
+    const int nk = (K + DT_BK - 1) / DT_BK;
+    double acc[4][4][2];
+#pragma unroll
+    for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+        for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int m = m0 + wm + mt * 8 + g, n = n0 + wn + nt * 8 + 2 * q + h;
+                acc[mt][nt][h] = (m < M && n < N) ? C[(int64_t)m + (int64_t)n * ldc] : 0.0;
+            }
+    if (tid == 0) {
+        for (int st = 0; st < DT_STAGES; st++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(full + st)) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(smem_u32(empty + st)) : "memory");
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    auto issue = [&](int kt) {  // thread 0: chunk kt into stage kt % DT_STAGES
+        const int st = kt % DT_STAGES;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(full + st)),
+                     "r"(DT_STAGE_BYTES)
+                     : "memory");
+        const int k0 = kt * DT_BK;
+#pragma unroll
+        for (int i = 0; i < 8; i++)  // A: box (m0 + 8 i .. + 8, k0 .. k0 + 16)
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                ::"r"(smem_u32(sA + st * DT_A_ELEMS + i * 128)), "l"(&mapA), "r"(m0 + 8 * i), "r"(k0),
+                "r"(smem_u32(full + st))
+                : "memory");
+#pragma unroll
+        for (int j = 0; j < 4; j++)  // B: box (k0 + 4 j .. + 4, n0 .. n0 + 64)
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                ::"r"(smem_u32(sB + st * DT_B_ELEMS + j * 256)), "l"(&mapB), "r"(k0 + 4 * j), "r"(n0),
+                "r"(smem_u32(full + st))
+                : "memory");
+    };
+    int issued = 0, consumed = 0;
+    if (tid == 0)
+        for (; issued < DT_STAGES && issued < nk; issued++) issue(issued);
+    bool bad = false;
+    for (int kt = 0; kt < nk; kt++) {
+        const int st = kt % DT_STAGES;
+        const unsigned ph = (unsigned)(kt / DT_STAGES) & 1u;
+        if (!mbar_wait_bounded(full + st, ph)) {
+            bad = true;
+            break;
+        }
+        consumed = kt + 1;
+        const double *a = sA + st * DT_A_ELEMS, *b = sB + st * DT_B_ELEMS;
+#pragma unroll
+        for (int ks = 0; ks < DT_BK; ks += 4) {
+            double af[4], bf[4];
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++) af[mt] = a[((wm >> 3) + mt) * 128 + (ks + q) * 8 + g];
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++) bf[nt] = b[(ks >> 2) * 256 + (wn + nt * 8 + g) * 4 + q];
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++) dmma_8x8x4(acc[mt][nt][0], acc[mt][nt][1], af[mt], bf[nt]);
+        }
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(empty + st)) : "memory");
+        if (tid == 0 && issued < nk) {  // refill this stage once every warp is done with it
+            if (!mbar_wait_bounded(empty + st, ph)) {
+                bad = true;
+                break;
+            }
+            issue(issued++);
+        }
+    }
+    if (bad) {
+        atomicExch(&g_gemm_err, 1);
+        if (tid == 0)  // the copies still in flight land in this CTA's shared memory: wait for them (bounded)
+            for (int kt = consumed; kt < issued; kt++)
+                if (!mbar_wait_bounded(full + kt % DT_STAGES, (unsigned)(kt / DT_STAGES) & 1u)) break;
+    }
+#pragma unroll
+    for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+        for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int m = m0 + wm + mt * 8 + g, n = n0 + wn + nt * 8 + 2 * q + h;
+                if (m < M && n < N) C[(int64_t)m + (int64_t)n * ldc] = bad ? CUDART_NAN : acc[mt][nt][h];
+            }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the library links no libcuda)
+static inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) != cudaSuccess ||
+            qr != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        cudaGetLastError();
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// a 2D tensor map of a column-major double matrix (inner x outer, leading dimension ld) with the given box
+static inline bool make_map(CUtensorMap *map, const double *ptr, int64_t inner, int64_t outer, int64_t ld,
+                            unsigned box_inner, unsigned box_outer) {
+    const auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(double)};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double *>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // host launcher
 template <int SR, typename T>
 cudaError_t launch_gemm(int64_t M, int64_t N, int64_t K, T *C, int64_t ldc, const T *A, int64_t lda, const T *B,
@@ -334,7 +514,26 @@ cudaError_t launch_gemm(int64_t M, int64_t N, int64_t K, T *C, int64_t ldc, cons
     if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
     if constexpr (SR == PLUSPROD && std::is_same<T, double>::value) {
         dim3 grid((unsigned)((M + DM_BM - 1) / DM_BM), (unsigned)((N + DM_BN - 1) / DM_BN));
-        gemm_dmma_kernel<T><<<grid, 128, 0, st>>>((int)M, (int)N, (int)K, C, ldc, A, lda, B, ldb);
+        // TMA-staged when the operands allow tensor maps: 16-byte aligned bases, leading dimensions of whole
+        // 16-byte units; otherwise the register-staged kernel
+        CUtensorMap ma, mb;
+        const bool tma = ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0 &&
+                         (lda & 1) == 0 && (ldb & 1) == 0 && make_map(&ma, A, M, K, lda, 8, DT_BK) &&
+                         make_map(&mb, B, K, N, ldb, 4, DM_BN);
+        if (tma) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            static bool attr[64] = {};
+            if (dev < 64 && !attr[dev]) {
+                cudaError_t e = cudaFuncSetAttribute(gemm_dmma_tma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int)dmma_tma_smem);
+                if (e != cudaSuccess) return e;
+                attr[dev] = true;
+            }
+            gemm_dmma_tma_kernel<T><<<grid, 128, dmma_tma_smem, st>>>((int)M, (int)N, (int)K, C, ldc, ma, mb);
+        } else {
+            gemm_dmma_kernel<T><<<grid, 128, 0, st>>>((int)M, (int)N, (int)K, C, ldc, A, lda, B, ldb);
+        }
         return cudaGetLastError();
     }
     int dev = 0;

@@ -28,8 +28,12 @@ def torch_dt(dtype):
 
 
 @pytest.mark.parametrize("name,dtype", CASES)
-@pytest.mark.parametrize("mnk", [(1, 1, 1), (7, 5, 3), (33, 65, 17), (130, 129, 40), (257, 200, 129)])
+@pytest.mark.parametrize("mnk", [(1, 1, 1), (7, 5, 3), (33, 65, 17), (130, 129, 40), (257, 200, 129), (2, 4, 6),
+                                 (192, 66, 96), (64, 130, 258)])
 def test_gemm(gpu, name, dtype, mnk):
+    """C (+)= A (x) B against the oracle.  For PlusProd Float64 the sizes with even leading dimensions (m and k
+    even) run the TMA-staged tensor-core kernel, with partial tiles in m, n and k; the others the
+    register-staged one."""
     import torch
 
     m, n, k = mnk

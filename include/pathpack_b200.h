@@ -171,6 +171,15 @@ int32_t pp_rmul_t(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t where);
    several GPUs share one star. */
 int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where);
 
+/* Columns cols[0 .. ncols-1] of the star A* (original labels; any order, repeats allowed) into C (n x ncols,
+   column-major, leading dimension ldc): the closure's entries towards a set of targets. */
+int32_t pp_star_cols(pp_handle *h, void *C, int64_t ldc, const int64_t *cols, int64_t ncols, int32_t where);
+
+/* Rows sources[0 .. k-1] of the star A* (original labels) into C (k x n, column-major, leading dimension ldc >= k):
+   the closure from a set of sources, apsp_gpu(A, sources) of the reference (ext/PATHPACKCUDAExt/api.jl:103-154),
+   computed as rmul! of unit rows. */
+int32_t pp_star_rows(pp_handle *h, void *C, int64_t ldc, const int64_t *sources, int64_t k, int32_t where);
+
 /* Wait for the handle's stream; reports a device error of the calls enqueued since the last wait. */
 int32_t pp_sync(pp_handle *h);
 

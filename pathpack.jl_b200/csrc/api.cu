@@ -2097,7 +2097,7 @@ extern "C" int32_t pp_rmul_t(pp_handle *h, void *B, int64_t ldb, int64_t k, int3
 // Host threads that copy star panels out of the pinned ring into the caller's pageable array: every thread
 // copies its share of the columns of every panel, in panel order, while the GPU computes the next panels.
 struct RingCopier {
-    struct Job {
+    struct Job {  // w runs of col_bytes: run c from src + c * col_bytes to dst + c * ldc_bytes
         const unsigned char *src = nullptr;
         unsigned char *dst = nullptr;
         size_t col_bytes = 0, ldc_bytes = 0;
@@ -2155,20 +2155,27 @@ struct RingCopier {
     }
 };
 
-extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where) {
+// Columns of A* into C (n x ncols): col0 .. col0 + ncols - 1, or cols[0 .. ncols - 1] (original labels) when cols is
+// given.  rows: the rows cols[0 .. ncols - 1] of A* into C (ncols x n), rmul! of unit rows.
+static int32_t star_impl(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, const int64_t *cols,
+                         int32_t where, const char *who, bool rows = false) {
     AllocScope alloc_scope(h);
-    const char *who = "pp_star";
-    if (!h) return fail(nullptr, PP_EINVAL, "pp_star: null handle");
-    if (!h->factored) return fail(h, PP_ESTATE, "pp_star: no factorization (call pp_factor)");
+    if (!h) return fail(nullptr, PP_EINVAL, "%s: null handle", who);
+    if (!h->factored) return fail(h, PP_ESTATE, "%s: no factorization (call pp_factor)", who);
     const int n = h->hp.n;
-    if (col0 < 0 || ncols < 0 || col0 + ncols > n) return fail(h, PP_EINVAL, "pp_star: columns out of range");
-    if (where != PP_HOST && where != PP_DEVICE) return fail(h, PP_EINVAL, "pp_star: where");
+    if (cols) col0 = 0;
+    if (col0 < 0 || ncols < 0 || (cols ? ncols > INT32_MAX : col0 + ncols > n))
+        return fail(h, PP_EINVAL, "%s: columns out of range", who);
+    if (where != PP_HOST && where != PP_DEVICE) return fail(h, PP_EINVAL, "%s: where", who);
     if (ncols == 0) {
         ok(h);
         return PP_OK;
     }
-    if (!C || ldc < n) return fail(h, PP_EINVAL, "pp_star: C / ldc");
-    CK(h, cudaSetDevice(h->device), "pp_star");
+    if (!C || ldc < (rows ? ncols : n)) return fail(h, PP_EINVAL, "%s: C / ldc", who);
+    if (cols)
+        for (int64_t c = 0; c < ncols; c++)
+            if (cols[c] < 0 || cols[c] >= n) return fail(h, PP_EINVAL, "%s: column %lld out of range", who, (long long)cols[c]);
+    CK(h, cudaSetDevice(h->device), who);
     const size_t es = h->ops->esize;
     // panel width, a multiple of 32 columns: wide panels give the sweeps of the top fronts, whose 64-row blocks
     // form dependency chains, many independent column tiles to run beside each chain (about 2 GB of right-hand
@@ -2191,21 +2198,30 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
     // device output: the requested columns are taken in elimination order (sorted positions) and each panel
     // column is written to its own column of C, so the 32 sources of a tile lie in a few neighbouring subtrees
     // and the forward sweep skips every front outside their root paths (its zero test is per tile)
-    const bool mapped = where == PP_DEVICE && ncols > 32;
+    const bool mapped = !rows && where == PP_DEVICE && ncols > 32;
     const int *d_pos = nullptr, *d_cmap = nullptr;
+    std::vector<int> &hm = h->star_host;
     if (mapped) {
-        std::vector<int> &hm = h->star_host;
+        // hm[0 .. ncols): the positions of the sources in elimination order; hm[ncols + j]: the output column
         hm.resize(2 * (size_t)ncols);
-        for (int64_t c = 0; c < ncols; c++) hm[ncols + c] = (int)(col0 + c);
-        std::sort(hm.begin() + ncols, hm.end(), [&](int a, int b) { return h->invp[a] < h->invp[b]; });
+        std::vector<int> order(ncols);
+        for (int64_t c = 0; c < ncols; c++) order[c] = (int)c;
+        auto src = [&](int c) { return (int)(cols ? cols[c] : col0 + c); };
+        std::sort(order.begin(), order.end(), [&](int a, int b) { return h->invp[src(a)] < h->invp[src(b)]; });
         for (int64_t c = 0; c < ncols; c++) {
-            hm[c] = h->invp[hm[ncols + c]];
-            hm[ncols + c] -= (int)col0;
+            hm[c] = h->invp[src(order[c])];
+            hm[ncols + c] = order[c];
         }
+    } else if (cols) {
+        // caller order: hm[j] the position of source j
+        hm.resize((size_t)ncols);
+        for (int64_t c = 0; c < ncols; c++) hm[c] = h->invp[cols[c]];
+    }
+    if (mapped || cols) {
         CK(h, h->star_map.ensure(sizeof(int) * hm.size()), who);
         CK(h, cudaMemcpyAsync(h->star_map.p, hm.data(), sizeof(int) * hm.size(), cudaMemcpyHostToDevice, st), who);
         d_pos = h->star_map.as<int>();
-        d_cmap = d_pos + ncols;
+        if (mapped) d_cmap = d_pos + ncols;
     }
     // host output into pageable memory (not page-locked, not registered): the copy engine cannot write it at full
     // speed, so each panel goes to a slot of a page-locked ring first and host threads copy it into C from there
@@ -2230,11 +2246,18 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
     }
     auto ring_job = [&](int64_t p) {
         RingCopier::Job j;
+        const int w = (int)std::min<int64_t>(pw, ncols - p * pw);
         j.src = static_cast<const unsigned char *>(h->ring.p) + (size_t)(p % 3) * slot_bytes;
-        j.dst = static_cast<unsigned char *>(C) + es * (size_t)(p * pw) * (size_t)ldc;
-        j.col_bytes = es * (size_t)n;
         j.ldc_bytes = es * (size_t)ldc;
-        j.w = (int)std::min<int64_t>(pw, ncols - p * pw);
+        if (rows) {  // n runs of w elements: row block p * pw .. of every column of C
+            j.dst = static_cast<unsigned char *>(C) + es * (size_t)(p * pw);
+            j.col_bytes = es * (size_t)w;
+            j.w = n;
+        } else {  // w columns of n elements
+            j.dst = static_cast<unsigned char *>(C) + es * (size_t)(p * pw) * (size_t)ldc;
+            j.col_bytes = es * (size_t)n;
+            j.w = w;
+        }
         return j;
     };
     CK(h, cudaEventRecord(h->ev0, st), who);
@@ -2245,18 +2268,22 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
         const int w = (int)std::min<int64_t>(pw, ncols - c0);
         const int buf = (int)(panel & 1);
         CK(h, h->ops->fill_zero(h->X.p, (int64_t)n * ldx, st), who);
-        if (mapped)
+        if (d_pos)
             CK(h, h->ops->unit_positions(h->X.p, ldx, d_pos + c0, w, st), who);
         else
             CK(h, h->ops->unit_sources(h->X.p, ldx, h->hp.dev.invp, col0 + c0, w, st), who);
-        CK(h, h->ops->solve(h->hp, values_of(h), 1, h->X.p, ldx, w, st, &nl), who);
+        CK(h, h->ops->solve(h->hp, values_of(h), rows ? 0 : 1, h->X.p, ldx, w, st, &nl), who);
         void *stage = static_cast<char *>(h->stage_out.p) + (size_t)buf * es * (size_t)n * pw;
-        void *dst = where == PP_HOST ? stage : (void *)(static_cast<char *>(C) + es * (size_t)c0 * ldc);
-        const int64_t lddst = where == PP_HOST ? n : ldc;
+        // the panel's first element in C: column c0 (n x ncols), or row c0 (ncols x n)
+        char *cpan = static_cast<char *>(C) + es * (size_t)c0 * (rows ? 1 : (size_t)ldc);
+        void *dst = where == PP_HOST ? stage : (void *)cpan;
+        const int64_t lddst = where == PP_HOST ? (rows ? w : n) : ldc;
         if (where == PP_HOST && panel >= 2) CK(h, cudaStreamWaitEvent(st, h->panel_copied[buf], 0), who);
         const int pi = h->prof.begin(K_PERMUTE, st);
         if (mapped)
             CK(h, h->ops->rows_out_mapped(C, ldc, h->X.p, ldx, h->hp.dev.invp, d_cmap + c0, n, w, st), who);
+        else if (rows)
+            CK(h, h->ops->cols_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
         else
             CK(h, h->ops->rows_out(dst, lddst, h->X.p, ldx, h->hp.dev.invp, n, w, st), who);
         h->prof.end(pi, st, 2.0 * n * w, 0);
@@ -2279,9 +2306,12 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
         } else if (where == PP_HOST) {
             CK(h, cudaEventRecord(h->panel_ready[buf], st), who);
             CK(h, cudaStreamWaitEvent(h->copy_stream, h->panel_ready[buf], 0), who);
-            CK(h, cudaMemcpy2DAsync(static_cast<char *>(C) + es * (size_t)c0 * ldc, es * ldc, stage, es * n, es * n, w,
-                                    cudaMemcpyDeviceToHost, h->copy_stream),
-               who);
+            if (rows)  // n columns of w elements
+                CK(h, cudaMemcpy2DAsync(cpan, es * ldc, stage, es * w, es * w, n, cudaMemcpyDeviceToHost, h->copy_stream),
+                   who);
+            else
+                CK(h, cudaMemcpy2DAsync(cpan, es * ldc, stage, es * n, es * n, w, cudaMemcpyDeviceToHost, h->copy_stream),
+                   who);
             CK(h, cudaEventRecord(h->panel_copied[buf], h->copy_stream), who);
         }
     }
@@ -2304,6 +2334,20 @@ extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int
     }
     ok(h);
     return PP_OK;
+}
+
+extern "C" int32_t pp_star(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64_t ncols, int32_t where) {
+    return star_impl(h, C, ldc, col0, ncols, nullptr, where, "pp_star");
+}
+
+extern "C" int32_t pp_star_cols(pp_handle *h, void *C, int64_t ldc, const int64_t *cols, int64_t ncols, int32_t where) {
+    if (ncols > 0 && !cols) return fail(h, PP_EINVAL, "pp_star_cols: null cols");
+    return star_impl(h, C, ldc, 0, ncols, cols, where, "pp_star_cols");
+}
+
+extern "C" int32_t pp_star_rows(pp_handle *h, void *C, int64_t ldc, const int64_t *sources, int64_t k, int32_t where) {
+    if (k > 0 && !sources) return fail(h, PP_EINVAL, "pp_star_rows: null sources");
+    return star_impl(h, C, ldc, 0, k, sources, where, "pp_star_rows", true);
 }
 
 extern "C" int32_t pp_sync(pp_handle *h) {

@@ -67,6 +67,8 @@ SIGNATURES = {
     "pp_lmul_static": (C.c_int32, [_P, _P, C.c_int64, C.c_int64]),
     "pp_star": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int64, C.c_int32]),
     "pp_sync": (C.c_int32, [_P]),
+    "pp_star_cols": (C.c_int32, [_P, _P, C.c_int64, _I64P, C.c_int64, C.c_int32]),
+    "pp_star_rows": (C.c_int32, [_P, _P, C.c_int64, _I64P, C.c_int64, C.c_int32]),
     "pp_comm_id": (C.c_int32, [C.c_void_p]),
     "pp_comm_init": (C.c_int32, [_P, C.c_void_p, C.c_int32, C.c_int32]),
     "pp_plan_lmul": (C.c_int32, [_P, _P, _P, _P, C.c_int64, C.c_int64, C.POINTER(_P)]),

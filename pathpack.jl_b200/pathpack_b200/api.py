@@ -269,6 +269,36 @@ class B200SLU:
         return out
 
 
+def star_cols(F, cols, out=None):
+    """Columns `cols` of A* (original labels, any order) as an n x len(cols) column-major array (pp_star_cols);
+    `out` may be a column-major CUDA tensor."""
+    cols = np.ascontiguousarray(cols, dtype=np.int64)
+    n, k = F.S.n, len(cols)
+    if out is None:
+        out = np.empty((n, k), dtype=F.dtype, order="F")
+    if hasattr(out, "data_ptr"):
+        check(lib().pp_star_cols(F._h, vptr(out), out.stride(1), i64ptr(cols), k, PP_DEVICE), F._h)
+        F.sync()
+    else:
+        check(lib().pp_star_cols(F._h, vptr(out), out.shape[0], i64ptr(cols), k, PP_HOST), F._h)
+    return out
+
+
+def star_rows(F, sources, out=None):
+    """Rows `sources` of A* (the closure from a set of sources; apsp_gpu(A, sources) of the reference) as a
+    len(sources) x n column-major array (pp_star_rows); `out` may be a column-major CUDA tensor."""
+    sources = np.ascontiguousarray(sources, dtype=np.int64)
+    n, k = F.S.n, len(sources)
+    if out is None:
+        out = np.empty((k, n), dtype=F.dtype, order="F")
+    if hasattr(out, "data_ptr"):
+        check(lib().pp_star_rows(F._h, vptr(out), out.stride(1), i64ptr(sources), k, PP_DEVICE), F._h)
+        F.sync()
+    else:
+        check(lib().pp_star_rows(F._h, vptr(out), out.shape[0], i64ptr(sources), k, PP_HOST), F._h)
+    return out
+
+
 class Plan:
     """A captured refactor + lmul! step of a B200SLU (see B200SLU.plan_lmul)."""
 

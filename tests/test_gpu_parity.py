@@ -243,3 +243,37 @@ def test_star_into_pageable_and_pinned_host_memory(gpu):
         assert np.array_equal(part.view(np.uint64), want[:, 5000:9001].view(np.uint64))
     finally:
         F.close()
+
+
+@pytest.mark.parametrize("name,dtype", [("MinPlus", np.float64), ("MaxMin", np.float32), ("OrAnd", np.int32),
+                                        ("PlusProd", np.float64), ("MinPlus", np.int32)])
+def test_star_columns_and_rows_of_a_source_set(gpu, name, dtype):
+    """pp_star_cols / pp_star_rows: the star towards / from a set of vertices (unsorted, with a repeat), into
+    host memory (pageable: the page-locked ring) and device memory; columns against lmul! of unit columns, rows
+    against rmul! of unit rows, both the oracle's (rows: the apsp_gpu(A, sources) of the reference)."""
+    import torch
+
+    n, I, J, _ = graphs.grid2d(60, 50, seed=7)
+    W = weights(name, dtype, len(I), 8)
+    cp, rv, nz = graphs.csc(n, I, J, W)
+    S = pp.ssymbolic(n, cp, rv)
+    F = pp.B200SLU(SR[name], dtype, S, device=0).assemble_csc(cp, rv, nz).factor()
+    O = OracleLU(name, dtype, S).assemble(cp, rv, nz).factor()
+    try:
+        rng = np.random.default_rng(3)
+        src = rng.choice(n, 700, replace=False)
+        src = np.concatenate([src, src[:1]])  # a repeated vertex
+        z, one = SR[name].zero(dtype), SR[name].one(dtype)
+        E = np.full((n, len(src)), z, dtype=dtype, order="F")
+        E[src, np.arange(len(src))] = one
+        want_c = O.lmul(E)
+        want_r = O.rmul(np.asfortranarray(E.T))
+        same(pp.star_cols(F, src), want_c, name, dtype, "star columns (host)")
+        same(pp.star_rows(F, src), want_r, name, dtype, "star rows (host)")
+        td = torch_dt(dtype)
+        Dc = torch.empty((len(src), n), dtype=td, device="cuda:0").t()
+        same(pp.star_cols(F, src, out=Dc).cpu().numpy(), want_c, name, dtype, "star columns (device)")
+        Dr = torch.empty((n, len(src)), dtype=td, device="cuda:0").t()
+        same(pp.star_rows(F, src, out=Dr).cpu().numpy(), want_r, name, dtype, "star rows (device)")
+    finally:
+        F.close()

@@ -201,6 +201,30 @@ int32_t pp_comm_id(void *id);
 /* Join the handle as `rank` of `nranks` (nranks = 1 leaves any group); blocks until every rank has joined. */
 int32_t pp_comm_init(pp_handle *h, const void *id, int32_t nranks, int32_t rank);
 
+/* ---- several GPUs driven by one process: a multi-device handle ----
+   A pp_multi holds a handle per device of `devices`, joined into one group as above; each call runs the
+   corresponding call on every device at once (one host thread per device, as the reference's multi-GPU driver
+   runs one task per device, ext/PATHPACKCUDAExt/multigpu.jl:432-450) and returns the first failure (message:
+   pp_last_error(NULL) on the calling thread).  pp_multi_lmul / pp_multi_rmul split the k right-hand sides of a
+   host B into one contiguous panel per device (trans = 1: the transposed factor, as pp_lmul_t / pp_rmul_t);
+   pp_multi_star splits the columns col0 .. col0+ncols-1 of A* into one contiguous panel per device, written into
+   the host array C (n x ncols).  pp_multi_handle gives a device's handle for the one-device calls (device
+   outputs: pp_star into each device's own memory). */
+typedef struct pp_multi pp_multi;
+int32_t pp_multi_create(const int32_t *devices, int32_t ndev, const pp_options *opt, pp_multi **m);
+int32_t pp_multi_destroy(pp_multi *m);
+int32_t pp_multi_handle(pp_multi *m, int32_t i, pp_handle **h);
+int32_t pp_multi_set_structure(pp_multi *m, int64_t n, int64_t nf, int64_t nB, const int64_t *Rptr,
+                               const int64_t *Sptr, const int64_t *Stgt, const int64_t *Bptr, const int64_t *Fptr,
+                               const int64_t *Nptr, const int64_t *Ntgt, const int64_t *perm, int32_t base);
+int32_t pp_multi_assemble(pp_multi *m, int32_t semiring, int32_t dtype, const int64_t *colptr, const int64_t *rowval,
+                          const void *nzval, int32_t base);
+/* the split factorization on every device; returns when it is complete everywhere */
+int32_t pp_multi_factor(pp_multi *m);
+int32_t pp_multi_lmul(pp_multi *m, void *B, int64_t ldb, int64_t k, int32_t trans);
+int32_t pp_multi_rmul(pp_multi *m, void *B, int64_t ldb, int64_t k, int32_t trans);
+int32_t pp_multi_star(pp_multi *m, void *C, int64_t ldc, int64_t col0, int64_t ncols);
+
 /* ---- lmul! allocating nothing (no counterpart in the reference) ----
    pp_lmul_static is pp_lmul for device-resident B (n x k, leading dimension ldb, on the handle's device) that
    allocates nothing: no device memory, no host staging, no profiler events.  It is for callers that must not

@@ -2076,6 +2076,8 @@ int32_t pp_internal_device(const pp_handle *h, int *device) {
 
 int32_t pp_internal_fail(pp_handle *h, int32_t code, const char *msg) { return fail(h, code, "%s", msg); }
 
+size_t pp_internal_esize(const pp_handle *h) { return h && h->ops ? h->ops->esize : 0; }
+
 // scratch bytes of pp_internal_lmul_scratch for k right-hand sides: the workspace (rounded to 256 bytes)
 // and the counters of ensure_sync
 size_t pp_internal_lmul_scratch_bytes(const pp_handle *h, int64_t k) {

@@ -16,3 +16,5 @@ PP_INTERNAL size_t pp_internal_lmul_scratch_bytes(const pp_handle *h, int64_t k)
 // the handle's device; an error return that records `msg` as the handle's last error
 PP_INTERNAL int32_t pp_internal_device(const pp_handle *h, int *device);
 PP_INTERNAL int32_t pp_internal_fail(pp_handle *h, int32_t code, const char *msg);
+// the element size of the handle's semiring and type (0 before pp_assemble / pp_set_values)
+PP_INTERNAL size_t pp_internal_esize(const pp_handle *h);

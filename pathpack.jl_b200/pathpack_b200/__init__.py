@@ -6,5 +6,5 @@ Matrix) and its semirings on top of it.  Import it with pathpack.jl_b200/ on sys
 """
 from .semiring import MinPlus, MaxPlus, MaxMin, MinMax, MaxProd, PlusProd, OrAnd, supported  # noqa: F401
 from .symbolic import Structure, ssymbolic  # noqa: F401
-from .api import B200SLU, TransposedSLU, comm_id, mlu, mstar, lu_, lmul_, rmul_, Matrix, star_cols, star_rows, transpose  # noqa: F401
+from .api import B200SLU, MultiSLU, TransposedSLU, comm_id, mlu, mstar, lu_, lmul_, rmul_, Matrix, star_cols, star_rows, transpose  # noqa: F401
 from ._lib import PPError, lib  # noqa: F401

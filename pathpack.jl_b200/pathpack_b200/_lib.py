@@ -71,6 +71,15 @@ SIGNATURES = {
     "pp_star_rows": (C.c_int32, [_P, _P, C.c_int64, _I64P, C.c_int64, C.c_int32]),
     "pp_comm_id": (C.c_int32, [C.c_void_p]),
     "pp_comm_init": (C.c_int32, [_P, C.c_void_p, C.c_int32, C.c_int32]),
+    "pp_multi_create": (C.c_int32, [C.POINTER(C.c_int32), C.c_int32, C.c_void_p, C.POINTER(_P)]),
+    "pp_multi_destroy": (C.c_int32, [_P]),
+    "pp_multi_handle": (C.c_int32, [_P, C.c_int32, C.POINTER(_P)]),
+    "pp_multi_set_structure": (C.c_int32, [_P, C.c_int64, C.c_int64, C.c_int64] + [_I64P] * 8 + [C.c_int32]),
+    "pp_multi_assemble": (C.c_int32, [_P, C.c_int32, C.c_int32, _I64P, _I64P, _P, C.c_int32]),
+    "pp_multi_factor": (C.c_int32, [_P]),
+    "pp_multi_lmul": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int32]),
+    "pp_multi_rmul": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int32]),
+    "pp_multi_star": (C.c_int32, [_P, _P, C.c_int64, C.c_int64, C.c_int64]),
     "pp_plan_lmul": (C.c_int32, [_P, _P, _P, _P, C.c_int64, C.c_int64, C.POINTER(_P)]),
     "pp_plan_launch": (C.c_int32, [_P]),
     "pp_plan_launches": (C.c_int32, [_P, C.POINTER(C.c_int64)]),

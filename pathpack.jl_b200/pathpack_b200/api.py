@@ -350,6 +350,71 @@ def transpose(F):
     return F.parent if isinstance(F, TransposedSLU) else TransposedSLU(F)
 
 
+class MultiSLU:
+    """One matrix factored on several GPUs by one process (pp_multi): a handle per device joined into one group;
+    factor() splits the factorization, lmul_/rmul_/star split the right-hand sides or columns by device."""
+
+    def __init__(self, s, dtype, structure, devices, **options):
+        dtype = np.dtype(dtype)
+        if not sr.supported(s, dtype):
+            raise TypeError("%r over %s is not supported (pp_check_semiring)" % (s, dtype))
+        self.s, self.dtype, self.S, self.devices = s, dtype, structure, list(devices)
+        self._dt = sr.DTYPES[dtype]
+        devs = (C.c_int32 * len(self.devices))(*self.devices)
+        m = C.c_void_p()
+        check(lib().pp_multi_create(devs, len(self.devices), C.byref(_options(options)) if options else None,
+                                    C.byref(m)))
+        self._m = m
+        S = structure
+        check(lib().pp_multi_set_structure(m, S.n, S.nf, S.nB, i64ptr(S.Rptr), i64ptr(S.Sptr), i64ptr(S.Stgt),
+                                           i64ptr(S.Bptr), i64ptr(S.Fptr), i64ptr(S.Nptr), i64ptr(S.Ntgt),
+                                           i64ptr(S.perm), 0))
+
+    def close(self):
+        if getattr(self, "_m", None):
+            lib().pp_multi_destroy(self._m)
+            self._m = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def assemble_csc(self, colptr, rowval, nzval):
+        cp = np.ascontiguousarray(colptr, dtype=np.int64)
+        rv = np.ascontiguousarray(rowval, dtype=np.int64)
+        nz = np.ascontiguousarray(nzval, dtype=self.dtype)
+        check(lib().pp_multi_assemble(self._m, self.s.id, self._dt, i64ptr(cp), i64ptr(rv), vptr(nz), 0))
+        return self
+
+    def factor(self):
+        check(lib().pp_multi_factor(self._m))
+        return self
+
+    def lmul_(self, B, trans=False):
+        """B <- A* B (host n x k, column-major), the k columns split by device."""
+        if not (isinstance(B, np.ndarray) and B.flags.f_contiguous and B.dtype == self.dtype):
+            raise TypeError("B must be a column-major numpy array of the factor's element type")
+        check(lib().pp_multi_lmul(self._m, vptr(B), B.shape[0], B.shape[1], 1 if trans else 0))
+        return B
+
+    def rmul_(self, B, trans=False):
+        """B <- B A* (host k x n, column-major), the k rows split by device."""
+        if not (isinstance(B, np.ndarray) and B.flags.f_contiguous and B.dtype == self.dtype):
+            raise TypeError("B must be a column-major numpy array of the factor's element type")
+        check(lib().pp_multi_rmul(self._m, vptr(B), B.shape[0], B.shape[0], 1 if trans else 0))
+        return B
+
+    def star(self, col0=0, ncols=None):
+        """Columns col0 .. col0+ncols-1 of A* (host n x ncols), split by device."""
+        n = self.S.n
+        ncols = n - col0 if ncols is None else ncols
+        out = np.empty((n, ncols), dtype=self.dtype, order="F")
+        check(lib().pp_multi_star(self._m, vptr(out), n, col0, ncols))
+        return out
+
+
 def comm_id():
     """A new group id for B200SLU.join (pp_comm_id, 128 bytes): make it on one rank, send it to the others."""
     buf = C.create_string_buffer(128)

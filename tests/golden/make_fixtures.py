@@ -1,6 +1,6 @@
 """Generate the golden fixtures tests/golden/{paris,bunny}.npz from the reference's data files.
 
-    python tests/golden/make_fixtures.py [REFERENCE_ROOT]
+    python tests/golden/make_fixtures.py <REFERENCE_ROOT>
 
 The reference ships, for its website, the factorization PATHPACK.jl computed with mlu(MinPlus(), A) in
 Float32 for two demo graphs (docs/src/public/data/<name>-lu.bin.gz, written by docs/site_factors.jl:136-205)

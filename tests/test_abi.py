@@ -90,3 +90,17 @@ def test_default_options():
     assert L.pp_set_options(None, C.byref(o)) == _lib.PP_EINVAL
     with pytest.raises(TypeError):
         pp.api._options({"no_such_option": 1})
+
+
+def test_multi_device_handle_argument_errors():
+    """pp_multi_create refuses bad arguments before touching a device, and reports a device it cannot open."""
+    L = pp.lib()
+    m = C.c_void_p()
+    assert L.pp_multi_create(None, 1, None, C.byref(m)) == _lib.PP_EINVAL and not m.value
+    devs = (C.c_int32 * 1)(0)
+    assert L.pp_multi_create(devs, 0, None, C.byref(m)) == _lib.PP_EINVAL
+    assert L.pp_multi_factor(None) == _lib.PP_EINVAL
+    assert L.pp_multi_destroy(None) == 0
+    if not __import__("torch").cuda.is_available():
+        r = L.pp_multi_create(devs, 1, None, C.byref(m))
+        assert r != 0 and not m.value and L.pp_last_error(None)

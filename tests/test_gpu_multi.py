@@ -109,3 +109,37 @@ def test_split_factorization_two_gpus(gpu, case):
     while not errq.empty():
         errs.append(errq.get())
     assert not errs and all(p.exitcode == 0 for p in procs), errs
+
+
+def test_multi_device_handle(gpu):
+    """pp_multi (one process driving the GPUs it is given, one host thread per device): factor, lmul!, rmul!
+    (and their transposes) and star columns split by device, against the oracle.  On one GPU it is a group of
+    one; with two it runs the split factorization."""
+    import torch
+
+    import pathpack_b200 as pp
+    from oracle.oracle import OracleLU
+    from pathpack_b200 import graphs
+    from tests.helpers import same
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    devices = list(range(min(2, torch.cuda.device_count())))
+    n, I, J, W = graphs.grid2d(96, 96, 1.0, 10.0, seed=41, dtype=np.float64)
+    cp, rv, nz = graphs.csc(n, I, J, W)
+    S = pp.ssymbolic(n, cp, rv)
+    O = OracleLU("MinPlus", np.float64, S).assemble(cp, rv, nz).factor()
+    M = pp.MultiSLU(pp.MinPlus(), np.float64, S, devices)
+    try:
+        M.assemble_csc(cp, rv, nz).factor()
+        B, _ = graphs.unit_columns(n, 37, seed=2)
+        same(M.lmul_(B.copy(order="F")), O.lmul(B), "MinPlus", np.float64, "multi lmul!")
+        R = np.asfortranarray(graphs.unit_columns(n, 23, seed=3)[0].T)
+        same(M.rmul_(R.copy(order="F")), O.rmul(R), "MinPlus", np.float64, "multi rmul!")
+        E = np.full((n, 300), np.inf, order="F")
+        E[np.arange(1000, 1300), np.arange(300)] = 0.0
+        same(M.star(1000, 300), O.lmul(E), "MinPlus", np.float64, "multi star columns")
+        # the transposed factor: lmul!(transpose(F), B) = (rmul!(B^T, F))^T
+        Bt = M.lmul_(B.copy(order="F"), trans=True)
+        same(Bt, np.asfortranarray(O.rmul(np.asfortranarray(B.T)).T), "MinPlus", np.float64, "multi lmul! transposed")
+    finally:
+        M.close()

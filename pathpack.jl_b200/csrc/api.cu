@@ -691,15 +691,19 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
             sbot[f] = (hp.nn[f] <= SWEEP_NNW) && (hp.nn[f] + hp.na[f] <= SWEEP_NJW) && allbot[f];
             if (!sbot[f] && pnt[f] >= 0) allbot[pnt[f]] = 0;
         }
-        // subtrees solved in shared memory: the whole subtree is in the bottom and its residual range plus the
-        // root's separator fit SUBTREE_ROWS rows; maximal such subtrees are disjoint
+        // subtrees solved in shared memory: the whole subtree is in the bottom, its residual range plus the
+        // root's separator fit SUBTREE_ROWS rows, and its fronts' factor blocks and separator slots fit the
+        // staging areas (contiguous ranges, the subtree's fronts being contiguous); maximal such subtrees are
+        // disjoint
         std::vector<int> fdsc(nf);
         for (int64_t f = 0; f < nf; f++) fdsc[f] = (int)f;
         for (int64_t f = 0; f < nf; f++)
             if (pnt[f] >= 0) fdsc[pnt[f]] = std::min(fdsc[pnt[f]], fdsc[f]);
         std::vector<char> qual(nf, 0), covered(nf, 0);
         for (int64_t f = 0; f < nf; f++)
-            qual[f] = sbot[f] && (R[f + 1] - R[fdsc[f]] + hp.na[f] <= SUBTREE_ROWS);
+            qual[f] = sbot[f] && (R[f + 1] - R[fdsc[f]] + hp.na[f] <= SUBTREE_ROWS) &&
+                      (hp.dptr[f + 1] - hp.dptr[fdsc[f]] + hp.lptr[f + 1] - hp.lptr[fdsc[f]] <= SUBTREE_FAC) &&
+                      (Sp[f + 1] - Sp[fdsc[f]] <= SUBTREE_SLOTS);
         std::vector<int> sroot_of(nf, -1);
         for (int64_t f = nf - 1; f >= 0; f--) {
             if (!qual[f]) continue;

@@ -250,7 +250,7 @@ struct Engine {
     static cudaError_t sweep_subtrees(const HostPlan &hp, const SubtreeList &sl, const T *Dv, const T *Ov, T *X,
                                       int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
         if (sl.count == 0) return cudaSuccess;
-        const size_t smem = 4 * subtree_warp_bytes<T>();
+        const size_t smem = subtree_cta_bytes<T>();
         int dev = 0;
         cudaGetDevice(&dev);
         static size_t attr[64] = {};
@@ -259,10 +259,10 @@ struct Engine {
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
             attr[dev] = smem;
         }
-        const int64_t tasks = (int64_t)sl.count * ((k + 31) / 32);
+        const int64_t tasks = (int64_t)sl.count * ((k + 127) / 128);  // (subtree, 128-column group)
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_SUBTREE : K_SWEEP_BWD_SUBTREE, st) : -1;
-        sweep_subtree_kernel<SR, T, FWD, TRANS><<<(unsigned)((tasks + 3) / 4), 128, smem, st>>>(
-            hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit);
+        sweep_subtree_kernel<SR, T, FWD, TRANS><<<(unsigned)tasks, 32 * SUBTREE_WARPS, smem, st>>>(
+            hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit, hp.d_err);
         PP_TRY(cudaGetLastError());
         if (pi >= 0) {
             double pairs = 0, elems = 0;

@@ -347,153 +347,255 @@ __global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict
 //
 // A subtree rooted at r touches only its residual rows, the contiguous positions rlo(fd(r)) .. rhi(r), and the
 // separator of r (the running-intersection property of the clique tree: a separator vertex of a front in the
-// subtree is either in the subtree or in sep(r)).  A warp task (subtree, 32-column tile) loads those rows once
-// into shared memory, runs every front of the subtree in postorder (forward) or reverse postorder (backward)
-// there, and writes back once; the forward sweep (+)-scatters the accumulated separator rows with atomics.
-// slot[Sptr[g] + i] is the shared-memory row of the i-th separator vertex of front g.  Each lane touches only
-// its own column, so a task needs no barrier.
+// subtree is either in the subtree or in sep(r)).  A CTA task (subtree, 128-column group) stages everything the
+// subtree's fronts read in shared memory once: their descriptors (sizes, first row, offsets of their blocks),
+// the separator slots (slot[Sptr[g] + i] is the subtree row of the i-th separator vertex of front g) and the
+// factor blocks D (nn x nn) and O (nn x na), which are contiguous ranges of the factor arrays because the
+// subtree's fronts are contiguous in postorder.  Each warp then loads its columns' rows of the subtree, runs
+// every front in postorder (forward) or reverse postorder (backward) from shared memory, and writes back
+// once; the forward sweep (+)-scatters the accumulated separator rows with atomics.  A lane holds C columns,
+// and touches only its own columns' rows, so the front loop needs no barrier.  The host admits a subtree only
+// when its rows, slots and factor blocks fit the staging areas (SUBTREE_ROWS, SUBTREE_SLOTS, SUBTREE_FAC).
 
+// columns per lane of the subtree sweep, and its warps per CTA (a CTA covers 128 columns)
+constexpr int SUBTREE_C = 1;
+constexpr int SUBTREE_WARPS = 4 / SUBTREE_C;
 
-// One front of a subtree for this lane's right-hand side: its nn <= NMAX residual values in registers (the
-// loops are unrolled to NMAX and guarded by nn), the factor blocks D (nn x nn) and O (the off-diagonal block)
-// and the separator slots sl, the subtree's rows in xs.  Same operations in the same order
-// as warp_front_tile.
-template <int SR, typename T, bool FWD, bool TRANS, int NMAX>
-__device__ __forceinline__ void subtree_front(int nn, int na, T *xg, T *xs, const T *__restrict__ D,
-                                              const T *__restrict__ O, const int *__restrict__ sl, bool scale) {
+// shared memory of sweep_subtree_kernel: per warp the subtree's rows for its 32 * C columns, then the staged
+// factor blocks, slots and front descriptors (int4 {nn, na, first row - subtree's first row, slot offset},
+// int2 {offset of D, offset of O} in the staged factor area)
+template <typename T>
+__host__ __device__ constexpr size_t subtree_cta_bytes() {
+    return sizeof(T) * ((size_t)SUBTREE_WARPS * SUBTREE_ROWS * 32 * SUBTREE_C + SUBTREE_FAC) +
+           sizeof(int) * SUBTREE_SLOTS + (sizeof(int4) + sizeof(int2)) * SUBTREE_ROWS;
+}
+
+// One front of a subtree for this lane's C right-hand sides: its nn <= NMAX residual values in registers (the
+// loops are unrolled to NMAX and guarded by nn), the factor blocks D and O and the slots sl in shared memory,
+// the subtree's rows in xs (row s, column j of the lane at xs[s * 32C + 32j]).  Per element the same
+// operations in the same order as warp_front_tile.
+template <int SR, typename T, bool FWD, bool TRANS, int NMAX, int C>
+__device__ __forceinline__ void subtree_front(int nn, int na, T *xg, T *xs, const T *D, const T *O, const int *sl,
+                                              bool scale) {
     using S = Sem<SR, T>;
+    constexpr int RS = 32 * C;  // row stride of xs
     const T z = S::zero();
     const int drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;  // Te(r, c) = D[r * drs + c * dcs]
-    T x[NMAX];
+    T x[NMAX][C];
 #pragma unroll
-    for (int p = 0; p < NMAX; p++) x[p] = p < nn ? xg[32 * p] : z;
+    for (int p = 0; p < NMAX; p++)
+#pragma unroll
+        for (int j = 0; j < C; j++) x[p][j] = p < nn ? xg[p * RS + 32 * j] : z;
     if (FWD) {
         const int ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
 #pragma unroll
         for (int p = 0; p < NMAX; p++) {
             if (p >= nn) break;
-            if (scale) x[p] = S::mul(x[p], S::star(D[p * (drs + dcs)]));
+            if (scale) {
+                const T s = S::star(D[p * (drs + dcs)]);
+#pragma unroll
+                for (int j = 0; j < C; j++) x[p][j] = S::mul(x[p][j], s);
+            }
 #pragma unroll
             for (int q = p + 1; q < NMAX; q++)
-                if (q < nn) x[q] = S::muladd(D[q * drs + p * dcs], x[p], x[q]);
+                if (q < nn) {
+                    const T d = D[q * drs + p * dcs];
+#pragma unroll
+                    for (int j = 0; j < C; j++) x[q][j] = S::muladd(d, x[p][j], x[q][j]);
+                }
         }
         for (int i = 0; i < na; i++) {
-            T a = z;
+            T a[C];
+#pragma unroll
+            for (int j = 0; j < C; j++) a[j] = z;
 #pragma unroll
             for (int p = 0; p < NMAX; p++)
-                if (p < nn) a = S::muladd(O[i * ors + p * ocs], x[p], a);
-            T &c = xs[32 * sl[i]];
-            c = S::add(c, a);
+                if (p < nn) {
+                    const T o = O[i * ors + p * ocs];
+#pragma unroll
+                    for (int j = 0; j < C; j++) a[j] = S::muladd(o, x[p][j], a[j]);
+                }
+            T *c = xs + sl[i] * RS;
+#pragma unroll
+            for (int j = 0; j < C; j++) c[32 * j] = S::add(c[32 * j], a[j]);
         }
     } else {
         const int ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
         // four separator rows per step, their slots and values loaded together; per element the terms in
-        // increasing i as before
+        // increasing i
         int i = 0;
         for (; i + 4 <= na; i += 4) {
-            T xi[4];
+            T xi[4][C];
 #pragma unroll
-            for (int j = 0; j < 4; j++) xi[j] = xs[32 * sl[i + j]];
+            for (int q = 0; q < 4; q++) {
+                const T *c = xs + sl[i + q] * RS;
+#pragma unroll
+                for (int j = 0; j < C; j++) xi[q][j] = c[32 * j];
+            }
 #pragma unroll
             for (int p = 0; p < NMAX; p++)
                 if (p < nn) {
 #pragma unroll
-                    for (int j = 0; j < 4; j++) x[p] = S::muladd(O[p * ors + (i + j) * ocs], xi[j], x[p]);
+                    for (int q = 0; q < 4; q++) {
+                        const T o = O[p * ors + (i + q) * ocs];
+#pragma unroll
+                        for (int j = 0; j < C; j++) x[p][j] = S::muladd(o, xi[q][j], x[p][j]);
+                    }
                 }
         }
         for (; i < na; i++) {
-            const T xi = xs[32 * sl[i]];
+            const T *c = xs + sl[i] * RS;
+            T xi[C];
+#pragma unroll
+            for (int j = 0; j < C; j++) xi[j] = c[32 * j];
 #pragma unroll
             for (int p = 0; p < NMAX; p++)
-                if (p < nn) x[p] = S::muladd(O[p * ors + i * ocs], xi, x[p]);
+                if (p < nn) {
+                    const T o = O[p * ors + i * ocs];
+#pragma unroll
+                    for (int j = 0; j < C; j++) x[p][j] = S::muladd(o, xi[j], x[p][j]);
+                }
         }
 #pragma unroll
         for (int p = NMAX - 1; p >= 0; p--) {
             if (p >= nn) continue;
-            if (scale) x[p] = S::mul(S::star(D[p * (drs + dcs)]), x[p]);
+            if (scale) {
+                const T s = S::star(D[p * (drs + dcs)]);
 #pragma unroll
-            for (int q = 0; q < p; q++) x[q] = S::muladd(D[q * drs + p * dcs], x[p], x[q]);
+                for (int j = 0; j < C; j++) x[p][j] = S::mul(s, x[p][j]);
+            }
+#pragma unroll
+            for (int q = 0; q < p; q++) {
+                const T d = D[q * drs + p * dcs];
+#pragma unroll
+                for (int j = 0; j < C; j++) x[q][j] = S::muladd(d, x[p][j], x[q][j]);
+            }
         }
     }
 #pragma unroll
     for (int p = 0; p < NMAX; p++)
-        if (p < nn) xg[32 * p] = x[p];
+        if (p < nn)
+#pragma unroll
+            for (int j = 0; j < C; j++) xg[p * RS + 32 * j] = x[p][j];
 }
 
-// shared memory of one warp of sweep_subtree_kernel: the subtree's rows for its 32 right-hand sides
-template <typename T>
-__host__ __device__ constexpr size_t subtree_warp_bytes() {
-    return sizeof(T) * (size_t)SUBTREE_ROWS * 32;
-}
-
-// The fronts of the subtree are r's descendants fdsc[r] .. r, contiguous in postorder.  Each front's residual
-// values of this lane are held in registers while it is solved (subtree_front); the factor operands are read
-// through the read-only cache.
 template <int SR, typename T, bool FWD, bool TRANS>
 __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restrict__ roots, int nroots, DevPlan P,
                                                             const int *__restrict__ fdsc, const int *__restrict__ slot,
                                                             const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
-                                                            int64_t ldx, int k, int unit) {
+                                                            int64_t ldx, int k, int unit, int *err) {
     using S = Sem<SR, T>;
+    constexpr int C = SUBTREE_C, RS = 32 * C;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    T *xs = reinterpret_cast<T *>(smem_raw + (size_t)w * subtree_warp_bytes<T>()) + lane;  // row s at xs[32 * s]
-    const int ntiles = (k + 31) / 32;
-    const int64_t t = (int64_t)blockIdx.x * 4 + w;
-    if (t >= (int64_t)nroots * ntiles) return;
-    const int r = roots[t / ntiles], tile = (int)(t % ntiles);
-    const int col = tile * 32 + lane;
-    const bool ok = col < k;
-    T *Xc = X + (ok ? col : 0);
-    const T z = S::zero();
-    const bool scale = !unit && !S::integral;
-    const int f0 = fdsc[r];
+    T *xs_all = reinterpret_cast<T *>(smem_raw);
+    T *fac = xs_all + (size_t)SUBTREE_WARPS * SUBTREE_ROWS * RS;
+    int *sls = reinterpret_cast<int *>(fac + SUBTREE_FAC);
+    int4 *desc = reinterpret_cast<int4 *>(sls + SUBTREE_SLOTS);
+    int2 *desc2 = reinterpret_cast<int2 *>(desc + SUBTREE_ROWS);
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int ngrp = (k + 127) / 128;
+    const int sidx = blockIdx.x / ngrp, grp = blockIdx.x % ngrp;
+    if (sidx >= nroots) return;
+    const int r = roots[sidx];
+    const int f0 = fdsc[r], ng = r - f0 + 1;
     const int rlo0 = P.rlo[f0];
     const int nres = P.rlo[r] + P.nn[r] - rlo0;
     const int nsep = P.na[r];
-    const int *sepr = P.stgt + P.sptr[r];
-    const int ng = r - f0 + 1;
-    // the sizes and first row of front number gi of the traversal, loaded one front ahead
-    auto issue = [&](int gi, int, int &nn, int &na, int &rlo) {
-        const int g = FWD ? f0 + gi : r - gi;
-        nn = P.nn[g];
-        na = P.na[g];
-        rlo = P.rlo[g];
-    };
-    int nn1, na1, rlo1;
-    issue(0, 0, nn1, na1, rlo1);
-    bool nz = false;
+    const int64_t dbase = P.dptr[f0], lbase = P.lptr[f0], sbase = P.sptr[f0];
+    const int dlen = (int)(P.dptr[r + 1] - dbase), llen = (int)(P.lptr[r + 1] - lbase);
+    const int slen = (int)(P.sptr[r + 1] - sbase);
+    if (ng > SUBTREE_ROWS || nres + nsep > SUBTREE_ROWS || dlen + llen > SUBTREE_FAC || slen > SUBTREE_SLOTS) {
+        if (tid == 0) atomicExch(err, 1);  // the host admitted a subtree that does not fit (uniform)
+        return;
+    }
+    // this warp's columns c0 + 32j of the subtree's rows, copied asynchronously (all in flight at once);
+    // forward, the separator rows start at zero
+    const int c0 = grp * 128 + w * RS + lane;
+    T *xs = xs_all + (size_t)w * SUBTREE_ROWS * RS + lane;
+    const T z = S::zero();
+    bool ok[C];
+#pragma unroll
+    for (int j = 0; j < C; j++) ok[j] = c0 + 32 * j < k;
+#pragma unroll 4
     for (int s = 0; s < nres; s++) {
-        xs[32 * s] = ok ? Xc[(int64_t)(rlo0 + s) * ldx] : z;
-        nz |= !(xs[32 * s] == z);
+        const T *xr = X + (int64_t)(rlo0 + s) * ldx + c0;
+#pragma unroll
+        for (int j = 0; j < C; j++) {
+            if (ok[j])
+                cp_async_elem(xs + s * RS + 32 * j, xr + 32 * j);
+            else
+                xs[s * RS + 32 * j] = z;
+        }
     }
-    // forward: the 32 right-hand sides are zero on the subtree's rows, so no step changes anything (the
-    // sources of these columns lie outside the subtree)
+    const int *sepr = P.stgt + P.sptr[r];
+#pragma unroll 4
+    for (int i = 0; i < nsep; i++) {
+        const T *xr = X + (int64_t)sepr[i] * ldx + c0;
+#pragma unroll
+        for (int j = 0; j < C; j++) {
+            if (!FWD && ok[j])
+                cp_async_elem(xs + (nres + i) * RS + 32 * j, xr + 32 * j);
+            else
+                xs[(nres + i) * RS + 32 * j] = z;
+        }
+    }
+    bool nz = false;
+    if (FWD && zero_absorbs<SR>) {
+        // forward: the right-hand sides that are zero on the subtree's rows change nothing (the sources of
+        // these columns lie outside the subtree); a CTA whose columns all are leaves before staging anything
+        cp_async_wait_all();
+        for (int s = 0; s < nres; s++)
+#pragma unroll
+            for (int j = 0; j < C; j++) nz |= !(xs[s * RS + 32 * j] == z);
+        if (!__syncthreads_or(nz)) return;
+    }
+    // stage the subtree's factor blocks, slots and front descriptors
+    for (int e = tid; e < dlen; e += blockDim.x) cp_async_elem(fac + e, Dv + dbase + e);
+    for (int e = tid; e < llen; e += blockDim.x) cp_async_elem(fac + dlen + e, Ov + lbase + e);
+    for (int e = tid; e < slen; e += blockDim.x) cp_async_elem(sls + e, slot + sbase + e);
+    for (int g = tid; g < ng; g += blockDim.x) {
+        const int f = f0 + g;
+        desc[g] = make_int4(P.nn[f], P.na[f], P.rlo[f] - rlo0, (int)(P.sptr[f] - sbase));
+        desc2[g] = make_int2((int)(P.dptr[f] - dbase), dlen + (int)(P.lptr[f] - lbase));
+    }
+    cp_async_wait_all();
+    __syncthreads();  // the staged blocks (the last barrier: warps leave independently from here)
+    if (!__any_sync(0xffffffffu, ok[0])) return;
     if (FWD && zero_absorbs<SR> && !__any_sync(0xffffffffu, nz)) return;
-    for (int i = 0; i < nsep; i++) xs[32 * (nres + i)] = (FWD || !ok) ? z : Xc[(int64_t)sepr[i] * ldx];
+    const bool scale = !unit && !S::integral;
     for (int gi = 0; gi < ng; gi++) {
-        const int nn = nn1, na = na1, rlo = rlo1;
-        __syncwarp();
-        if (gi + 1 < ng) issue(gi + 1, (gi + 1) & 1, nn1, na1, rlo1);
-        T *xg = xs + 32 * (rlo - rlo0);  // the front's residual rows: xg[32 * p]
-        const int g = FWD ? f0 + gi : r - gi;
-        const T *D = Dv + P.dptr[g];
-        const T *O = Ov + P.lptr[g];
-        const int *sl = slot + P.sptr[g];
-        if (nn <= 4)
-            subtree_front<SR, T, FWD, TRANS, 4>(nn, na, xg, xs, D, O, sl, scale);
+        const int g = FWD ? gi : ng - 1 - gi;
+        const int4 d = desc[g];
+        const int2 o = desc2[g];
+        const int nn = d.x, na = d.y;
+        T *xg = xs + d.z * RS;
+        const T *D = fac + o.x, *O = fac + o.y;
+        const int *sl = sls + d.w;
+        if (nn == 1)
+            subtree_front<SR, T, FWD, TRANS, 1, C>(nn, na, xg, xs, D, O, sl, scale);
+        else if (nn == 2)
+            subtree_front<SR, T, FWD, TRANS, 2, C>(nn, na, xg, xs, D, O, sl, scale);
+        else if (nn <= 4)
+            subtree_front<SR, T, FWD, TRANS, 4, C>(nn, na, xg, xs, D, O, sl, scale);
         else if (nn <= 8)
-            subtree_front<SR, T, FWD, TRANS, 8>(nn, na, xg, xs, D, O, sl, scale);
+            subtree_front<SR, T, FWD, TRANS, 8, C>(nn, na, xg, xs, D, O, sl, scale);
         else
-            subtree_front<SR, T, FWD, TRANS, SWEEP_NNW>(nn, na, xg, xs, D, O, sl, scale);
-        __syncwarp();
+            subtree_front<SR, T, FWD, TRANS, SWEEP_NNW, C>(nn, na, xg, xs, D, O, sl, scale);
     }
-    if (!ok) return;
-    for (int s = 0; s < nres; s++) Xc[(int64_t)(rlo0 + s) * ldx] = xs[32 * s];
+    for (int s = 0; s < nres; s++) {
+        T *xr = X + (int64_t)(rlo0 + s) * ldx + c0;
+#pragma unroll
+        for (int j = 0; j < C; j++)
+            if (ok[j]) xr[32 * j] = xs[s * RS + 32 * j];
+    }
     if (FWD)
         for (int i = 0; i < nsep; i++) {
-            const T v = xs[32 * (nres + i)];
-            if (!(v == z)) S::atomic_add(Xc + (int64_t)sepr[i] * ldx, v);  // (+) zero changes nothing
+            T *xr = X + (int64_t)sepr[i] * ldx + c0;
+#pragma unroll
+            for (int j = 0; j < C; j++) {
+                const T v = xs[(nres + i) * RS + 32 * j];
+                if (ok[j] && !(v == z)) S::atomic_add(xr + 32 * j, v);  // (+) zero changes nothing
+            }
         }
 }
 

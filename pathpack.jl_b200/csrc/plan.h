@@ -14,8 +14,11 @@ constexpr int SWEEP_NNW = 16;
 // frontal matrix fits 32 KB of shared memory: 64 x 64 Float64), so that a solve sweeps all of the bottom of
 // the tree while the top is still being factored
 constexpr int SWEEP_NJW = 64;
-// rows (residual range + root separator) of a subtree solved in shared memory by one warp
+// rows (residual range + root separator) of a subtree solved in shared memory, and the factor values (its
+// fronts' D and O blocks) and separator slots its CTA stages there; the fronts of a subtree are at most its rows
 constexpr int SUBTREE_ROWS = 64;
+constexpr int SUBTREE_FAC = 640;
+constexpr int SUBTREE_SLOTS = 640;
 // tile edge of the persistent factorization of the top of the tree
 constexpr int TOP_TILE = 64;
 // rows of a block task of the top sweeps

@@ -204,8 +204,9 @@ struct pp_handle {
     DevBuf d_rlo, d_nn, d_na, d_sptr, d_stgt, d_rel, d_dptr, d_lptr, d_chdptr, d_chdtgt, d_mptr, d_mld, d_fws,
         d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_sfronts, d_sverts, d_pnt, d_fbottom,
         d_fpending0, d_spending0, d_sdone0, d_tpending0, d_sync, d_tentries, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags, d_croff,
-        d_crng, d_err;
+        d_crng, d_err, d_sinfo_l, d_sinfo_r, d_sheavy;
     std::vector<int> pnt, height, rel;
+    std::vector<int> sinfo_l, sinfo_r, sheavy;  // continuation of the bottom sweeps (host copies)
     std::vector<int> sfronts, sroots;  // host copies of the solve work lists (reordered by prepare_workspace)
     int maxh = 0;
     // values and work
@@ -1426,6 +1427,48 @@ static int32_t prepare_workspace(pp_handle *h) {
             hp.early_bot[d] = (int)(std::stable_partition(b, b + fw[0].second, in_bottom) - b);
         }
     }
+    // continuation of the bottom sweeps (sweep_bottom_kernel): per direction the segment of each bottom front
+    // (2 * stage + part, part 0 for stage 0's early fronts) and which parts its bottom children lie in; the
+    // heavy child of each bottom front, the one with the costliest chain of bottom fronts below it
+    {
+        std::vector<int> heavy(nf, -1), seg(nf, -1);
+        std::vector<double> chain(nf, 0.0);
+        for (int d = 0; d < 2; d++) {
+            const std::vector<std::pair<int64_t, int>> &fw = d ? hp.sb_fwd_r : hp.sb_fwd;
+            std::fill(seg.begin(), seg.end(), -1);
+            for (size_t sidx = 0; sidx < fw.size(); sidx++)
+                for (int i = 0; i < fw[sidx].second; i++) {
+                    const int f = h->sfronts[fw[sidx].first + i];
+                    seg[f] = 2 * (int)sidx + ((sidx == 0 && i < hp.early_bot[d]) ? 0 : 1);
+                }
+            std::vector<int> &info = d ? h->sinfo_r : h->sinfo_l;
+            info.assign(nf, -1);
+            for (int f = 0; f < nf; f++)
+                if (seg[f] >= 0) info[f] = seg[f] << 3;
+            if (d == 0) {
+                for (int f = 0; f < nf; f++) {  // children before parents
+                    if (seg[f] < 0) continue;
+                    chain[f] += 4.0 + hp.nn[f] * (double)hp.na[f] / 36.0;
+                    const int p = h->pnt[f];
+                    if (p >= 0 && seg[p] >= 0 && (heavy[p] < 0 || chain[f] > chain[heavy[p]])) heavy[p] = f;
+                    if (p >= 0 && seg[p] >= 0) chain[p] = std::max(chain[p], chain[f]);
+                }
+            }
+            for (int f = 0; f < nf; f++) {
+                const int p = h->pnt[f];
+                if (seg[f] < 0 || p < 0 || seg[p] < 0) continue;
+                info[p] |= (seg[f] & 1) ? 2 : 1;
+                if (heavy[p] == f) info[f] |= 4;
+            }
+        }
+        h->sheavy = heavy;
+    }
+    CK(h, upload(h->d_sinfo_l, h->sinfo_l, st), "upload");
+    CK(h, upload(h->d_sinfo_r, h->sinfo_r, st), "upload");
+    CK(h, upload(h->d_sheavy, h->sheavy, st), "upload");
+    hp.d_sinfo[0] = h->d_sinfo_l.as<int>();
+    hp.d_sinfo[1] = h->d_sinfo_r.as<int>();
+    hp.d_sheavy = h->d_sheavy.as<int>();
     hp.sroot_pairs.resize(h->sroots.size());
     hp.sroot_res.resize(h->sroots.size());
     hp.sroot_sep.resize(h->sroots.size());

@@ -209,8 +209,10 @@ struct Engine {
     }
 
     // reset = false continues the counters of the previous launch over the same list (its second part)
+    // d: 0 lmul!, 1 rmul!; the launch sweeps the bottom fronts of segments seg_lo .. seg_hi (sweep_bottom_kernel)
     template <bool FWD, bool TRANS>
-    static cudaError_t sweep_bottom(const HostPlan &hp, const std::pair<int64_t, int> &wl, const SLevel &cost,
+    static cudaError_t sweep_bottom(const HostPlan &hp, int d, int seg_lo, int seg_hi,
+                                    const std::pair<int64_t, int> &wl, const SLevel &cost,
                                     const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
                                     int64_t *nl, bool reset = true) {
         if (wl.second == 0) return cudaSuccess;
@@ -237,7 +239,8 @@ struct Engine {
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_BOTTOM : K_SWEEP_BWD_BOTTOM, st) : -1;
         sweep_bottom_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev,
                                                                         Dv, Ov, X, ldx, k, unit, hp.d_sync + 16,
-                                                                        hp.d_sync, hp.d_err, fmax, namax);
+                                                                        hp.d_sync, hp.d_err, fmax, namax,
+                                                                        hp.d_sinfo[d], hp.d_sheavy, seg_lo, seg_hi);
         PP_TRY(cudaGetLastError());
         if (pi >= 0)
             hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
@@ -287,7 +290,8 @@ struct Engine {
         const SLevel &cost = (d ? hp.sb_cost_r : hp.sb_cost_l)[s];
         if (s > 0 || !hp.ev_factored) {
             PP_TRY((sweep_subtrees<true, TRANS>(hp, sub, Dv, Ov, X, ldx, k, unit, st, nl)));
-            return sweep_bottom<true, TRANS>(hp, bot, cost, Dv, Ov, X, ldx, k, unit, st, nl);
+            return sweep_bottom<true, TRANS>(hp, d, 2 * (int)s, 2 * (int)s + 1, bot, cost, Dv, Ov, X, ldx, k, unit, st,
+                                             nl);
         }
         SubtreeList sa = sub, sb = sub;
         sa.count = std::min(hp.early_sub[d], sub.count);
@@ -299,10 +303,10 @@ struct Engine {
         bb.second = bot.second - ba.second;
         const SLevel none{};  // the profile counts the list's bytes and pairs once, with its first launch
         PP_TRY((sweep_subtrees<true, TRANS>(hp, sa, Dv, Ov, X, ldx, k, unit, st, nl)));
-        PP_TRY((sweep_bottom<true, TRANS>(hp, ba, cost, Dv, Ov, X, ldx, k, unit, st, nl)));
+        PP_TRY((sweep_bottom<true, TRANS>(hp, d, 0, 0, ba, cost, Dv, Ov, X, ldx, k, unit, st, nl)));
         PP_TRY(cudaStreamWaitEvent(st, hp.ev_factored, 0));
         PP_TRY((sweep_subtrees<true, TRANS>(hp, sb, Dv, Ov, X, ldx, k, unit, st, nl)));
-        return sweep_bottom<true, TRANS>(hp, bb, ba.second ? none : cost, Dv, Ov, X, ldx, k, unit, st, nl,
+        return sweep_bottom<true, TRANS>(hp, d, 1, 1, bb, ba.second ? none : cost, Dv, Ov, X, ldx, k, unit, st, nl,
                                          ba.second == 0);
     }
 
@@ -322,7 +326,8 @@ struct Engine {
                 PP_TRY((forward_bottom<false>(hp, 0, s, LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_top<true, false>(hp, hp.st_fwd[s], hp.st_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_top<false, false>(hp, hp.st_bwd[s], hp.st_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
-                PP_TRY((sweep_bottom<false, false>(hp, hp.sb_bwd[s], hp.sb_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
+                PP_TRY((sweep_bottom<false, false>(hp, 0, 2 * (int)s, 2 * (int)s + 1, hp.sb_bwd[s], hp.sb_cost_l[s], UD,
+                                                   UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_subtrees<false, false>(hp, hp.sub_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 if (sg.coupled && sg.nverts > 0) {
                     const int pi = hp.prof ? hp.prof->begin(K_COUPLING, st) : -1;
@@ -347,7 +352,8 @@ struct Engine {
                 PP_TRY((forward_bottom<true>(hp, 1, s, UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_top<true, true>(hp, hp.st_fwd_r[s], hp.st_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_top<false, true>(hp, hp.st_bwd_r[s], hp.st_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
-                PP_TRY((sweep_bottom<false, true>(hp, hp.sb_bwd_r[s], hp.sb_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
+                PP_TRY((sweep_bottom<false, true>(hp, 1, 2 * (int)s, 2 * (int)s + 1, hp.sb_bwd_r[s], hp.sb_cost_r[s], LD,
+                                                  LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_subtrees<false, true>(hp, hp.sub_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
             }
         }

@@ -131,6 +131,10 @@ struct HostPlan {
     const int *d_sroots = nullptr, *d_fdsc = nullptr, *d_slot = nullptr;
     int bot_fmax = 0, bot_namax = 0;   // largest nn * nn + nn * na and na of the other bottom fronts
     const int *d_sdone0 = nullptr;     // 1 for fronts outside the bottom, 0 inside (backward flags)
+    // continuation of the bottom sweeps: per direction (lmul!, rmul!) each bottom front's segment and children
+    // parts (sweep_bottom_kernel's sinfo), and the heavy child of each bottom front
+    const int *d_sinfo[2] = {nullptr, nullptr};
+    const int *d_sheavy = nullptr;
     // the top fronts of each stage for the persistent top sweep (forward ascending, backward descending heights)
     std::vector<std::pair<int64_t, int>> st_fwd, st_bwd, st_fwd_r, st_bwd_r;
     std::vector<SLevel> st_cost_l, st_cost_r;

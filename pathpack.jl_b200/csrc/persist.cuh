@@ -295,13 +295,24 @@ __device__ __forceinline__ bool warp_wait(const int *p, bool for_zero, int *err)
     return ok != 0;
 }
 
-// Independent warp tasks (front, 32-column tile), in work-list order with the tiles innermost.  flags holds one
-// counter (forward: children not yet done) or flag (backward: done) per (tile, front): flags[tile * nf + f].
+// Warp tasks (front, 32-column tile), in work-list order with the tiles innermost; flags holds one counter
+// (forward: children not yet done) or flag (backward: done) per (tile, front): flags[tile * nf + f].  A warp
+// that finishes a front continues along the tree without a wait: forward with the parent, when its decrement
+// of the parent's counter was the last one and the parent is swept by this launch; backward with the front's
+// heavy child (the child with the costliest chain of bottom fronts below it).  The list's entries that a
+// continuation reaches are skipped.  sinfo[f] of a bottom front: (segment << 3) | (heavy child of a bottom front
+// << 2) | (has a bottom child of the late part of its stage << 1) | (has one of the early part); the segment is
+// 2 * stage + part, part 0 for the fronts the bottom factorization kernel holds in stage 0 (swept while the
+// top is factored), else 1.  The launch sweeps the segments seg_lo .. seg_hi.
+__device__ __forceinline__ bool in_segs(int seg, int lo, int hi) { return seg >= lo && seg <= hi; }
+
 template <int SR, typename T, bool FWD, bool TRANS>
 __global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P,
                                                            const T *__restrict__ Dv, const T *__restrict__ Ov,
                                                            T *X, int64_t ldx, int k, int unit, int *flags,
-                                                           int *next, int *err, int fmax, int namax) {
+                                                           int *next, int *err, int fmax, int namax,
+                                                           const int *__restrict__ sinfo,
+                                                           const int *__restrict__ heavy, int seg_lo, int seg_hi) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *mine = smem_raw + (size_t)(threadIdx.x >> 5) * bottom_warp_bytes<T>(fmax, namax);
     T *fb = reinterpret_cast<T *>(mine);
@@ -316,29 +327,52 @@ __global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict
         t = __shfl_sync(0xffffffffu, t, 0);
         if (t >= ntask) return;
         const int idx = t / ntiles, tile = t - idx * ntiles;
-        const int f = wl[idx];
+        int f = wl[idx];
         int *fl = flags + (int64_t)tile * nf;
-        const int p = P.pnt[f];
-        if (FWD) {
-            if (!warp_wait(fl + f, true, err)) return;
-        } else if (p >= 0) {
-            if (!warp_wait(fl + p, false, err)) return;
-        }
-        const int nn = P.nn[f];
-        if (nn <= 4)
-            warp_front_tile<SR, T, FWD, TRANS, 4>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
-        else if (nn <= 8)
-            warp_front_tile<SR, T, FWD, TRANS, 8>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
-        else
-            warp_front_tile<SR, T, FWD, TRANS, SWEEP_NNW>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
-        __syncwarp();
-        if (lane == 0) {
-            __threadfence();
+        {
+            const int si = sinfo[f], seg = si >> 3;
             if (FWD) {
-                if (p >= 0) atomicSub(fl + p, 1);
+                // reached by the last of its children in this launch
+                const bool early = (si & 1) && in_segs(seg & ~1, seg_lo, seg_hi);
+                const bool late = (si & 2) && in_segs(seg | 1, seg_lo, seg_hi);
+                if (early || late) continue;
+                if (!warp_wait(fl + f, true, err)) return;  // its children ran in earlier launches
             } else {
-                atomicExch(fl + f, 1);
+                if (si & 4) continue;  // reached from its parent
+                const int p = P.pnt[f];
+                if (p >= 0 && !warp_wait(fl + p, false, err)) return;
             }
+        }
+        while (true) {
+            const int nn = P.nn[f];
+            if (nn <= 2)
+                warp_front_tile<SR, T, FWD, TRANS, 2>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+            else if (nn <= 4)
+                warp_front_tile<SR, T, FWD, TRANS, 4>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+            else if (nn <= 8)
+                warp_front_tile<SR, T, FWD, TRANS, 8>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+            else
+                warp_front_tile<SR, T, FWD, TRANS, SWEEP_NNW>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+            __syncwarp();
+            int nxt = -1;
+            if (lane == 0) {
+                __threadfence();
+                if (FWD) {
+                    const int p = P.pnt[f];
+                    if (p >= 0 && atomicSub(fl + p, 1) == 1) {
+                        const int sp = sinfo[p];
+                        if (sp >= 0 && in_segs(sp >> 3, seg_lo, seg_hi)) nxt = p;
+                    }
+                    if (nxt >= 0) __threadfence();  // the other children's updates of the parent's rows
+                } else {
+                    atomicExch(fl + f, 1);
+                    nxt = heavy[f];
+                }
+            }
+            nxt = __shfl_sync(0xffffffffu, nxt, 0);
+            __syncwarp();
+            if (nxt < 0) break;
+            f = nxt;
         }
     }
 }

@@ -185,6 +185,11 @@ struct pp_handle {
     cudaStream_t factor_stream = nullptr;
     cudaEvent_t ev_bottom = nullptr, ev_factored = nullptr;
     cudaEvent_t copy_ev = nullptr;
+    // lmul! on host memory in column panels: panel p's upload done (in_ev) and solve done (out_ev); the results
+    // go back on out_stream while the next panel is solved
+    static constexpr int kSolvePanels = 4;
+    cudaStream_t out_stream = nullptr;
+    cudaEvent_t in_ev[kSolvePanels] = {}, out_ev[kSolvePanels] = {};
     cudaEvent_t panel_ready[2] = {}, panel_copied[2] = {};  // double-buffered star panels to host memory
     cudaEvent_t ring_ev[3] = {};  // star panels into pageable host memory: the pinned ring's slots filled
     PinnedBuf ring;               // three panels of page-locked host memory (allocated on first use)
@@ -346,6 +351,11 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
     if (e == cudaSuccess) e = cudaEventCreate(&h->fev1);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->copy_ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->out_stream, cudaStreamNonBlocking);
+    for (int i = 0; i < pp_handle::kSolvePanels && e == cudaSuccess; i++) {
+        e = cudaEventCreateWithFlags(&h->in_ev[i], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->out_ev[i], cudaEventDisableTiming);
+    }
     for (int i = 0; i < 2 && e == cudaSuccess; i++) {
         e = cudaEventCreateWithFlags(&h->panel_ready[i], cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->panel_copied[i], cudaEventDisableTiming);
@@ -388,6 +398,14 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
     }
     for (int i = 0; i < 3; i++)
         if (h->ring_ev[i]) cudaEventDestroy(h->ring_ev[i]);
+    if (h->out_stream) {
+        cudaStreamSynchronize(h->out_stream);
+        cudaStreamDestroy(h->out_stream);
+    }
+    for (int i = 0; i < pp_handle::kSolvePanels; i++) {
+        if (h->in_ev[i]) cudaEventDestroy(h->in_ev[i]);
+        if (h->out_ev[i]) cudaEventDestroy(h->out_ev[i]);
+    }
     if (h->copy_stream) {
         cudaStreamSynchronize(h->copy_stream);
         cudaStreamDestroy(h->copy_stream);
@@ -1960,12 +1978,16 @@ static int32_t ensure_sync(pp_handle *h, int64_t k) {
 // The device part of a solve on caller-layout device buffers: Bin permuted into X, the sweeps, X permuted
 // out into Bout (Bin == Bout in place; both leading dimension ldb).  X and the counters must be allocated.
 static int32_t enqueue_solve(pp_handle *h, const void *Bin, void *Bout, int64_t ldb, int64_t k, int left, int trans,
-                             const char *who) {
+                             const char *who, bool first = true, bool last = true) {
     const int n = h->hp.n;
     const int64_t ldx = (k + 3) & ~(int64_t)3;
     cudaStream_t st = h->stream;
     int64_t nl = 0;
-    CK(h, record_timing(h, h->ev0, st), who);
+    if (first) {
+        h->st.pairs_solve = 0;
+        h->st.kernel_launches = 0;
+        CK(h, record_timing(h, h->ev0, st), who);
+    }
     int pi = h->prof.begin(K_PERMUTE, st);
     if (left)
         CK(h, h->ops->rows_in(Bin, ldb, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
@@ -1979,10 +2001,12 @@ static int32_t enqueue_solve(pp_handle *h, const void *Bin, void *Bout, int64_t 
     else
         CK(h, h->ops->cols_out(Bout, ldb, h->X.p, ldx, h->hp.dev.invp, n, (int)k, st), who);
     h->prof.end(pi, st, 2.0 * n * k, 0);
-    CK(h, record_timing(h, h->ev1, st), who);
-    h->solve_pending = !h->capturing;
-    h->st.pairs_solve = solve_pairs_per_rhs(h->hp) * (double)k;
-    h->st.kernel_launches = nl + 2;
+    if (last) {
+        CK(h, record_timing(h, h->ev1, st), who);
+        h->solve_pending = !h->capturing;
+    }
+    h->st.pairs_solve += solve_pairs_per_rhs(h->hp) * (double)k;
+    h->st.kernel_launches += nl + 2;
     return PP_OK;
 }
 
@@ -2017,6 +2041,45 @@ static int32_t run_solve(pp_handle *h, void *B, int64_t ldb, int64_t k, int32_t 
     cudaStream_t st = h->stream;
     void *Bd = B;
     int64_t ldbd = ldb;
+    if (where == PP_HOST && left && bbytes >= ((size_t)32 << 20) && k >= 128) {
+        // B in host memory, in up to four column panels of at least 128 right-hand sides: the uploads run on the
+        // copy stream (overlapping a factorization still queued on the handle's stream), panel p is solved on the
+        // handle's stream once its upload is done, and its result goes back on the output stream while panel
+        // p + 1 is solved, so that most of the PCIe traffic overlaps the solves
+        CK(h, h->stage_in.ensure(bbytes), who);
+        char *Bdev = static_cast<char *>(h->stage_in.p);
+        char *Bh = static_cast<char *>(B);
+        const int np = (int)std::min<int64_t>(pp_handle::kSolvePanels, k / 128);
+        // uploads, solves and downloads are enqueued in that order, so that a copy that blocks the host (pageable
+        // memory) finds the GPU work behind it already queued
+        for (int p = 0; p < np; p++) {
+            const int64_t c0 = k * p / np, c1 = k * (p + 1) / np;
+            CK(h, cudaMemcpy2DAsync(Bdev + es * n * c0, es * n, Bh + es * ldb * c0, es * ldb, es * n, c1 - c0,
+                                    cudaMemcpyHostToDevice, h->copy_stream), who);
+            CK(h, cudaEventRecord(h->in_ev[p], h->copy_stream), who);
+        }
+        for (int p = 0; p < np; p++) {
+            const int64_t c0 = k * p / np, c1 = k * (p + 1) / np;
+            CK(h, cudaStreamWaitEvent(st, h->in_ev[p], 0), who);
+            void *Bp = Bdev + es * n * c0;
+            const int32_t r = enqueue_solve(h, Bp, Bp, n, c1 - c0, left, trans, who, p == 0, p == np - 1);
+            if (r != PP_OK) return r;
+            CK(h, cudaEventRecord(h->out_ev[p], st), who);
+        }
+        for (int p = 0; p < np; p++) {
+            const int64_t c0 = k * p / np, c1 = k * (p + 1) / np;
+            CK(h, cudaStreamWaitEvent(h->out_stream, h->out_ev[p], 0), who);
+            CK(h, cudaMemcpy2DAsync(Bh + es * ldb * c0, es * ldb, Bdev + es * n * c0, es * n, es * n, c1 - c0,
+                                    cudaMemcpyDeviceToHost, h->out_stream), who);
+        }
+        // the handle's stream ends after the last download, and the call returns with the result in host memory
+        CK(h, cudaEventRecord(h->copy_ev, h->out_stream), who);
+        CK(h, cudaStreamWaitEvent(st, h->copy_ev, 0), who);
+        const int32_t r2 = settle(h, who);
+        if (r2 != PP_OK) return r2;
+        ok(h);
+        return PP_OK;
+    }
     if (where == PP_HOST) {
         // the copy runs on the copy stream, so it overlaps work still queued on the handle's stream (a
         // factorization enqueued just before); the stream waits for it before the solve reads B

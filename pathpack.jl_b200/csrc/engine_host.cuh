@@ -210,13 +210,11 @@ struct Engine {
 
     // reset = false continues the counters of the previous launch over the same list (its second part)
     // d: 0 lmul!, 1 rmul!; the launch sweeps the bottom fronts of segments seg_lo .. seg_hi (sweep_bottom_kernel)
-    template <bool FWD, bool TRANS>
-    static cudaError_t sweep_bottom(const HostPlan &hp, int d, int seg_lo, int seg_hi,
-                                    const std::pair<int64_t, int> &wl, const SLevel &cost,
-                                    const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
-                                    int64_t *nl, bool reset = true) {
-        if (wl.second == 0) return cudaSuccess;
-        const int ntiles = (k + 31) / 32;
+    template <bool FWD, bool TRANS, int C>
+    static cudaError_t sweep_bottom_c(const HostPlan &hp, int d, int seg_lo, int seg_hi,
+                                      const std::pair<int64_t, int> &wl, const T *Dv, const T *Ov, T *X, int64_t ldx,
+                                      int k, int unit, cudaStream_t st, bool reset) {
+        const int ntiles = (k + 32 * C - 1) / (32 * C);
         if (reset) {
             PP_TRY(reset_sync(hp, FWD ? hp.d_spending0 : hp.d_sdone0, ntiles, st));
         } else {
@@ -228,20 +226,34 @@ struct Engine {
         cudaGetDevice(&dev);
         static size_t attr[64] = {};
         if (dev < 64 && attr[dev] < smem) {
-            PP_TRY(cudaFuncSetAttribute(sweep_bottom_kernel<SR, T, FWD, TRANS>,
+            PP_TRY(cudaFuncSetAttribute(sweep_bottom_kernel<SR, T, FWD, TRANS, C>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
             attr[dev] = smem;
         }
         int per_sm = 1;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_bottom_kernel<SR, T, FWD, TRANS>, 256, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sweep_bottom_kernel<SR, T, FWD, TRANS, C>, 256, smem);
         const int64_t tasks = (int64_t)wl.second * ntiles;
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((tasks + 7) / 8, std::max(per_sm, 1) * hp.sm_count));
+        sweep_bottom_kernel<SR, T, FWD, TRANS, C><<<grid, 256, smem, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev,
+                                                                           Dv, Ov, X, ldx, k, unit, hp.d_sync + 16,
+                                                                           hp.d_sync, hp.d_err, fmax, namax,
+                                                                           hp.d_sinfo[d], hp.d_sheavy, seg_lo, seg_hi);
+        return cudaGetLastError();
+    }
+
+    template <bool FWD, bool TRANS>
+    static cudaError_t sweep_bottom(const HostPlan &hp, int d, int seg_lo, int seg_hi,
+                                    const std::pair<int64_t, int> &wl, const SLevel &cost,
+                                    const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
+                                    int64_t *nl, bool reset = true) {
+        if (wl.second == 0) return cudaSuccess;
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_BOTTOM : K_SWEEP_BWD_BOTTOM, st) : -1;
-        sweep_bottom_kernel<SR, T, FWD, TRANS><<<grid, 256, smem, st>>>(hp.d_sfronts + wl.first, wl.second, hp.dev,
-                                                                        Dv, Ov, X, ldx, k, unit, hp.d_sync + 16,
-                                                                        hp.d_sync, hp.d_err, fmax, namax,
-                                                                        hp.d_sinfo[d], hp.d_sheavy, seg_lo, seg_hi);
-        PP_TRY(cudaGetLastError());
+        // wide solves: two columns per lane, so each staged factor value serves two (x)(+) pairs and each task's
+        // wait and staging serve twice the columns
+        if (k >= SWEEP_WIDE_K)
+            PP_TRY((sweep_bottom_c<FWD, TRANS, 2>(hp, d, seg_lo, seg_hi, wl, Dv, Ov, X, ldx, k, unit, st, reset)));
+        else
+            PP_TRY((sweep_bottom_c<FWD, TRANS, 1>(hp, d, seg_lo, seg_hi, wl, Dv, Ov, X, ldx, k, unit, st, reset)));
         if (pi >= 0)
             hp.prof->end(pi, st, (double)k * (2.0 * cost.res_rows + (FWD ? 2.0 : 1.0) * cost.sep_rows) + cost.blk_elems,
                          (double)k * cost.pairs_col);
@@ -249,24 +261,36 @@ struct Engine {
         return cudaSuccess;
     }
 
-    template <bool FWD, bool TRANS>
-    static cudaError_t sweep_subtrees(const HostPlan &hp, const SubtreeList &sl, const T *Dv, const T *Ov, T *X,
-                                      int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
-        if (sl.count == 0) return cudaSuccess;
-        const size_t smem = subtree_cta_bytes<T>();
+    template <bool FWD, bool TRANS, int C>
+    static cudaError_t sweep_subtrees_c(const HostPlan &hp, const SubtreeList &sl, const T *Dv, const T *Ov, T *X,
+                                        int64_t ldx, int k, int unit, cudaStream_t st) {
+        const size_t smem = subtree_cta_bytes<T, C>();
         int dev = 0;
         cudaGetDevice(&dev);
         static size_t attr[64] = {};
         if (dev < 64 && attr[dev] < smem) {
-            PP_TRY(cudaFuncSetAttribute(sweep_subtree_kernel<SR, T, FWD, TRANS>,
+            PP_TRY(cudaFuncSetAttribute(sweep_subtree_kernel<SR, T, FWD, TRANS, C>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
             attr[dev] = smem;
         }
-        const int64_t tasks = (int64_t)sl.count * ((k + 127) / 128);  // (subtree, 128-column group)
-        const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_SUBTREE : K_SWEEP_BWD_SUBTREE, st) : -1;
-        sweep_subtree_kernel<SR, T, FWD, TRANS><<<(unsigned)tasks, 32 * SUBTREE_WARPS, smem, st>>>(
+        constexpr int cw = 32 * SUBTREE_WARPS * C;
+        const int64_t tasks = (int64_t)sl.count * ((k + cw - 1) / cw);  // (subtree, column group)
+        sweep_subtree_kernel<SR, T, FWD, TRANS, C><<<(unsigned)tasks, 32 * SUBTREE_WARPS, smem, st>>>(
             hp.d_sroots + sl.off, sl.count, hp.dev, hp.d_fdsc, hp.d_slot, Dv, Ov, X, ldx, k, unit, hp.d_err);
-        PP_TRY(cudaGetLastError());
+        return cudaGetLastError();
+    }
+
+    template <bool FWD, bool TRANS>
+    static cudaError_t sweep_subtrees(const HostPlan &hp, const SubtreeList &sl, const T *Dv, const T *Ov, T *X,
+                                      int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
+        if (sl.count == 0) return cudaSuccess;
+        const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_SUBTREE : K_SWEEP_BWD_SUBTREE, st) : -1;
+        // wide solves (the star's panels): two columns per lane, so each factor value read from shared memory
+        // serves two (x)(+) pairs
+        if (k >= SWEEP_WIDE_K)
+            PP_TRY((sweep_subtrees_c<FWD, TRANS, 2>(hp, sl, Dv, Ov, X, ldx, k, unit, st)));
+        else
+            PP_TRY((sweep_subtrees_c<FWD, TRANS, 1>(hp, sl, Dv, Ov, X, ldx, k, unit, st)));
         if (pi >= 0) {
             double pairs = 0, elems = 0;
             for (int64_t i = sl.off; i < sl.off + sl.count && i < (int64_t)hp.sroot_pairs.size(); i++) {

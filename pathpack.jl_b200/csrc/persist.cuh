@@ -186,33 +186,40 @@ __host__ __device__ constexpr size_t bottom_warp_bytes(int fmax, int namax) {
     return (sizeof(T) * (size_t)fmax + sizeof(int) * (size_t)namax + 15) & ~(size_t)15;
 }
 
-// One (front, 32-column tile) task of the bottom sweeps: the residual values (nn <= NMAX) in registers, the
-// factor blocks and separator positions copied into the warp's shared memory (cp.async, all in flight at
-// once), the separator values of the backward sweep loaded eight at a time ahead of their use.
-template <int SR, typename T, bool FWD, bool TRANS, int NMAX>
+// One (front, tile of 32 C columns) task of the bottom sweeps, a lane holding the C columns lane + 32 j: the
+// residual values (nn <= NMAX) in registers, the factor blocks and separator positions copied into the warp's
+// shared memory (cp.async, all in flight at once), the separator values of the backward sweep loaded eight at
+// a time ahead of their use.  Each factor value read from shared memory serves C (x)(+) pairs.
+template <int SR, typename T, bool FWD, bool TRANS, int NMAX, int C>
 __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &P, const T *__restrict__ Dv,
                                                 const T *__restrict__ Ov, T *X, int64_t ldx, int k, int unit,
                                                 T *fb, int *sb) {
     using S = Sem<SR, T>;
     const int lane = threadIdx.x & 31;
-    const int col = tile * 32 + lane;
-    const bool ok = col < k;
+    const int col0 = tile * 32 * C + lane;
+    bool ok[C];
+#pragma unroll
+    for (int j = 0; j < C; j++) ok[j] = col0 + 32 * j < k;
     const int rlo = P.rlo[f], nn = P.nn[f], na = P.na[f];
     const T *D = Dv + P.dptr[f];
     const T *O = Ov + P.lptr[f];
     const int *sep = P.stgt + P.sptr[f];
-    T *Xc = X + (ok ? col : 0);
+    T *Xc = X + (ok[0] ? col0 : 0);  // column j of the lane at Xc + 32 j (read and written only when ok[j])
     const T z = S::zero();
     const bool scale = !unit && !S::integral;
     const int drs = TRANS ? nn : 1, dcs = TRANS ? 1 : nn;  // Te(r, c) = D[r * drs + c * dcs]
-    T x[NMAX];
+    T x[NMAX][C];
 #pragma unroll
-    for (int p = 0; p < NMAX; p++) x[p] = (p < nn && ok) ? ld_cg(Xc + (int64_t)(rlo + p) * ldx) : z;
+    for (int p = 0; p < NMAX; p++)
+#pragma unroll
+        for (int j = 0; j < C; j++) x[p][j] = (p < nn && ok[j]) ? ld_cg(Xc + (int64_t)(rlo + p) * ldx + 32 * j) : z;
     if (FWD && zero_absorbs<SR>) {
-        // the 32 right-hand sides are zero on the whole residual: the step changes nothing
+        // the right-hand sides are zero on the whole residual: the step changes nothing
         bool nz = false;
 #pragma unroll
-        for (int p = 0; p < NMAX; p++) nz |= !(x[p] == z);
+        for (int p = 0; p < NMAX; p++)
+#pragma unroll
+            for (int j = 0; j < C; j++) nz |= !(x[p][j] == z);
         if (!__any_sync(0xffffffffu, nz)) return;
     }
     for (int e = lane; e < nn * nn; e += 32) cp_async_elem(fb + e, D + e);
@@ -226,45 +233,84 @@ __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &
 #pragma unroll
         for (int p = 0; p < NMAX; p++) {
             if (p >= nn) break;
-            if (scale) x[p] = S::mul(x[p], S::star(Ds[p * (drs + dcs)]));
+            if (scale) {
+                const T s = S::star(Ds[p * (drs + dcs)]);
+#pragma unroll
+                for (int j = 0; j < C; j++) x[p][j] = S::mul(x[p][j], s);
+            }
 #pragma unroll
             for (int q = p + 1; q < NMAX; q++)
-                if (q < nn) x[q] = S::muladd(Ds[q * drs + p * dcs], x[p], x[q]);
+                if (q < nn) {
+                    const T d = Ds[q * drs + p * dcs];
+#pragma unroll
+                    for (int j = 0; j < C; j++) x[q][j] = S::muladd(d, x[p][j], x[q][j]);
+                }
         }
 #pragma unroll
         for (int p = 0; p < NMAX; p++)
-            if (p < nn && ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, x[p]);
+            if (p < nn)
+#pragma unroll
+                for (int j = 0; j < C; j++)
+                    if (ok[j]) __stcg(Xc + (int64_t)(rlo + p) * ldx + 32 * j, x[p][j]);
         for (int i = 0; i < na; i++) {
-            T a = z;
+            T a[C];
+#pragma unroll
+            for (int j = 0; j < C; j++) a[j] = z;
 #pragma unroll
             for (int p = 0; p < NMAX; p++)
-                if (p < nn) a = S::muladd(Os[i * ors + p * ocs], x[p], a);
-            if (ok && !(a == z)) S::atomic_add(Xc + (int64_t)sb[i] * ldx, a);  // (+) zero changes nothing
+                if (p < nn) {
+                    const T o = Os[i * ors + p * ocs];
+#pragma unroll
+                    for (int j = 0; j < C; j++) a[j] = S::muladd(o, x[p][j], a[j]);
+                }
+            T *xr = Xc + (int64_t)sb[i] * ldx;
+#pragma unroll
+            for (int j = 0; j < C; j++)
+                if (ok[j] && !(a[j] == z)) S::atomic_add(xr + 32 * j, a[j]);  // (+) zero changes nothing
         }
     } else {
         const int ors = TRANS ? na : 1, ocs = TRANS ? 1 : nn;  // O(p, i) = O[p * ors + i * ocs]
         for (int i0 = 0; i0 < na; i0 += 8) {
-            T xv[8];
+            T xv[8][C];
 #pragma unroll
-            for (int u = 0; u < 8; u++) xv[u] = (i0 + u < na && ok) ? ld_cg(Xc + (int64_t)sb[i0 + u] * ldx) : z;
+            for (int u = 0; u < 8; u++) {
+                const T *xr = Xc + (int64_t)sb[min(i0 + u, na - 1)] * ldx;
+#pragma unroll
+                for (int j = 0; j < C; j++) xv[u][j] = (i0 + u < na && ok[j]) ? ld_cg(xr + 32 * j) : z;
+            }
 #pragma unroll
             for (int u = 0; u < 8; u++) {
                 if (i0 + u >= na) break;
 #pragma unroll
                 for (int p = 0; p < NMAX; p++)
-                    if (p < nn) x[p] = S::muladd(Os[p * ors + (i0 + u) * ocs], xv[u], x[p]);
+                    if (p < nn) {
+                        const T o = Os[p * ors + (i0 + u) * ocs];
+#pragma unroll
+                        for (int j = 0; j < C; j++) x[p][j] = S::muladd(o, xv[u][j], x[p][j]);
+                    }
             }
         }
 #pragma unroll
         for (int p = NMAX - 1; p >= 0; p--) {
             if (p >= nn) continue;
-            if (scale) x[p] = S::mul(S::star(Ds[p * (drs + dcs)]), x[p]);
+            if (scale) {
+                const T s = S::star(Ds[p * (drs + dcs)]);
 #pragma unroll
-            for (int q = 0; q < p; q++) x[q] = S::muladd(Ds[q * drs + p * dcs], x[p], x[q]);
+                for (int j = 0; j < C; j++) x[p][j] = S::mul(s, x[p][j]);
+            }
+#pragma unroll
+            for (int q = 0; q < p; q++) {
+                const T d = Ds[q * drs + p * dcs];
+#pragma unroll
+                for (int j = 0; j < C; j++) x[q][j] = S::muladd(d, x[p][j], x[q][j]);
+            }
         }
 #pragma unroll
         for (int p = 0; p < NMAX; p++)
-            if (p < nn && ok) __stcg(Xc + (int64_t)(rlo + p) * ldx, x[p]);
+            if (p < nn)
+#pragma unroll
+                for (int j = 0; j < C; j++)
+                    if (ok[j]) __stcg(Xc + (int64_t)(rlo + p) * ldx + 32 * j, x[p][j]);
     }
     __syncwarp();  // the buffers are reused by the warp's next task
 }
@@ -295,7 +341,7 @@ __device__ __forceinline__ bool warp_wait(const int *p, bool for_zero, int *err)
     return ok != 0;
 }
 
-// Warp tasks (front, 32-column tile), in work-list order with the tiles innermost; flags holds one counter
+// Warp tasks (front, tile of 32 C columns), in work-list order with the tiles innermost; flags holds one counter
 // (forward: children not yet done) or flag (backward: done) per (tile, front): flags[tile * nf + f].  A warp
 // that finishes a front continues along the tree without a wait: forward with the parent, when its decrement
 // of the parent's counter was the last one and the parent is swept by this launch; backward with the front's
@@ -306,7 +352,7 @@ __device__ __forceinline__ bool warp_wait(const int *p, bool for_zero, int *err)
 // top is factored), else 1.  The launch sweeps the segments seg_lo .. seg_hi.
 __device__ __forceinline__ bool in_segs(int seg, int lo, int hi) { return seg >= lo && seg <= hi; }
 
-template <int SR, typename T, bool FWD, bool TRANS>
+template <int SR, typename T, bool FWD, bool TRANS, int C>
 __global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P,
                                                            const T *__restrict__ Dv, const T *__restrict__ Ov,
                                                            T *X, int64_t ldx, int k, int unit, int *flags,
@@ -317,7 +363,7 @@ __global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict
     unsigned char *mine = smem_raw + (size_t)(threadIdx.x >> 5) * bottom_warp_bytes<T>(fmax, namax);
     T *fb = reinterpret_cast<T *>(mine);
     int *sb = reinterpret_cast<int *>(fb + fmax);
-    const int ntiles = (k + 31) / 32;
+    const int ntiles = (k + 32 * C - 1) / (32 * C);
     const int lane = threadIdx.x & 31;
     const int nf = P.nf;
     const int64_t ntask = (int64_t)count * ntiles;
@@ -346,13 +392,13 @@ __global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict
         while (true) {
             const int nn = P.nn[f];
             if (nn <= 2)
-                warp_front_tile<SR, T, FWD, TRANS, 2>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+                warp_front_tile<SR, T, FWD, TRANS, 2, C>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
             else if (nn <= 4)
-                warp_front_tile<SR, T, FWD, TRANS, 4>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+                warp_front_tile<SR, T, FWD, TRANS, 4, C>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
             else if (nn <= 8)
-                warp_front_tile<SR, T, FWD, TRANS, 8>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+                warp_front_tile<SR, T, FWD, TRANS, 8, C>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
             else
-                warp_front_tile<SR, T, FWD, TRANS, SWEEP_NNW>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
+                warp_front_tile<SR, T, FWD, TRANS, SWEEP_NNW, C>(f, tile, P, Dv, Ov, X, ldx, k, unit, fb, sb);
             __syncwarp();
             int nxt = -1;
             if (lane == 0) {
@@ -391,16 +437,15 @@ __global__ void __launch_bounds__(256) sweep_bottom_kernel(const int *__restrict
 // and touches only its own columns' rows, so the front loop needs no barrier.  The host admits a subtree only
 // when its rows, slots and factor blocks fit the staging areas (SUBTREE_ROWS, SUBTREE_SLOTS, SUBTREE_FAC).
 
-// columns per lane of the subtree sweep, and its warps per CTA (a CTA covers 128 columns)
-constexpr int SUBTREE_C = 1;
-constexpr int SUBTREE_WARPS = 4 / SUBTREE_C;
+// warps per CTA of the subtree sweep; a lane holds C columns (1, or 2 for wide solves), so a CTA covers 128 C
+constexpr int SUBTREE_WARPS = 4;
 
 // shared memory of sweep_subtree_kernel: per warp the subtree's rows for its 32 * C columns, then the staged
 // factor blocks, slots and front descriptors (int4 {nn, na, first row - subtree's first row, slot offset},
 // int2 {offset of D, offset of O} in the staged factor area)
-template <typename T>
+template <typename T, int C>
 __host__ __device__ constexpr size_t subtree_cta_bytes() {
-    return sizeof(T) * ((size_t)SUBTREE_WARPS * SUBTREE_ROWS * 32 * SUBTREE_C + SUBTREE_FAC) +
+    return sizeof(T) * ((size_t)SUBTREE_WARPS * SUBTREE_ROWS * 32 * C + SUBTREE_FAC) +
            sizeof(int) * SUBTREE_SLOTS + (sizeof(int4) + sizeof(int2)) * SUBTREE_ROWS;
 }
 
@@ -513,13 +558,13 @@ __device__ __forceinline__ void subtree_front(int nn, int na, T *xg, T *xs, cons
             for (int j = 0; j < C; j++) xg[p * RS + 32 * j] = x[p][j];
 }
 
-template <int SR, typename T, bool FWD, bool TRANS>
+template <int SR, typename T, bool FWD, bool TRANS, int C>
 __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restrict__ roots, int nroots, DevPlan P,
                                                             const int *__restrict__ fdsc, const int *__restrict__ slot,
                                                             const T *__restrict__ Dv, const T *__restrict__ Ov, T *X,
                                                             int64_t ldx, int k, int unit, int *err) {
     using S = Sem<SR, T>;
-    constexpr int C = SUBTREE_C, RS = 32 * C;
+    constexpr int RS = 32 * C, CW = SUBTREE_WARPS * RS;  // columns per CTA
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *xs_all = reinterpret_cast<T *>(smem_raw);
     T *fac = xs_all + (size_t)SUBTREE_WARPS * SUBTREE_ROWS * RS;
@@ -527,7 +572,7 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     int4 *desc = reinterpret_cast<int4 *>(sls + SUBTREE_SLOTS);
     int2 *desc2 = reinterpret_cast<int2 *>(desc + SUBTREE_ROWS);
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    const int ngrp = (k + 127) / 128;
+    const int ngrp = (k + CW - 1) / CW;
     const int sidx = blockIdx.x / ngrp, grp = blockIdx.x % ngrp;
     if (sidx >= nroots) return;
     const int r = roots[sidx];
@@ -544,7 +589,7 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     }
     // this warp's columns c0 + 32j of the subtree's rows, copied asynchronously (all in flight at once);
     // forward, the separator rows start at zero
-    const int c0 = grp * 128 + w * RS + lane;
+    const int c0 = grp * CW + w * RS + lane;
     T *xs = xs_all + (size_t)w * SUBTREE_ROWS * RS + lane;
     const T z = S::zero();
     bool ok[C];

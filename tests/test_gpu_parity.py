@@ -203,7 +203,7 @@ def test_star_device_output(gpu, name, dtype, kind):
 
 @pytest.mark.parametrize("name,dtype", [("MinPlus", np.float64), ("MaxMin", np.float32), ("PlusProd", np.float64),
                                         ("OrAnd", np.int32), ("MaxPlus", np.float32)])
-@pytest.mark.parametrize("k", [300, 513])
+@pytest.mark.parametrize("k", [300, 513, 1100])
 def test_wide_solves(gpu, name, dtype, k):
     """lmul! and rmul! with more than 256 right-hand sides (the top fronts' 128-column tasks) against the oracle."""
     n, S, F, O = factor_both("grid3d", name, dtype)

@@ -189,38 +189,108 @@ __global__ void coupling_gather_kernel(const int *__restrict__ js, int cnt, DevP
     }
 }
 
+// The row permutations of lmul! fused with the transpose between the caller's column-major B (n x k) and the
+// internal layout X[position][rhs].  A CTA moves a tile of 64 labels x 256 bytes of right-hand sides through
+// shared memory: on the X side each label's row segment (256 contiguous bytes at position invp[label]) is moved
+// as 16-byte vectors, on the B side each column's 64 consecutive labels, as 16-byte vectors when B's base and
+// column stride allow it (vec_b).  Both sides are coalesced in runs of 256 bytes.
+constexpr int PERM_TL = 64;  // labels per tile
+
+template <typename T>
+struct PermTile {
+    static constexpr int NV = 16 / (int)sizeof(T);     // elements per 16-byte vector
+    static constexpr int TC = 256 / (int)sizeof(T);    // right-hand sides per tile
+    static constexpr int LD = TC + 1;                  // padded row of the shared tile
+};
+
+template <typename T>
+union Vec16u {
+    uint4 v;
+    T e[16 / sizeof(T)];
+};
+
 // X[invp[i]][c] = B[i + c * ldb] (lmul!: permuterows!(B, rinvp) into the internal layout)
 template <typename T>
-__global__ void rows_in_kernel(const T *__restrict__ B, int64_t ldb, T *__restrict__ X, int64_t ldx,
-                               const int *__restrict__ invp, int n, int k) {
-    __shared__ T t[32][33];
-    const int i0 = blockIdx.x * 32, c0 = blockIdx.y * 32, tx = threadIdx.x, ty = threadIdx.y;
-    for (int cc = ty; cc < 32; cc += 8) {
-        const int i = i0 + tx, c = c0 + cc;
-        if (i < n && c < k) t[cc][tx] = B[i + (int64_t)c * ldb];
+__global__ void __launch_bounds__(256) rows_in_kernel(const T *__restrict__ B, int64_t ldb, T *__restrict__ X,
+                                                      int64_t ldx, const int *__restrict__ invp, int n, int k,
+                                                      bool vec_b) {
+    using PT = PermTile<T>;
+    constexpr int NV = PT::NV, TC = PT::TC, LD = PT::LD, GL = PERM_TL / NV, GC = TC / NV;
+    __shared__ T t[PERM_TL * LD];
+    const int l0 = blockIdx.x * PERM_TL, c0 = blockIdx.y * TC;
+    // B: column c0 + cc, labels l0 + g NV .. (PERM_TL / NV groups per column)
+#pragma unroll
+    for (int q = 0; q < TC * GL / 256; q++) {
+        const int v = threadIdx.x + 256 * q, cc = v / GL, g = v % GL, c = c0 + cc, l = l0 + g * NV;
+        if (c >= k) continue;
+        const T *src = B + (int64_t)c * ldb + l;
+        Vec16u<T> u;
+        if (vec_b && l + NV <= n) {
+            u.v = __ldg(reinterpret_cast<const uint4 *>(src));
+        } else {
+#pragma unroll
+            for (int e = 0; e < NV; e++) u.e[e] = l + e < n ? src[e] : T();
+        }
+#pragma unroll
+        for (int e = 0; e < NV; e++) t[(g * NV + e) * LD + cc] = u.e[e];
     }
     __syncthreads();
-    for (int ii = ty; ii < 32; ii += 8) {
-        const int i = i0 + ii, c = c0 + tx;
-        if (i < n && c < k) X[(int64_t)invp[i] * ldx + c] = t[tx][ii];
+    // X: the row of label l0 + r, right-hand sides c0 + cv NV ..
+#pragma unroll
+    for (int q = 0; q < PERM_TL * GC / 256; q++) {
+        const int v = threadIdx.x + 256 * q, r = v / GC, cv = v % GC, l = l0 + r, c = c0 + cv * NV;
+        if (l >= n || c >= k) continue;
+        T *dst = X + (int64_t)invp[l] * ldx + c;
+        Vec16u<T> u;
+#pragma unroll
+        for (int e = 0; e < NV; e++) u.e[e] = t[r * LD + cv * NV + e];
+        if (c + NV <= k) {
+            *reinterpret_cast<uint4 *>(dst) = u.v;  // ldx is a multiple of 4 elements: 16-byte aligned
+        } else {
+            for (int e = 0; c + e < k; e++) dst[e] = u.e[e];
+        }
     }
 }
 
 // B[i + c * ldb] = X[invp[i]][c] (lmul!: permuterows!(B, cperm) out of the internal layout; also the star's
 // column panels); with a column map, column c of the panel goes to column cmap[c] of B
 template <typename T>
-__global__ void rows_out_kernel(T *__restrict__ B, int64_t ldb, const T *__restrict__ X, int64_t ldx,
-                                const int *__restrict__ invp, int n, int k, const int *__restrict__ cmap) {
-    __shared__ T t[32][33];
-    const int i0 = blockIdx.x * 32, c0 = blockIdx.y * 32, tx = threadIdx.x, ty = threadIdx.y;
-    for (int ii = ty; ii < 32; ii += 8) {
-        const int i = i0 + ii, c = c0 + tx;
-        if (i < n && c < k) t[ii][tx] = X[(int64_t)invp[i] * ldx + c];
+__global__ void __launch_bounds__(256) rows_out_kernel(T *__restrict__ B, int64_t ldb, const T *__restrict__ X,
+                                                       int64_t ldx, const int *__restrict__ invp, int n, int k,
+                                                       const int *__restrict__ cmap, bool vec_b) {
+    using PT = PermTile<T>;
+    constexpr int NV = PT::NV, TC = PT::TC, LD = PT::LD, GL = PERM_TL / NV, GC = TC / NV;
+    __shared__ T t[PERM_TL * LD];
+    const int l0 = blockIdx.x * PERM_TL, c0 = blockIdx.y * TC;
+#pragma unroll
+    for (int q = 0; q < PERM_TL * GC / 256; q++) {
+        const int v = threadIdx.x + 256 * q, r = v / GC, cv = v % GC, l = l0 + r, c = c0 + cv * NV;
+        if (l >= n || c >= k) continue;
+        const T *src = X + (int64_t)invp[l] * ldx + c;
+        Vec16u<T> u;
+        if (c + NV <= k) {
+            u.v = __ldcs(reinterpret_cast<const uint4 *>(src));  // read once: streaming
+        } else {
+#pragma unroll
+            for (int e = 0; e < NV; e++) u.e[e] = c + e < k ? src[e] : T();
+        }
+#pragma unroll
+        for (int e = 0; e < NV; e++) t[r * LD + cv * NV + e] = u.e[e];
     }
     __syncthreads();
-    for (int cc = ty; cc < 32; cc += 8) {
-        const int i = i0 + tx, c = c0 + cc;
-        if (i < n && c < k) B[i + (int64_t)(cmap ? cmap[c] : c) * ldb] = t[tx][cc];
+#pragma unroll
+    for (int q = 0; q < TC * GL / 256; q++) {
+        const int v = threadIdx.x + 256 * q, cc = v / GL, g = v % GL, c = c0 + cc, l = l0 + g * NV;
+        if (c >= k || l >= n) continue;
+        T *dst = B + (int64_t)(cmap ? cmap[c] : c) * ldb + l;
+        Vec16u<T> u;
+#pragma unroll
+        for (int e = 0; e < NV; e++) u.e[e] = t[(g * NV + e) * LD + cc];
+        if (vec_b && l + NV <= n) {
+            __stcs(reinterpret_cast<uint4 *>(dst), u.v);
+        } else {
+            for (int e = 0; e < NV && l + e < n; e++) dst[e] = u.e[e];
+        }
     }
 }
 

@@ -248,9 +248,11 @@ struct Engine {
                                     int64_t *nl, bool reset = true) {
         if (wl.second == 0) return cudaSuccess;
         const int pi = hp.prof ? hp.prof->begin(FWD ? K_SWEEP_FWD_BOTTOM : K_SWEEP_BWD_BOTTOM, st) : -1;
-        // wide solves: two columns per lane, so each staged factor value serves two (x)(+) pairs and each task's
-        // wait and staging serve twice the columns
-        if (k >= SWEEP_WIDE_K)
+        // wide solves: two columns per lane (four in the forward sweep of 4-byte types), so each staged factor
+        // value serves several (x)(+) pairs and each task's wait and staging serve more columns
+        if (FWD && sizeof(T) == 4 && k >= 4 * SWEEP_WIDE_K)  // (backward measured slower at four)
+            PP_TRY((sweep_bottom_c<FWD, TRANS, 4>(hp, d, seg_lo, seg_hi, wl, Dv, Ov, X, ldx, k, unit, st, reset)));
+        else if (k >= SWEEP_WIDE_K)
             PP_TRY((sweep_bottom_c<FWD, TRANS, 2>(hp, d, seg_lo, seg_hi, wl, Dv, Ov, X, ldx, k, unit, st, reset)));
         else
             PP_TRY((sweep_bottom_c<FWD, TRANS, 1>(hp, d, seg_lo, seg_hi, wl, Dv, Ov, X, ldx, k, unit, st, reset)));
@@ -395,26 +397,30 @@ struct Engine {
         return cudaGetLastError();
     }
 
+    // 16-byte vectors on the caller's side when its base and column stride are 16-byte aligned
+    static bool vec_ok(const void *B, int64_t ldb) {
+        return ((uintptr_t)B % 16 == 0) && ((ldb * (int64_t)sizeof(T)) % 16 == 0);
+    }
+    static dim3 perm_grid(int n, int k) {
+        constexpr int tc = PermTile<T>::TC;
+        return dim3((n + PERM_TL - 1) / PERM_TL, (k + tc - 1) / tc);
+    }
     static cudaError_t rows_out_mapped(void *B, int64_t ldb, const void *X, int64_t ldx, const int *invp,
                                        const int *cmap, int n, int k, cudaStream_t st) {
-        dim3 grid((n + 31) / 32, (k + 31) / 32), block(32, 8);
-        rows_out_kernel<T><<<grid, block, 0, st>>>(static_cast<T *>(B), ldb, static_cast<const T *>(X), ldx, invp, n, k,
-                                                   cmap);
+        rows_out_kernel<T><<<perm_grid(n, k), 256, 0, st>>>(static_cast<T *>(B), ldb, static_cast<const T *>(X), ldx,
+                                                            invp, n, k, cmap, vec_ok(B, ldb));
         return cudaGetLastError();
     }
 
     static cudaError_t rows_in(const void *B, int64_t ldb, void *X, int64_t ldx, const int *invp, int n, int k,
                                cudaStream_t st) {
-        dim3 grid((n + 31) / 32, (k + 31) / 32), block(32, 8);
-        rows_in_kernel<T><<<grid, block, 0, st>>>(static_cast<const T *>(B), ldb, static_cast<T *>(X), ldx, invp, n, k);
+        rows_in_kernel<T><<<perm_grid(n, k), 256, 0, st>>>(static_cast<const T *>(B), ldb, static_cast<T *>(X), ldx,
+                                                           invp, n, k, vec_ok(B, ldb));
         return cudaGetLastError();
     }
     static cudaError_t rows_out(void *B, int64_t ldb, const void *X, int64_t ldx, const int *invp, int n, int k,
                                 cudaStream_t st) {
-        dim3 grid((n + 31) / 32, (k + 31) / 32), block(32, 8);
-        rows_out_kernel<T><<<grid, block, 0, st>>>(static_cast<T *>(B), ldb, static_cast<const T *>(X), ldx, invp, n, k,
-                                                   nullptr);
-        return cudaGetLastError();
+        return rows_out_mapped(B, ldb, X, ldx, invp, nullptr, n, k, st);
     }
     static cudaError_t cols_in(const void *B, int64_t ldb, void *X, int64_t ldx, const int *invp, int n, int k,
                                cudaStream_t st) {

@@ -232,19 +232,20 @@ __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &
         const int ors = TRANS ? nn : 1, ocs = TRANS ? 1 : na;  // O(i, p) = O[i * ors + p * ocs]
 #pragma unroll
         for (int p = 0; p < NMAX; p++) {
-            if (p >= nn) break;
-            if (scale) {
-                const T s = S::star(Ds[p * (drs + dcs)]);
+            if (p < nn) {
+                if (scale) {
+                    const T s = S::star(Ds[p * (drs + dcs)]);
 #pragma unroll
-                for (int j = 0; j < C; j++) x[p][j] = S::mul(x[p][j], s);
-            }
-#pragma unroll
-            for (int q = p + 1; q < NMAX; q++)
-                if (q < nn) {
-                    const T d = Ds[q * drs + p * dcs];
-#pragma unroll
-                    for (int j = 0; j < C; j++) x[q][j] = S::muladd(d, x[p][j], x[q][j]);
+                    for (int j = 0; j < C; j++) x[p][j] = S::mul(x[p][j], s);
                 }
+#pragma unroll
+                for (int q = p + 1; q < NMAX; q++)
+                    if (q < nn) {
+                        const T d = Ds[q * drs + p * dcs];
+#pragma unroll
+                        for (int j = 0; j < C; j++) x[q][j] = S::muladd(d, x[p][j], x[q][j]);
+                    }
+            }
         }
 #pragma unroll
         for (int p = 0; p < NMAX; p++)
@@ -280,14 +281,15 @@ __device__ __forceinline__ void warp_front_tile(int f, int tile, const DevPlan &
             }
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-                if (i0 + u >= na) break;
+                if (i0 + u < na) {
 #pragma unroll
-                for (int p = 0; p < NMAX; p++)
-                    if (p < nn) {
-                        const T o = Os[p * ors + (i0 + u) * ocs];
+                    for (int p = 0; p < NMAX; p++)
+                        if (p < nn) {
+                            const T o = Os[p * ors + (i0 + u) * ocs];
 #pragma unroll
-                        for (int j = 0; j < C; j++) x[p][j] = S::muladd(o, xv[u][j], x[p][j]);
-                    }
+                            for (int j = 0; j < C; j++) x[p][j] = S::muladd(o, xv[u][j], x[p][j]);
+                        }
+                }
             }
         }
 #pragma unroll

@@ -159,32 +159,36 @@ __global__ void getrf_batched_kernel(int n, T *A) {
 // transposed solves, B <- B U* and B <- B L* on the rows of B).  FWD is the forward sweep with the (+)-scatter
 // to the separator; otherwise the backward sweep gathering from it.  unit = diag :U (no star on the diagonal).
 
+// The coupling products run a thread per (coupled vertex j, right-hand side c): blockIdx.x picks j, the
+// threads of blockIdx.y cover the columns (coalesced rows of X), so that a stage with few coupled vertices
+// still fills the GPU.
+// lmul!: after the solve of a component, X[i] <- X[i] (+) N[i, j] (x) X[j] for its coupling entries
+// (sgemx_sparse!, src/CPU/sparse/sgemx.jl:101-213); a zero product changes nothing and is not scattered.
 template <int SR, typename T>
-__global__ void coupling_scatter_kernel(const int *__restrict__ js, int cnt, DevPlan P, const T *__restrict__ Nval,
-                                        T *X, int64_t ldx, int k) {
+__global__ void coupling_scatter_kernel(const int *__restrict__ js, DevPlan P, const T *__restrict__ Nval, T *X,
+                                        int64_t ldx, int k) {
     using S = Sem<SR, T>;
-    const int wid = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-    if (wid >= cnt) return;
-    const int j = js[wid];
-    for (int64_t p = P.nptr[j]; p < P.nptr[j + 1]; p++) {
-        const int i = P.ntgt[p];
-        const T v = Nval[p];
-        for (int c = lane; c < k; c += 32) S::atomic_add(X + (int64_t)i * ldx + c, S::mul(v, X[(int64_t)j * ldx + c]));
+    const int j = js[blockIdx.x];
+    const int64_t p0 = P.nptr[j], p1 = P.nptr[j + 1];
+    for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < k; c += gridDim.y * blockDim.x) {
+        const T xj = X[(int64_t)j * ldx + c];
+        for (int64_t p = p0; p < p1; p++) {
+            const T m = S::mul(Nval[p], xj);
+            if (!(m == S::zero())) S::atomic_add(X + (int64_t)P.ntgt[p] * ldx + c, m);
+        }
     }
 }
 
 // rmul!: before the solve of a component, X[j] <- X[j] (+) X[i] (x) N[i, j] (sgemx_sparse_st!, :101-113)
 template <int SR, typename T>
-__global__ void coupling_gather_kernel(const int *__restrict__ js, int cnt, DevPlan P, const T *__restrict__ Nval,
-                                       T *X, int64_t ldx, int k) {
+__global__ void coupling_gather_kernel(const int *__restrict__ js, DevPlan P, const T *__restrict__ Nval, T *X,
+                                       int64_t ldx, int k) {
     using S = Sem<SR, T>;
-    const int wid = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-    if (wid >= cnt) return;
-    const int j = js[wid];
-    for (int c = lane; c < k; c += 32) {
+    const int j = js[blockIdx.x];
+    const int64_t p0 = P.nptr[j], p1 = P.nptr[j + 1];
+    for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < k; c += gridDim.y * blockDim.x) {
         T acc = X[(int64_t)j * ldx + c];
-        for (int64_t p = P.nptr[j]; p < P.nptr[j + 1]; p++)
-            acc = S::muladd(X[(int64_t)P.ntgt[p] * ldx + c], Nval[p], acc);
+        for (int64_t p = p0; p < p1; p++) acc = S::muladd(X[(int64_t)P.ntgt[p] * ldx + c], Nval[p], acc);
         X[(int64_t)j * ldx + c] = acc;
     }
 }

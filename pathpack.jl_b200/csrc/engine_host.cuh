@@ -336,6 +336,11 @@ struct Engine {
                                          ba.second == 0);
     }
 
+    // the coupling kernels: a CTA row per coupled vertex, 256 columns per CTA
+    static dim3 coupling_grid(int nverts, int k) {
+        return dim3((unsigned)nverts, (unsigned)std::min(65535, (k + 255) / 256));
+    }
+
     // left: lmul! (X <- A* X: per stage L* forward, U* backward, then the coupling scatter);
     // otherwise rmul! on the transposed layout (per stage the coupling gather, then U* forward, L* backward).
     // src/CPU/blocked/sgetrs.jl:203-255 and src/CPU/chordal/sgetrs.jl:29-51.
@@ -357,8 +362,8 @@ struct Engine {
                 PP_TRY((sweep_subtrees<false, false>(hp, hp.sub_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 if (sg.coupled && sg.nverts > 0) {
                     const int pi = hp.prof ? hp.prof->begin(K_COUPLING, st) : -1;
-                    coupling_scatter_kernel<SR, T><<<(sg.nverts + 7) / 8, 256, 0, st>>>(
-                        hp.d_sverts + sg.voff, sg.nverts, hp.dev, Nv, X, ldx, k);
+                    coupling_scatter_kernel<SR, T><<<coupling_grid(sg.nverts, k), 256, 0, st>>>(
+                        hp.d_sverts + sg.voff, hp.dev, Nv, X, ldx, k);
                     PP_TRY(cudaGetLastError());
                     if (pi >= 0) hp.prof->end(pi, st, 0, 0);
                     nl++;
@@ -369,8 +374,8 @@ struct Engine {
                 const Stage &sg = hp.rstages[s];
                 if (sg.coupled && sg.nverts > 0) {
                     const int pi = hp.prof ? hp.prof->begin(K_COUPLING, st) : -1;
-                    coupling_gather_kernel<SR, T><<<(sg.nverts + 7) / 8, 256, 0, st>>>(
-                        hp.d_sverts + sg.voff, sg.nverts, hp.dev, Nv, X, ldx, k);
+                    coupling_gather_kernel<SR, T><<<coupling_grid(sg.nverts, k), 256, 0, st>>>(
+                        hp.d_sverts + sg.voff, hp.dev, Nv, X, ldx, k);
                     PP_TRY(cudaGetLastError());
                     if (pi >= 0) hp.prof->end(pi, st, 0, 0);
                     nl++;

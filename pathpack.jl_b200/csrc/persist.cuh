@@ -178,6 +178,37 @@ __device__ __forceinline__ void cp_async_elem(T *dst, const T *src) {
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// 16 bytes (both addresses 16-byte aligned), bypassing L1
+__device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
+// A warp copies `rows` rows of RS elements (columns cw0 .. cw0 + RS - 1 of X, rows row(s)) into shared memory at
+// xw + s * RS, as 16-byte chunks (or zero-fills them when zero): the columns of a chunk are contiguous in both.
+// Columns at or past k are zero-filled.  The data are visible to the warp after cp_async_wait_all + __syncwarp.
+template <typename T, int RS, typename RowOf>
+__device__ __forceinline__ void warp_stage_rows(T *xw, const T *X, int64_t ldx, int cw0, int k, int rows, RowOf row,
+                                                bool zero, T z) {
+    constexpr int NV = 16 / (int)sizeof(T), NCH = RS / NV;
+    const int lane = threadIdx.x & 31;
+    for (int e = lane; e < rows * NCH; e += 32) {
+        const int s = e / NCH, ch = e - s * NCH, col = cw0 + ch * NV;
+        T *dst = xw + s * RS + ch * NV;
+        if (!zero && col + NV <= k) {
+            cp_async_16(dst, X + (int64_t)row(s) * ldx + col);
+        } else {
+            const T *src = X + (int64_t)row(s) * ldx + col;
+#pragma unroll
+            for (int u = 0; u < NV; u++) {
+                if (!zero && col + u < k)
+                    cp_async_elem(dst + u, src + u);
+                else
+                    dst[u] = z;
+            }
+        }
+    }
+}
 
 // shared memory of one warp of sweep_bottom_kernel: a front's factor blocks (D, then the off-diagonal block)
 // and its separator positions
@@ -591,40 +622,23 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
     }
     // this warp's columns c0 + 32j of the subtree's rows, copied asynchronously (all in flight at once);
     // forward, the separator rows start at zero
-    const int c0 = grp * CW + w * RS + lane;
-    T *xs = xs_all + (size_t)w * SUBTREE_ROWS * RS + lane;
+    const int cw0 = grp * CW + w * RS, c0 = cw0 + lane;
+    T *const xw = xs_all + (size_t)w * SUBTREE_ROWS * RS;  // this warp's rows
+    T *xs = xw + lane;                                     // this lane's column 0 of them
     const T z = S::zero();
     bool ok[C];
 #pragma unroll
     for (int j = 0; j < C; j++) ok[j] = c0 + 32 * j < k;
-#pragma unroll 4
-    for (int s = 0; s < nres; s++) {
-        const T *xr = X + (int64_t)(rlo0 + s) * ldx + c0;
-#pragma unroll
-        for (int j = 0; j < C; j++) {
-            if (ok[j])
-                cp_async_elem(xs + s * RS + 32 * j, xr + 32 * j);
-            else
-                xs[s * RS + 32 * j] = z;
-        }
-    }
     const int *sepr = P.stgt + P.sptr[r];
-#pragma unroll 4
-    for (int i = 0; i < nsep; i++) {
-        const T *xr = X + (int64_t)sepr[i] * ldx + c0;
-#pragma unroll
-        for (int j = 0; j < C; j++) {
-            if (!FWD && ok[j])
-                cp_async_elem(xs + (nres + i) * RS + 32 * j, xr + 32 * j);
-            else
-                xs[(nres + i) * RS + 32 * j] = z;
-        }
-    }
+    // the subtree's rows as 16-byte chunks; forward, the separator rows start at zero
+    warp_stage_rows<T, RS>(xw, X, ldx, cw0, k, nres, [&](int s) { return rlo0 + s; }, false, z);
+    warp_stage_rows<T, RS>(xw + nres * RS, X, ldx, cw0, k, nsep, [&](int i) { return sepr[i]; }, FWD, z);
     bool nz = false;
     if (FWD && zero_absorbs<SR>) {
         // forward: the right-hand sides that are zero on the subtree's rows change nothing (the sources of
         // these columns lie outside the subtree); a CTA whose columns all are leaves before staging anything
         cp_async_wait_all();
+        __syncwarp();
         for (int s = 0; s < nres; s++)
 #pragma unroll
             for (int j = 0; j < C; j++) nz |= !(xs[s * RS + 32 * j] == z);
@@ -663,11 +677,20 @@ __global__ void __launch_bounds__(128) sweep_subtree_kernel(const int *__restric
         else
             subtree_front<SR, T, FWD, TRANS, SWEEP_NNW, C>(nn, na, xg, xs, D, O, sl, scale);
     }
-    for (int s = 0; s < nres; s++) {
-        T *xr = X + (int64_t)(rlo0 + s) * ldx + c0;
-#pragma unroll
-        for (int j = 0; j < C; j++)
-            if (ok[j]) xr[32 * j] = xs[s * RS + 32 * j];
+    // the residual rows back, as 16-byte chunks (a lane writes columns other lanes computed)
+    __syncwarp();
+    {
+        constexpr int NV = 16 / (int)sizeof(T), NCH = RS / NV;
+        for (int e = lane; e < nres * NCH; e += 32) {
+            const int s = e / NCH, ch = e - s * NCH, col = cw0 + ch * NV;
+            T *dst = X + (int64_t)(rlo0 + s) * ldx + col;
+            const T *src = xw + s * RS + ch * NV;
+            if (col + NV <= k) {
+                *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+            } else {
+                for (int u = 0; u < NV && col + u < k; u++) dst[u] = src[u];
+            }
+        }
     }
     if (FWD)
         for (int i = 0; i < nsep; i++) {

@@ -544,6 +544,8 @@ static std::vector<int> schedule_order(const std::vector<int> &fronts, const std
     return order;
 }
 
+static cudaError_t exchange_parts(void *ctx, cudaStream_t st);  // the split factorization's exchange (below)
+
 // Unpadded algorithmic costs per front of a merged plan (see HostPlan::ufac_pairs).
 struct UCost {
     std::vector<double> fpairs, felems, spairs;
@@ -980,6 +982,10 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
         hp.ev_bottom = h->ev_bottom;
         hp.ev_factored = h->ev_factored;
         hp.top_stream = h->factor_stream;
+        // a handle joined to a group of GPUs (pp_comm_init) before its structure was set keeps the exchange of
+        // the ranks' parts
+        hp.exchange = h->nranks > 1 ? exchange_parts : nullptr;
+        hp.exchange_ctx = h->nranks > 1 ? h : nullptr;
         h->invp = invp;
         h->pnt = pnt;
         h->sfronts = sfronts;

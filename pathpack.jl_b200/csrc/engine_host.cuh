@@ -91,10 +91,10 @@ struct Engine {
             PP_TRY(reset_sync(hp, hp.d_fpending0, 1, st));
             const size_t smem = (size_t)hp.fb_maxnj * hp.fb_maxnj * sizeof(T);
             int per_sm = 1;
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, factor_bottom_kernel<SR, T>, 128, smem);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, factor_bottom_kernel<SR, T>, FB_THREADS, smem);
             const int grid = std::max(1, std::min(hp.fb_count, std::max(per_sm, 1) * hp.sm_count));
             const int pi = hp.prof ? hp.prof->begin(K_FRONT_BOTTOM, st) : -1;
-            factor_bottom_kernel<SR, T><<<grid, 128, smem, st>>>(hp.d_fbottom, hp.fb_count, hp.dev, LD, LL, UD, UL, W,
+            factor_bottom_kernel<SR, T><<<grid, FB_THREADS, smem, st>>>(hp.d_fbottom, hp.fb_count, hp.dev, LD, LL, UD, UL, W,
                                                                  hp.d_sync + 16, hp.d_sync, hp.d_err);
             PP_TRY(cudaGetLastError());
             if (pi >= 0) hp.prof->end(pi, st, hp.fb_bytes, hp.fb_pairs);

@@ -122,7 +122,7 @@ __device__ __forceinline__ int cta_claim(int *p, int *err) {
 // for its children and factors it unless such a CTA claimed it first.  Every front is claimed exactly once
 // (the counter goes 0 -> -1 by compare-and-swap).
 template <int SR, typename T>
-__global__ void __launch_bounds__(128) factor_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P, T *LD,
+__global__ void __launch_bounds__(FB_THREADS) factor_bottom_kernel(const int *__restrict__ wl, int count, DevPlan P, T *LD,
                                                             T *LL, T *UD, T *UL, T *W, int *pending, int *next,
                                                             int *err) {
     extern __shared__ __align__(16) unsigned char smem_raw[];

@@ -21,6 +21,8 @@ constexpr int SUBTREE_FAC = 640;
 constexpr int SUBTREE_SLOTS = 640;
 // solves with at least this many right-hand sides take two columns per lane in the subtree and bottom sweeps
 constexpr int SWEEP_WIDE_K = 1024;
+// threads of a CTA of the bottom factorization (a CTA per front)
+constexpr int FB_THREADS = 256;
 // tile edge of the persistent factorization of the top of the tree
 constexpr int TOP_TILE = 64;
 // rows of a block task of the top sweeps

@@ -2296,12 +2296,13 @@ static int32_t star_impl(pp_handle *h, void *C, int64_t ldc, int64_t col0, int64
     CK(h, cudaSetDevice(h->device), who);
     const size_t es = h->ops->esize;
     // panel width, a multiple of 32 columns: wide panels give the sweeps of the top fronts, whose 64-row blocks
-    // form dependency chains, many independent column tiles to run beside each chain (about 2 GB of right-hand
-    // sides per panel, at most 16,384 columns); host output uses panels of about 256 MB so that the copy of one
-    // panel to the host overlaps the computation of the next
-    const int64_t budget = where == PP_DEVICE ? ((int64_t)1 << 31) : ((int64_t)1 << 28);
+    // form dependency chains, many independent column tiles to run beside each chain, and each panel pays the
+    // launches' tails once (about 8 GB of right-hand sides per panel, at most 32,768 columns: config 3's star
+    // 255.7 -> 228.7 ms against 2 GB panels of at most 16,384); host output uses panels of about 256 MB so that
+    // the copy of one panel to the host overlaps the computation of the next
+    const int64_t budget = where == PP_DEVICE ? ((int64_t)1 << 33) : ((int64_t)1 << 28);
     int64_t pw = budget / std::max<int64_t>((int64_t)es * n, 1);
-    pw = std::max<int64_t>(32, std::min<int64_t>(pw & ~(int64_t)31, where == PP_DEVICE ? 16384 : 4096));
+    pw = std::max<int64_t>(32, std::min<int64_t>(pw & ~(int64_t)31, where == PP_DEVICE ? 32768 : 4096));
     pw = std::min<int64_t>(pw, (ncols + 31) & ~(int64_t)31);
     const int64_t ldx = pw;
     const size_t xbytes = es * (size_t)n * ldx;

@@ -119,3 +119,27 @@ def test_config4_star_columns_vs_oracle(gpu):
         same(got, want, "MinPlus", np.float32, "config 4 star columns")
     finally:
         F.close()
+
+
+def test_star_wide_device_panel(gpu):
+    """Matrix(F) into device memory in one panel wider than 16,384 columns (the star takes panels of up to 32,768
+    columns): 256 columns spread over the panel, bit for bit against the oracle's lmul! of their unit columns."""
+    import torch
+
+    n, I, J, W = graphs.grid2d(141, 141, 1.0, 10.0, seed=77, dtype=np.float32)
+    cp, rv, nz = graphs.csc(n, I, J, W)
+    S = pp.ssymbolic(n, cp, rv)
+    F = pp.B200SLU(pp.MinPlus(), np.float32, S, device=0).assemble_csc(cp, rv, nz).factor()
+    try:
+        assert n > 16384
+        out = torch.empty((n, n), dtype=torch.float32, device="cuda:0").t()  # column-major n x n
+        F.star(0, n, out=out)
+        cols = np.sort(np.random.default_rng(5).choice(n, 256, replace=False))
+        O = OracleLU("MinPlus", np.float32, S).assemble(cp, rv, nz).factor()
+        E = np.full((n, len(cols)), np.inf, dtype=np.float32, order="F")
+        E[cols, np.arange(len(cols))] = 0.0
+        want = O.lmul(E)
+        got = out[:, torch.from_numpy(cols).cuda()].cpu().numpy()
+        same(got, want, "MinPlus", np.float32, "star columns of a 19,881-column device panel")
+    finally:
+        F.close()

@@ -184,6 +184,7 @@ struct pp_handle {
     // writes the factor makes the handle's stream wait for ev_factored first (after_factor)
     cudaStream_t factor_stream = nullptr;
     cudaEvent_t ev_bottom = nullptr, ev_factored = nullptr;
+    cudaEvent_t ev_top_a = nullptr;  // the end of the top factorization's first launch (every front but the roots)
     cudaEvent_t copy_ev = nullptr;
     // lmul! on host memory in column panels: panel p's upload done (in_ev) and solve done (out_ev); the results
     // go back on out_stream while the next panel is solved
@@ -345,6 +346,7 @@ extern "C" int32_t pp_create(int32_t device, pp_handle **out) {
     if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&h->factor_stream, cudaStreamNonBlocking, prio_high);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->ev_bottom, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->ev_factored, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->ev_top_a, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&h->ev1);
     if (e == cudaSuccess) e = cudaEventCreate(&h->fev0);
@@ -390,7 +392,7 @@ extern "C" int32_t pp_destroy(pp_handle *h) {
         cudaStreamSynchronize(h->factor_stream);
         cudaStreamDestroy(h->factor_stream);
     }
-    for (cudaEvent_t ev : {h->ev_bottom, h->ev_factored})
+    for (cudaEvent_t ev : {h->ev_bottom, h->ev_factored, h->ev_top_a})
         if (ev) cudaEventDestroy(ev);
     for (int i = 0; i < 2; i++) {
         if (h->panel_ready[i]) cudaEventDestroy(h->panel_ready[i]);
@@ -805,7 +807,7 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
                                 std::vector<std::pair<int64_t, int>> &bbwd, std::vector<SLevel> &bcost,
                                 std::vector<SubtreeList> &subs, std::vector<int> &sroots,
                                 std::vector<std::pair<int64_t, int>> &tfwd, std::vector<std::pair<int64_t, int>> &tbwd,
-                                std::vector<SLevel> &tcost, std::vector<int> &tentries) {
+                                std::vector<SLevel> &tcost, std::vector<int> &tentries, std::vector<int> &tfa) {
             int ns = 0;
             for (int64_t c = 0; c < nB; c++) ns = std::max(ns, stage_of[c] + 1);
             if (nB == 0) ns = 0;
@@ -819,6 +821,7 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
             tfwd.clear();
             tbwd.clear();
             tcost.clear();
+            tfa.clear();
             for (int s = 0; s < ns; s++) {
                 Stage sg;
                 std::vector<std::vector<int>> byh(maxh + 1), bot(maxh + 1);
@@ -881,6 +884,21 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
                     tc.pairs_col += col_pairs(f);
                 }
                 tf.second = (int)(tentries.size() / 2 - tf.first);
+                {
+                    // the roots' entries last (a root is forward-swept once the whole factorization has ended)
+                    std::vector<std::pair<int, int>> ent(tf.second);
+                    for (int i = 0; i < tf.second; i++)
+                        ent[i] = {tentries[2 * (tf.first + i)], tentries[2 * (tf.first + i) + 1]};
+                    std::stable_partition(ent.begin(), ent.end(),
+                                          [&](const std::pair<int, int> &e) { return pnt[e.first] >= 0; });
+                    int na = 0;
+                    for (int i = 0; i < tf.second; i++) {
+                        tentries[2 * (tf.first + i)] = ent[i].first;
+                        tentries[2 * (tf.first + i) + 1] = ent[i].second;
+                        if (pnt[ent[i].first] >= 0) na++;
+                    }
+                    tfa.push_back(na);
+                }
                 std::pair<int64_t, int> tb{(int64_t)tentries.size() / 2, 0};
                 for (int f : schedule_order(tdown, tscost, pnt, false, tslots))
                     for (int b = blocks(hp.nn[f]) - 1; b >= 0; b--) tentries.insert(tentries.end(), {f, b});
@@ -899,10 +917,10 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
         };
         std::vector<int> sfronts, sverts, sroots, tentries;
         build_stages(lstage, hp.lstages, sfronts, sverts, hp.sb_fwd, hp.sb_bwd, hp.sb_cost_l, hp.sub_l, sroots,
-                     hp.st_fwd, hp.st_bwd, hp.st_cost_l, tentries);
+                     hp.st_fwd, hp.st_bwd, hp.st_cost_l, tentries, hp.st_fwd_a);
         // rmul stages: the gather concerns the stage's own columns j (rows of earlier components feed them)
         build_stages(rstage, hp.rstages, sfronts, sverts, hp.sb_fwd_r, hp.sb_bwd_r, hp.sb_cost_r, hp.sub_r, sroots,
-                     hp.st_fwd_r, hp.st_bwd_r, hp.st_cost_r, tentries);
+                     hp.st_fwd_r, hp.st_bwd_r, hp.st_cost_r, tentries, hp.st_fwd_r_a);
         (void)ccoupled;
         std::vector<int64_t> Np64(Np.begin(), Np.end());
         // device uploads
@@ -981,6 +999,7 @@ static int32_t build_structure(pp_handle *h, int64_t n, int64_t nf, int64_t nB, 
         hp.sm_count = h->sm_count;
         hp.ev_bottom = h->ev_bottom;
         hp.ev_factored = h->ev_factored;
+        hp.ev_top_a = h->ev_top_a;
         hp.top_stream = h->factor_stream;
         // a handle joined to a group of GPUs (pp_comm_init) before its structure was set keeps the exchange of
         // the ranks' parts
@@ -1562,6 +1581,9 @@ static int32_t prepare_workspace(pp_handle *h) {
         std::vector<double> tcost(nf, 0.0);
         for (int f : tl) tcost[f] = 20.0 + 50.0 * ((hp.nn[f] + TOP_TILE - 1) / TOP_TILE);
         tl = schedule_order(tl, tcost, h->pnt, true, std::max(1, h->sm_count * 2 / 16));
+        // the roots of the tree last: the factorization's second launch (every dependency of a root is earlier)
+        std::stable_partition(tl.begin(), tl.end(), [&](int f) { return h->pnt[f] >= 0; });
+        int ntasks_a = -1;
         std::vector<int> tasks, crng;
         std::vector<int64_t> foff(nf, 0), croff(std::max<size_t>(hp.chdtgt.size(), 1), 0);
         int64_t nflags = 16;
@@ -1569,6 +1591,7 @@ static int32_t prepare_workspace(pp_handle *h) {
         std::vector<std::pair<int, int>> tiles;
         std::vector<int> bounds;
         for (int f : tl) {
+            if (ntasks_a < 0 && h->pnt[f] < 0) ntasks_a = (int)(tasks.size() / 4);
             const int nn = hp.nn[f], na = hp.na[f];
             const int kb = (nn + TOP_TILE - 1) / TOP_TILE, nbt = kb + (na + TOP_TILE - 1) / TOP_TILE;
             foff[f] = nflags;
@@ -1597,6 +1620,7 @@ static int32_t prepare_workspace(pp_handle *h) {
             front_cost(hp, f, acc);
         }
         hp.top_ntasks = (int)(tasks.size() / 4);
+        hp.top_ntasks_a = ntasks_a < 0 ? hp.top_ntasks : ntasks_a;
         hp.top_cost = acc;
         hp.tflags_n = nflags;
         if (tasks.empty()) tasks.assign(4, 0);
@@ -2550,6 +2574,7 @@ extern "C" int32_t pp_get_profile(pp_handle *h, pp_kernel_class *out, int32_t ma
 static cudaError_t uncapture_events(pp_handle *h) {
     cudaError_t e = cudaEventRecord(h->ev_bottom, h->stream);
     if (e == cudaSuccess) e = cudaEventRecord(h->ev_factored, h->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(h->ev_top_a, h->stream);
     return e;
 }
 

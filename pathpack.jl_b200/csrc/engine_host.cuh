@@ -112,14 +112,27 @@ struct Engine {
             PP_TRY(cudaMemsetAsync(hp.d_tflags, 0, sizeof(int) * (size_t)hp.tflags_n, ts));
             int per_sm = 1;
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, factor_top_kernel<SR, T>, 256, smem);
-            const int grid = std::max(1, std::min(hp.top_ntasks, std::max(per_sm, 1) * hp.sm_count));
-            const int pi = hp.prof ? hp.prof->begin(K_FACTOR_TOP, ts) : -1;
-            factor_top_kernel<SR, T><<<grid, 256, smem, ts>>>(hp.d_ttasks, hp.top_ntasks, hp.dev, hp.d_tfoff,
-                                                              hp.d_croff, hp.d_crng, LD, LL, UD, UL, W, hp.d_tflags,
-                                                              hp.d_err, hp.d_trace);
-            PP_TRY(cudaGetLastError());
-            if (pi >= 0) hp.prof->end(pi, ts, hp.top_cost.bytes, hp.top_cost.pairs);
-            nl++;
+            // two launches when the top runs on its own stream: every front but the roots, then the roots (the
+            // tile flags persist, the task counter restarts); a solve sweeps the lower fronts in between
+            const bool split = ts != st && hp.ev_top_a && hp.top_ntasks_a > 0 && hp.top_ntasks_a < hp.top_ntasks;
+            const int parts[2][2] = {{0, split ? hp.top_ntasks_a : hp.top_ntasks},
+                                     {split ? hp.top_ntasks_a : hp.top_ntasks, hp.top_ntasks}};
+            for (int q = 0; q < 2; q++) {
+                const int t0 = parts[q][0], cnt = parts[q][1] - parts[q][0];
+                if (cnt <= 0) continue;
+                if (q == 1) PP_TRY(cudaMemsetAsync(hp.d_tflags, 0, sizeof(int), ts));  // the task counter
+                const int grid = std::max(1, std::min(cnt, std::max(per_sm, 1) * hp.sm_count));
+                const int pi = hp.prof ? hp.prof->begin(K_FACTOR_TOP, ts) : -1;
+                factor_top_kernel<SR, T><<<grid, 256, smem, ts>>>(
+                    hp.d_ttasks + t0, cnt, hp.dev, hp.d_tfoff, hp.d_croff, hp.d_crng, LD, LL, UD, UL, W, hp.d_tflags,
+                    hp.d_err, hp.d_trace ? hp.d_trace + (size_t)PP_TRACE_WORDS * t0 : nullptr);
+                PP_TRY(cudaGetLastError());
+                if (pi >= 0) hp.prof->end(pi, ts, q == 0 ? hp.top_cost.bytes : 0, q == 0 ? hp.top_cost.pairs : 0);
+                nl++;
+                if (q == 0 && ts != st && hp.ev_top_a) PP_TRY(cudaEventRecord(hp.ev_top_a, ts));
+            }
+        } else if (ts != st && hp.ev_top_a) {
+            PP_TRY(cudaEventRecord(hp.ev_top_a, ts));
         }
         if (ts != st) PP_TRY(cudaEventRecord(hp.ev_factored, ts));
         if (launches) *launches += nl;
@@ -129,7 +142,7 @@ struct Engine {
     template <bool FWD, bool TRANS>
     static cudaError_t sweep_wide(const HostPlan &hp, const std::pair<int64_t, int> &wl, const SLevel &cost,
                                   const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
-                                  int64_t *nl) {
+                                  int64_t *nl, bool reset = true) {
         constexpr size_t smem = sweep_wide_smem<T>();
         int dev = 0;
         cudaGetDevice(&dev);
@@ -141,7 +154,9 @@ struct Engine {
         }
         const int ntiles = (k + SWW_CT - 1) / SWW_CT;
         const size_t cells = (size_t)ntiles * hp.nf;  // per (tile, front)
-        if (FWD) {
+        if (FWD && !reset) {
+            PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int), st));  // the task counter only
+        } else if (FWD) {
             PP_TRY(reset_sync(hp, hp.d_tpending0, ntiles, st));
             PP_TRY(cudaMemsetAsync(hp.d_sync + 16 + cells, 0, sizeof(int) * 2 * cells, st));  // blocks done
         } else {
@@ -166,14 +181,15 @@ struct Engine {
 
     // the top fronts of a stage: one persistent launch (sweep_top_kernel), counters reset from a template
     template <bool FWD, bool TRANS>
+    // reset = false (forward only) continues the counters of the previous launch (the first part of the list)
     static cudaError_t sweep_top(const HostPlan &hp, const std::pair<int64_t, int> &wl, const SLevel &cost,
                                  const T *Dv, const T *Ov, T *X, int64_t ldx, int k, int unit, cudaStream_t st,
-                                 int64_t *nl) {
+                                 int64_t *nl, bool reset = true) {
         if (wl.second == 0) return cudaSuccess;
         // many right-hand sides (the star's panels, wide solves): 128-column tasks, when the rows of X allow
         // 16-byte vector loads
         if (k > 256 && ldx % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0)
-            return sweep_wide<FWD, TRANS>(hp, wl, cost, Dv, Ov, X, ldx, k, unit, st, nl);
+            return sweep_wide<FWD, TRANS>(hp, wl, cost, Dv, Ov, X, ldx, k, unit, st, nl, reset);
         constexpr size_t smem = sweep_top_smem<T>();
         int dev = 0;
         cudaGetDevice(&dev);
@@ -185,7 +201,9 @@ struct Engine {
         }
         const int ntiles = (k + SW_CT - 1) / SW_CT;
         const size_t cells = (size_t)ntiles * hp.nf;  // per (tile, front)
-        if (FWD) {
+        if (FWD && !reset) {
+            PP_TRY(cudaMemsetAsync(hp.d_sync, 0, sizeof(int), st));  // the task counter only
+        } else if (FWD) {
             PP_TRY(reset_sync(hp, hp.d_tpending0, ntiles, st));
             PP_TRY(cudaMemsetAsync(hp.d_sync + 16 + cells, 0, sizeof(int) * 2 * cells, st));  // blocks done
         } else {
@@ -330,10 +348,31 @@ struct Engine {
         const SLevel none{};  // the profile counts the list's bytes and pairs once, with its first launch
         PP_TRY((sweep_subtrees<true, TRANS>(hp, sa, Dv, Ov, X, ldx, k, unit, st, nl)));
         PP_TRY((sweep_bottom<true, TRANS>(hp, d, 0, 0, ba, cost, Dv, Ov, X, ldx, k, unit, st, nl)));
-        PP_TRY(cudaStreamWaitEvent(st, hp.ev_factored, 0));
+        // the rest of the bottom needs the lower top fronts only (factored by the first top launch)
+        PP_TRY(cudaStreamWaitEvent(st, hp.ev_top_a ? hp.ev_top_a : hp.ev_factored, 0));
         PP_TRY((sweep_subtrees<true, TRANS>(hp, sb, Dv, Ov, X, ldx, k, unit, st, nl)));
         return sweep_bottom<true, TRANS>(hp, d, 1, 1, bb, ba.second ? none : cost, Dv, Ov, X, ldx, k, unit, st, nl,
                                          ba.second == 0);
+    }
+
+    // The forward top sweep of stage s.  In stage 0, behind a factorization whose top ran in two launches, the
+    // fronts other than the roots (listed first) are swept as soon as the first launch has ended, while the
+    // roots are still being factored; the roots' entries follow once the factorization has ended, with the
+    // counters of the first part.
+    template <bool TRANS>
+    static cudaError_t forward_top(const HostPlan &hp, size_t s, const std::pair<int64_t, int> &wl,
+                                   const std::vector<int> &na, const SLevel &cost, const T *Dv, const T *Ov, T *X,
+                                   int64_t ldx, int k, int unit, cudaStream_t st, int64_t *nl) {
+        const int a = s < na.size() ? std::min(na[s], wl.second) : wl.second;
+        if (s == 0 && hp.ev_factored && hp.ev_top_a && a < wl.second) {
+            if (a > 0) PP_TRY((sweep_top<true, TRANS>(hp, {wl.first, a}, cost, Dv, Ov, X, ldx, k, unit, st, nl)));
+            PP_TRY(cudaStreamWaitEvent(st, hp.ev_factored, 0));
+            const SLevel none{};
+            return sweep_top<true, TRANS>(hp, {wl.first + a, wl.second - a}, a > 0 ? none : cost, Dv, Ov, X, ldx, k,
+                                          unit, st, nl, a == 0);
+        }
+        if (s == 0 && hp.ev_factored) PP_TRY(cudaStreamWaitEvent(st, hp.ev_factored, 0));
+        return sweep_top<true, TRANS>(hp, wl, cost, Dv, Ov, X, ldx, k, unit, st, nl);
     }
 
     // the coupling kernels: a CTA row per coupled vertex, 256 columns per CTA
@@ -355,7 +394,7 @@ struct Engine {
             for (size_t s = 0; s < hp.lstages.size(); s++) {
                 const Stage &sg = hp.lstages[s];
                 PP_TRY((forward_bottom<false>(hp, 0, s, LD, LL, X, ldx, k, 1, st, &nl)));
-                PP_TRY((sweep_top<true, false>(hp, hp.st_fwd[s], hp.st_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
+                PP_TRY((forward_top<false>(hp, s, hp.st_fwd[s], hp.st_fwd_a, hp.st_cost_l[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_top<false, false>(hp, hp.st_bwd[s], hp.st_cost_l[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_bottom<false, false>(hp, 0, 2 * (int)s, 2 * (int)s + 1, hp.sb_bwd[s], hp.sb_cost_l[s], UD,
                                                    UL, X, ldx, k, 0, st, &nl)));
@@ -381,7 +420,7 @@ struct Engine {
                     nl++;
                 }
                 PP_TRY((forward_bottom<true>(hp, 1, s, UD, UL, X, ldx, k, 0, st, &nl)));
-                PP_TRY((sweep_top<true, true>(hp, hp.st_fwd_r[s], hp.st_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
+                PP_TRY((forward_top<true>(hp, s, hp.st_fwd_r[s], hp.st_fwd_r_a, hp.st_cost_r[s], UD, UL, X, ldx, k, 0, st, &nl)));
                 PP_TRY((sweep_top<false, true>(hp, hp.st_bwd_r[s], hp.st_cost_r[s], LD, LL, X, ldx, k, 1, st, &nl)));
                 PP_TRY((sweep_bottom<false, true>(hp, 1, 2 * (int)s, 2 * (int)s + 1, hp.sb_bwd_r[s], hp.sb_cost_r[s], LD,
                                                   LL, X, ldx, k, 1, st, &nl)));

@@ -91,8 +91,10 @@ struct HostPlan {
     std::vector<int64_t> mptr, fws;
     std::vector<int> mld;
     int64_t ws_elems = 0;
-    // top of the tree: the tile tasks of the persistent factorization (top.cuh), fronts by height
-    int top_ntasks = 0;
+    // top of the tree: the tile tasks of the persistent factorization (top.cuh), fronts by height; the first
+    // top_ntasks_a tasks are every front but the roots of the tree, the rest the roots' (two launches, so that a
+    // solve can sweep the lower fronts forward while the roots are factored)
+    int top_ntasks = 0, top_ntasks_a = 0;
     const int4 *d_ttasks = nullptr;   // (front, I, J, 0): tile (I, J) of the front
     const int64_t *d_tfoff = nullptr;  // per front: first of its flags in d_tflags
     const int64_t *d_croff = nullptr;  // per child edge (index into chdtgt): first of its ranges in d_crng
@@ -137,6 +139,8 @@ struct HostPlan {
     const int *d_sheavy = nullptr;
     // the top fronts of each stage for the persistent top sweep (forward ascending, backward descending heights)
     std::vector<std::pair<int64_t, int>> st_fwd, st_bwd, st_fwd_r, st_bwd_r;
+    // per stage: the forward lists' entries of fronts other than roots (listed first; the roots' entries follow)
+    std::vector<int> st_fwd_a, st_fwd_r_a;
     std::vector<SLevel> st_cost_l, st_cost_r;
     const int *d_tpending0 = nullptr;  // top children per front (forward counters of the top sweep)
     int *d_sync = nullptr;             // scratch: [0] task counter, [16, 16 + nf * tiles) counters
@@ -145,8 +149,9 @@ struct HostPlan {
     // bottom kernel); ev_factored marks its end.  A solve enqueued behind the factorization runs the first
     // early_sub[d] subtrees and early_bot[d] forward bottom fronts of its stage 0 (d = 0 lmul!, 1 rmul!; all of
     // them factored by the bottom kernel, listed first) before it waits for ev_factored.
+    // ev_top_a marks the end of the first launch of the top factorization (every front but the roots).
     cudaStream_t top_stream = nullptr;
-    cudaEvent_t ev_bottom = nullptr, ev_factored = nullptr;
+    cudaEvent_t ev_bottom = nullptr, ev_factored = nullptr, ev_top_a = nullptr;
     int early_sub[2] = {0, 0}, early_bot[2] = {0, 0};
     int64_t sync_cap = 0;              // ints allocated at d_sync
     int sm_count = 148;

@@ -211,6 +211,9 @@ struct pp_handle {
         d_nptr, d_ntgt, d_perm, d_invp, d_idx, d_bptr, d_fcc, d_sfronts, d_sverts, d_pnt, d_fbottom,
         d_fpending0, d_spending0, d_sdone0, d_tpending0, d_sync, d_tentries, d_sroots, d_fdsc, d_slot, d_ttasks, d_tfoff, d_tflags, d_croff,
         d_crng, d_err, d_sinfo_l, d_sinfo_r, d_sheavy;
+    // the amalgamation map on the device: the caller's structure (R, Sp, St), each caller front's merged front
+    // and the offsets of its blocks in the caller's arrays (merged plans only)
+    DevBuf d_oR, d_oSp, d_oSt, d_ogroup, d_oDf, d_oLf, d_ostage;  // d_ostage: the caller's four arrays
     std::vector<int> pnt, height, rel;
     std::vector<int> sinfo_l, sinfo_r, sheavy;  // continuation of the bottom sweeps (host copies)
     std::vector<int> sfronts, sroots;  // host copies of the solve work lists (reordered by prepare_workspace)
@@ -547,6 +550,7 @@ static std::vector<int> schedule_order(const std::vector<int> &fronts, const std
 }
 
 static cudaError_t exchange_parts(void *ctx, cudaStream_t st);  // the split factorization's exchange (below)
+static cudaError_t upload_merge_map(pp_handle *h, cudaStream_t st);  // the amalgamation map's inputs (below)
 
 // Unpadded algorithmic costs per front of a merged plan (see HostPlan::ufac_pairs).
 struct UCost {
@@ -1278,6 +1282,7 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
             h->ufac_elems = std::move(uc.felems);
             h->usolve_pairs = std::move(uc.spairs);
             r = use_plan(h, true);
+            if (r == PP_OK) CK(h, upload_merge_map(h, h->stream), "pp_set_structure");
         } else {
             h->group.clear();
             h->mrg = pp_handle::Structure();
@@ -1290,60 +1295,122 @@ extern "C" int32_t pp_set_structure(pp_handle *h, int64_t n, int64_t nf, int64_t
     return r;
 }
 
-// The bit pattern of the semiring's zero (the padding of merged blocks).
-static void zero_value(int sr, int dt, void *out) {
-    const bool lo = sr == PP_MINPLUS || sr == PP_MINMAX;  // +Inf
-    const bool hi = sr == PP_MAXPLUS || sr == PP_MAXMIN;  // -Inf
-    if (dt == PP_F32) {
-        const float v = lo ? INFINITY : hi ? -INFINITY : 0.0f;
-        memcpy(out, &v, 4);
-    } else if (dt == PP_F64) {
-        const double v = lo ? (double)INFINITY : hi ? -(double)INFINITY : 0.0;
-        memcpy(out, &v, 8);
-    } else {
-        const int32_t v = sr == PP_MINPLUS ? INT32_MAX : 0;
-        memcpy(out, &v, 4);
+
+// The amalgamation map, evaluated per entry on the device: each entry of the caller's factor arrays (LD, UD,
+// LL, UL of the caller's structure) has one place in the blocks of its front's merged front; the other entries of
+// the merged blocks are the semiring's zero.  A CTA per caller front f moves each of its entries between the
+// caller's layout (c*) and the merged blocks (m*): TO_CALLER gathers
+// (pp_get_factor), otherwise it scatters (pp_set_values; the merged arrays were filled with the semiring's
+// zero first).  The row of a separator vertex in the merged front is its residual offset, or its place in
+// the merged separator (binary search: separators are sorted).  U is an unsigned type of the element size.
+template <typename U, bool TO_CALLER>
+__global__ void merged_layout_kernel(const int64_t *__restrict__ oR, const int64_t *__restrict__ oSp,
+                                     const int64_t *__restrict__ oSt, const int *__restrict__ group,
+                                     const int64_t *__restrict__ oDf, const int64_t *__restrict__ oLf, DevPlan P,
+                                     U *cLD, U *cUD, U *cLL, U *cUL, U *mLD, U *mUD, U *mLL, U *mUL) {
+    const int64_t f = blockIdx.x;
+    const int q = group[f];
+    const int64_t nn = oR[f + 1] - oR[f], na = oSp[f + 1] - oSp[f];
+    const int64_t rq = P.rlo[q], nnq = P.nn[q], naq = P.na[q], off = oR[f] - rq, Dq = P.dptr[q], Lq = P.lptr[q];
+    const int64_t Df = oDf[f], Lf = oLf[f];
+    const int *sq = P.stgt + P.sptr[q];
+    auto move = [&](U *c, int64_t a, U *m, int64_t b) {
+        if (TO_CALLER)
+            c[a] = m[b];
+        else
+            m[b] = c[a];
+    };
+    for (int64_t e = threadIdx.x; e < nn * nn; e += blockDim.x) {
+        const int64_t i = e % nn, j = e / nn, b = Dq + (off + i) + (off + j) * nnq;
+        move(cLD, Df + e, mLD, b);
+        move(cUD, Df + e, mUD, b);
+    }
+    // the merged row of the caller's separator vertex r
+    auto mrow = [&](int64_t r, bool &inres) -> int64_t {
+        const int64_t v = oSt[oSp[f] + r];
+        inres = v < rq + nnq;
+        if (inres) return v - rq;
+        int64_t lo = 0, hi = naq;  // first separator entry >= v
+        while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (sq[mid] < v)
+                lo = mid + 1;
+            else
+                hi = mid;
+        }
+        return lo;
+    };
+    for (int64_t e = threadIdx.x; e < na * nn; e += blockDim.x) {
+        const int64_t r = e % na, j = e / na;  // LL: na x nn
+        bool inres;
+        const int64_t row = mrow(r, inres);
+        if (inres)
+            move(cLL, Lf + e, mLD, Dq + row + (off + j) * nnq);
+        else
+            move(cLL, Lf + e, mLL, Lq + row + (off + j) * naq);
+    }
+    for (int64_t e = threadIdx.x; e < nn * na; e += blockDim.x) {
+        const int64_t i = e % nn, r = e / nn;  // UL: nn x na
+        bool inres;
+        const int64_t row = mrow(r, inres);
+        if (inres)
+            move(cUL, Lf + e, mUD, Dq + (off + i) + row * nnq);
+        else
+            move(cUL, Lf + e, mUL, Lq + (off + i) + row * nnq);
     }
 }
 
-// Every entry of the caller's factor arrays with its place in the merged ones: fn(a, o, ma, mo) for array a
-// (0 LD, 1 UD, 2 LL, 3 UL) at offset o and merged array ma at offset mo.
-template <typename Fn>
-static void for_each_merged_entry(const pp_handle *h, Fn fn) {
-    const pp_handle::Structure &o = h->orig, &m = h->mrg;
-    const HostPlan &hp = h->hp;
-    int64_t Df = 0, Lf = 0;
+// the device copy of the amalgamation map's inputs (the caller's structure, groups, block offsets)
+static cudaError_t upload_merge_map(pp_handle *h, cudaStream_t st) {
+    const pp_handle::Structure &o = h->orig;
+    std::vector<int64_t> Df(o.nf), Lf(o.nf);
+    int64_t d = 0, l = 0;
     for (int64_t f = 0; f < o.nf; f++) {
-        const int q = h->group[f];
         const int64_t nn = o.R[f + 1] - o.R[f], na = o.Sp[f + 1] - o.Sp[f];
-        const int64_t off = o.R[f] - m.R[q], nnq = hp.nn[q], naq = hp.na[q], Dq = hp.dptr[q], Lq = hp.lptr[q];
-        for (int64_t j = 0; j < nn; j++)
-            for (int64_t i = 0; i < nn; i++) {
-                const int64_t a = Df + i + j * nn, b = Dq + (off + i) + (off + j) * nnq;
-                fn(0, a, 0, b);
-                fn(1, a, 1, b);
-            }
-        const int64_t *sq0 = m.St.data() + m.Sp[q], *sq1 = m.St.data() + m.Sp[q + 1];
-        for (int64_t r = 0; r < na; r++) {
-            const int64_t v = o.St[o.Sp[f] + r];
-            const bool inres = v < m.R[q + 1];
-            const int64_t row = inres ? v - m.R[q] : (int64_t)(std::lower_bound(sq0, sq1, v) - sq0);
-            for (int64_t j = 0; j < nn; j++) {
-                if (inres)
-                    fn(2, Lf + r + j * na, 0, Dq + row + (off + j) * nnq);
-                else
-                    fn(2, Lf + r + j * na, 2, Lq + row + (off + j) * naq);
-            }
-            for (int64_t i = 0; i < nn; i++) {
-                if (inres)
-                    fn(3, Lf + i + r * nn, 1, Dq + (off + i) + row * nnq);
-                else
-                    fn(3, Lf + i + r * nn, 3, Lq + (off + i) + row * nnq);
-            }
-        }
-        Df += nn * nn;
-        Lf += nn * na;
+        Df[f] = d;
+        Lf[f] = l;
+        d += nn * nn;
+        l += nn * na;
     }
+    cudaError_t e = upload(h->d_oR, o.R, st);
+    if (e == cudaSuccess) e = upload(h->d_oSp, o.Sp, st);
+    if (e == cudaSuccess) e = upload(h->d_oSt, o.St, st);
+    if (e == cudaSuccess) e = upload(h->d_ogroup, h->group, st);
+    if (e == cudaSuccess) e = upload(h->d_oDf, Df, st);
+    if (e == cudaSuccess) e = upload(h->d_oLf, Lf, st);
+    if (e == cudaSuccess) e = stream_wait(h, st);  // the host vectors are freed on return
+    return e;
+}
+
+// caller layout <-> merged blocks on the device; c[4] = caller LD, UD, LL, UL in device memory
+static cudaError_t merged_layout(pp_handle *h, void *const c[4], bool to_caller, cudaStream_t st) {
+    const int64_t nf = h->orig.nf;
+    if (nf == 0) return cudaSuccess;
+    const int64_t *oR = h->d_oR.as<int64_t>(), *oSp = h->d_oSp.as<int64_t>(), *oSt = h->d_oSt.as<int64_t>();
+    const int *grp = h->d_ogroup.as<int>();
+    const int64_t *oDf = h->d_oDf.as<int64_t>(), *oLf = h->d_oLf.as<int64_t>();
+    void *m[4] = {h->LD.p, h->UD.p, h->LL.p, h->UL.p};
+    auto go = [&](auto tag) {
+        using U = decltype(tag);
+        U *cc[4], *mm[4];
+        for (int a = 0; a < 4; a++) {
+            cc[a] = static_cast<U *>(c[a]);
+            mm[a] = static_cast<U *>(m[a]);
+        }
+        if (to_caller)
+            merged_layout_kernel<U, true><<<(unsigned)nf, 128, 0, st>>>(oR, oSp, oSt, grp, oDf, oLf, h->hp.dev, cc[0],
+                                                                         cc[1], cc[2], cc[3], mm[0], mm[1], mm[2],
+                                                                         mm[3]);
+        else
+            merged_layout_kernel<U, false><<<(unsigned)nf, 128, 0, st>>>(oR, oSp, oSt, grp, oDf, oLf, h->hp.dev, cc[0],
+                                                                          cc[1], cc[2], cc[3], mm[0], mm[1], mm[2],
+                                                                          mm[3]);
+    };
+    if (h->ops->esize == 8)
+        go((unsigned long long)0);
+    else
+        go((unsigned)0);
+    return cudaGetLastError();
 }
 
 // Algorithmic traffic (elements) and (x)(+) pairs of one front's factorization: read the assembled blocks
@@ -1820,28 +1887,23 @@ extern "C" int32_t pp_set_values(pp_handle *h, int32_t semiring, int32_t dtype, 
     if ((h->st.nD > 0 && (!LD || !UD)) || (h->st.nL > 0 && (!LL || !UL)) || (h->hp.nN > 0 && !Nval))
         return fail(h, PP_EINVAL, "pp_set_values: null array");
     if (h->merged) {
-        // the caller's blocks placed into zero-filled merged blocks on the host, then uploaded
-        std::vector<unsigned char> m[4];
+        // the caller's blocks uploaded as they are, then placed into the zero-filled merged blocks on the device
+        // (the amalgamation map, merged_layout_kernel)
+        const int64_t cD = h->st.nD, cL = h->st.nL;
+        const size_t sb = es * (size_t)std::max<int64_t>(2 * cD + 2 * cL, 1);
+        if (sb > h->d_ostage.bytes && need_memory(h, sb, "pp_set_values") != PP_OK) return PP_ENOMEM;
+        CK(h, h->d_ostage.ensure(sb), "pp_set_values");
+        char *stg = static_cast<char *>(h->d_ostage.p);
+        void *c[4] = {stg, stg + es * cD, stg + es * 2 * cD, stg + es * (2 * cD + cL)};
         const void *srcs[4] = {LD, UD, LL, UL};
-        DevBuf *dst[4] = {&h->LD, &h->UD, &h->LL, &h->UL};
-        unsigned char zero[8];
-        zero_value(semiring, dtype, zero);
-        try {
-            for (int a = 0; a < 4; a++) {
-                const size_t len = (size_t)std::max<int64_t>(a < 2 ? h->nD : h->nL, 1);
-                m[a].resize(es * len);
-                for (size_t i = 0; i < len; i++) memcpy(m[a].data() + es * i, zero, es);
-            }
-        } catch (const std::bad_alloc &) {
-            return fail(h, PP_ENOMEM, "pp_set_values: out of host memory");
-        }
-        for_each_merged_entry(h, [&](int a, int64_t o, int ma, int64_t mo) {
-            memcpy(m[ma].data() + es * mo, static_cast<const unsigned char *>(srcs[a]) + es * o, es);
-        });
         for (int a = 0; a < 4; a++)
-            if (a < 2 ? h->nD : h->nL)
-                CK(h, cudaMemcpyAsync(dst[a]->p, m[a].data(), es * (a < 2 ? h->nD : h->nL), cudaMemcpyHostToDevice, st),
-                   "pp_set_values");
+            if (a < 2 ? cD : cL)
+                CK(h, cudaMemcpyAsync(c[a], srcs[a], es * (a < 2 ? cD : cL), cudaMemcpyHostToDevice, st), "pp_set_values");
+        if (h->nD) CK(h, h->ops->fill_zero(h->LD.p, h->nD, st), "pp_set_values");
+        if (h->nD) CK(h, h->ops->fill_zero(h->UD.p, h->nD, st), "pp_set_values");
+        if (h->nL) CK(h, h->ops->fill_zero(h->LL.p, h->nL, st), "pp_set_values");
+        if (h->nL) CK(h, h->ops->fill_zero(h->UL.p, h->nL, st), "pp_set_values");
+        CK(h, merged_layout(h, c, false, st), "pp_set_values");
         if (h->hp.nN) CK(h, cudaMemcpyAsync(h->Nval.p, Nval, es * h->hp.nN, cudaMemcpyHostToDevice, st), "pp_set_values");
         CK(h, stream_wait(h, st), "pp_set_values");
         h->have_values = true;
@@ -1946,27 +2008,26 @@ extern "C" int32_t pp_get_factor(pp_handle *h, void *LD, void *LL, void *UD, voi
     const size_t es = h->ops->esize;
     cudaStream_t st = h->stream;
     if (h->merged) {
-        // the merged blocks to the host, then each of the caller's entries from its place in them
-        std::vector<unsigned char> m[4];
+        // the caller's layout gathered from the merged blocks on the device (the amalgamation map,
+        // merged_layout_kernel), then downloaded
+        const int64_t cD = h->st.nD, cL = h->st.nL;
+        const size_t sb = es * (size_t)std::max<int64_t>(2 * cD + 2 * cL, 1);
+        if (sb > h->d_ostage.bytes && need_memory(h, sb, "pp_get_factor") != PP_OK) return PP_ENOMEM;
+        CK(h, h->d_ostage.ensure(sb), "pp_get_factor");
+        char *stg = static_cast<char *>(h->d_ostage.p);
+        void *c[4] = {stg, stg + es * cD, stg + es * 2 * cD, stg + es * (2 * cD + cL)};
         void *dst[4] = {LD, UD, LL, UL};
-        const DevBuf *src[4] = {&h->LD, &h->UD, &h->LL, &h->UL};
-        try {
-            for (int a = 0; a < 4; a++) m[a].resize(es * (size_t)std::max<int64_t>(a < 2 ? h->nD : h->nL, 1));
-        } catch (const std::bad_alloc &) {
-            return fail(h, PP_ENOMEM, "pp_get_factor: out of host memory");
-        }
+        CK(h, after_factor(h), "pp_get_factor");
+        CK(h, merged_layout(h, c, true, st), "pp_get_factor");
         for (int a = 0; a < 4; a++)
-            if (dst[a] && (a < 2 ? h->nD : h->nL))
-                CK(h, cudaMemcpyAsync(m[a].data(), src[a]->p, es * (a < 2 ? h->nD : h->nL), cudaMemcpyDeviceToHost, st),
-                   "pp_get_factor");
+            if (dst[a] && (a < 2 ? cD : cL))
+                CK(h, cudaMemcpyAsync(dst[a], c[a], es * (a < 2 ? cD : cL), cudaMemcpyDeviceToHost, st), "pp_get_factor");
         const int32_t r = settle(h, "pp_get_factor");
         if (r != PP_OK) return r;
-        for_each_merged_entry(h, [&](int a, int64_t o, int ma, int64_t mo) {
-            if (dst[a]) memcpy(static_cast<unsigned char *>(dst[a]) + es * o, m[ma].data() + es * mo, es);
-        });
         ok(h);
         return PP_OK;
     }
+    CK(h, after_factor(h), "pp_get_factor");  // the top of the tree is factored on its own stream
     if (LD && h->nD) CK(h, cudaMemcpyAsync(LD, h->LD.p, es * h->nD, cudaMemcpyDeviceToHost, st), "pp_get_factor");
     if (UD && h->nD) CK(h, cudaMemcpyAsync(UD, h->UD.p, es * h->nD, cudaMemcpyDeviceToHost, st), "pp_get_factor");
     if (LL && h->nL) CK(h, cudaMemcpyAsync(LL, h->LL.p, es * h->nL, cudaMemcpyDeviceToHost, st), "pp_get_factor");
